@@ -1,0 +1,494 @@
+"""Benchmark of the A->F->A MoE round trip (one DeepSeek-V3-shape MXFP4 MoE layer) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N = 1: one GPU holds one A rank and one F rank (loopback arenas): T = 16384 tokens, hidden 7168, 256 routed
+experts (all on the F rank), top-8 sigmoid routing, intermediate 2048, MXFP4 weights, plus one bf16 shared
+expert (intermediate 2048) computed on the A side and added in the combine.
+N > 1 (torchrun, one rank per GPU): ranks [0, N/2) are A replicas (T = 16384 each), ranks [N/2, N) F ranks with
+a contiguous share of the 256 experts; the data path is P2P stores over NVLink (no collective); gloo carries the
+plumbing (endpoint exchange, barriers, the max over ranks of the timed region).
+
+A step is one layer through dispatch -> experts -> combine for every A replica.  value = tokens of all A replicas
+per second over exactly K timed steps (CUDA events, barrier + synchronize around, max over ranks); inputs are
+larger than L2 (x 235 MB, weights 6 GB).  e2e = the same through AsapMoE.forward with pinned host buffers and the
+host<->device copies inside the timed region.  --impl reference times the CPU restatement of the reference's
+torch semantics (oracle/, test infrastructure) on a bounded sample of the same workload, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sgl-afd-plugin_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE layer tokens/s A->F->A (DeepSeek-V3-shape MXFP4 layer, T=16384 per A replica)"
+H, I, E, K_TOP, T_DEFAULT = 7168, 2048, 256, 8, 16384
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            return json.load(fh), "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------ workload
+def make_routing(T, seed, device):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    logits = torch.randn(T, E, device=device, generator=g)
+    scores = torch.sigmoid(logits)
+    w, ids = torch.topk(scores, K_TOP, dim=1)
+    w = w / w.sum(1, keepdim=True)
+    return ids.to(torch.int32).contiguous(), w.float().contiguous()
+
+
+class SharedExpert:
+    """One bf16 shared expert (SwiGLU, intermediate 2048) on the A side, cuBLAS GEMMs through torch."""
+
+    def __init__(self, device, seed=7):
+        import torch
+
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.w13 = (torch.randn(2 * I, H, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        self.w2 = (torch.randn(H, I, device=device, generator=g) * 0.02).to(torch.bfloat16)
+
+    def __call__(self, x):
+        import torch
+
+        gu = x @ self.w13.t()
+        return (torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]) @ self.w2.t()
+
+
+def gemm_flops(pairs):
+    return 2.0 * pairs * H * (2 * I), 2.0 * pairs * I * H
+
+
+# ------------------------------------------------------------------------------------------ 1 GPU
+def run_single(args):
+    import torch
+
+    from asap_b200.dispatcher import AsapDispatcher
+    from asap_b200.experts import Mxfp4Experts
+    from asap_b200.layer import AsapMoE
+    from asap_b200.loopback import Loopback
+    from asap_b200.sglang_shim import StandardTopKOutput
+    from asap_b200 import _native as N
+    from asap_b200.transport.layout import Geometry
+    import ctypes
+
+    dev = "cuda:0"
+    torch.cuda.set_device(0)
+    T = args.tokens
+    experts = Mxfp4Experts.random(E, H, I, seed=1, scale_lo=117, scale_hi=120)
+    lb = Loopback(Geometry(1, 1, 2, T, H, K_TOP, 1), {0: experts}, timeout_s=30.0)
+    lb.install()
+    shared = SharedExpert(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    ids, w = make_routing(T, 3, dev)
+    disp = AsapDispatcher(0)
+    topk = StandardTopKOutput(w, ids)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        d = disp.dispatch(x, topk)
+        s = shared(x)
+        return disp.combine(d, shared=s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    lb.check()
+    N.call("asap_ffn_enable_timing", lb.sched.ws_handle, 1)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    lb.check()
+    ms = t0.elapsed_time(t1) / args.steps
+    kms = (ctypes.c_float * 5)()
+    N.call("asap_ffn_last_timing", lb.sched.ws_handle, kms, 5)
+    N.call("asap_ffn_enable_timing", lb.sched.ws_handle, 0)
+    kernel_ms = dict(zip(("route_local", "quant_permute", "gemm1", "gemm2", "finalize_reply"), list(kms)))
+    pairs = int(lb.sched.debug_tensors()["expert_counts"].sum().item())
+
+    # dispatch / combine kernel times on their own streams (extra measured steps, outside the timed region)
+    dsp, cmb = [], []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        buf = lb.buffer
+        buf.send_stream.wait_stream(stream)
+        e0.record(buf.send_stream)
+        d = disp.dispatch(x, topk)
+        e1.record(buf.send_stream)
+        s = shared(x)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        lb.local.before_combine(d.ticket, stream)
+        c0.record(stream)
+        disp.combine(d, shared=s)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        dsp.append(e0.elapsed_time(e1))
+        cmb.append(c0.elapsed_time(c1))
+    lb.check()
+
+    # e2e: the public API (AsapMoE.forward) on pinned host buffers, copies inside the timed region
+    moe = AsapMoE(E, H, I, 0, top_k=K_TOP)
+    hx, hids, hw = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
+    hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        dx = hx.to(dev, non_blocking=True)
+        di = hids.to(dev, non_blocking=True)
+        dw = hw.to(dev, non_blocking=True)
+        out = moe(dx, StandardTopKOutput(dw, di))
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    lb.check()
+    e2e_ms = t0.elapsed_time(t1) / args.steps
+    h2d = hx.numel() * 2 + hids.numel() * 4 + hw.numel() * 4
+    d2h = hout.numel() * 2
+
+    peaks, peak_kind = load_peaks()
+    g1_flops, g2_flops = gemm_flops(pairs)
+    fp8_peak = 2.0 * peaks["bf16_tflops_sustained"]  # kind::f8f6f4 runs at twice the bf16 rate
+    achieved = g1_flops / (kernel_ms["gemm1"] * 1e-3) / 1e12
+    traffic = load_traffic("gemm1", pairs)
+    cpu = cpu_baseline(args.cpu_experts) if not args.no_cpu else None
+    clk = clocks.summary()
+    nvlink_bytes_dispatch = T * (2 * H + 8 * K_TOP)
+    line = {
+        "metric": METRIC, "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport", "data": "synthetic",
+        "config": {"workload": "1 GPU loopback A+F: config 2 layer (T=16384, H=7168, 256 experts, top-8 sigmoid, "
+                               "I=2048, MXFP4 weights, 1 bf16 shared expert)", "tokens_per_replica": T,
+                   "a_replicas": 1, "f_ranks": 1, "parallelism": "1A1F loopback",
+                   "l2": "inputs larger than L2 (x 235 MB, weights 6.0 GB), no flush"},
+        "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps * 9,
+        "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained x 2 (FP8-rate tensor kind)",
+                     "frac_of_fp4_dense_nominal": round(achieved / 9000.0, 4)},
+        "kernels_ms": {k: round(v, 4) for k, v in kernel_ms.items()},
+        "dispatch_ms": round(statistics.median(dsp), 4), "combine_ms": round(statistics.median(cmb), 4),
+        "dispatch_gbs_algorithmic": round(nvlink_bytes_dispatch / (statistics.median(dsp) * 1e-3) / 1e9, 1),
+        "pairs": pairs, "gemm_tflops_per_step": round((g1_flops + g2_flops) / 1e12, 3),
+        "cpu_baseline": cpu, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    lb.close()
+    experts.release()
+
+
+def load_traffic(kernel, pairs):
+    """DRAM bytes per launch of ``kernel`` from a committed ncu summary, scaled to this launch's pair count."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as fh:
+        d = json.load(fh).get(kernel)
+    if not d:
+        return None
+    return int(d["dram_bytes"] * pairs / d["pairs"])
+
+
+# ------------------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0):
+    """The oracle (the reference's torch semantics restated in numpy, with the same MXFP8 activation rounding)
+    on the host cores: every (token, slot) pair of the T=16384 layer that routes to experts [0, n_experts),
+    dequantised MXFP4 weights (dequantisation not timed).  tokens/s counts pairs / top-k."""
+    import numpy as np
+
+    from oracle import moe, mx
+
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(seed)
+    T = T_DEFAULT
+    logits = rng.standard_normal((T, E))
+    ids, w = moe.topk_routing(logits, K_TOP, "sigmoid")
+    sel = np.any(ids < n_experts, axis=1)
+    x = mx.bf16_round(rng.standard_normal((int(sel.sum()), H)).astype(np.float32))
+    P = n_experts
+    codes13 = rng.integers(0, 256, (P, 2 * I, H // 2), dtype=np.uint8)
+    sf13 = rng.integers(117, 121, (P, 2 * I * H // 32), dtype=np.uint8)
+    codes2 = rng.integers(0, 256, (P, H, I // 2), dtype=np.uint8)
+    sf2 = rng.integers(117, 121, (P, H * I // 32), dtype=np.uint8)
+    gate, up = moe.dequant_w13(codes13, sf13, P, H, I)
+    w2 = moe.dequant_w2(codes2, sf2, P, H, I)
+    pairs = int(np.sum(ids[sel] < n_experts))
+    times = []
+    for i in range(warmup + steps):
+        t = time.perf_counter()
+        moe.ffn_rank(x, ids[sel], w[sel], gate, up, w2, 0, P, act_quant=True)
+        if i >= warmup:
+            times.append(time.perf_counter() - t)
+    dt = statistics.median(times)
+    return {"value": round(pairs / K_TOP / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"all {pairs} (token, expert) pairs of the T=16384 config-2 layer that route to experts "
+                      f"0..{n_experts - 1} (numpy oracle, MXFP8 activation emulation, {cores} host threads); "
+                      f"tokens = pairs / top-k; {dt:.2f} s per sample"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline(args.cpu_experts, steps=1)
+    vals = []
+    t_all = time.perf_counter()
+    last = None
+    for _ in range(args.steps):
+        last = cpu_baseline(args.cpu_experts, steps=1)
+        vals.append(last["value"])
+    wall = time.perf_counter() - t_all
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
+            "data": "synthetic",
+            "config": {"workload": "config 2 layer, bounded CPU sample", "tokens_per_replica": T_DEFAULT},
+            "cpu_baseline": {**last, "value": v},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------ N GPUs
+def expert_bounds(num_f):
+    return [(f * E) // num_f for f in range(num_f + 1)]
+
+
+def run_multi(args):
+    import ctypes
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from asap_b200.experts import Mxfp4Experts
+    from asap_b200.scheduler import FfnScheduler
+    from asap_b200.transport.channel import AttnChannel
+    from asap_b200.transport.layout import Geometry
+    from asap_b200.transport.server import FfnServer
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    n_a = world // 2
+    n_f = world - n_a
+    T = args.tokens
+    g = Geometry(n_a, 1, 2, T, H, K_TOP, n_f)
+    bounds = expert_bounds(n_f)
+    is_a = rank < n_a
+    total_steps = 2 * (args.warmup + args.steps)  # device-timed run, then the e2e run
+    timeout_s = 120.0
+    ep = None
+    if not is_a:
+        f = rank - n_a
+        experts = Mxfp4Experts.random(bounds[f + 1] - bounds[f], H, I, expert_base=bounds[f], seed=100 + f,
+                                      scale_lo=117, scale_hi=120, device=dev)
+        server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
+                           host="127.0.0.1", port=0).start()
+        sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s)
+        ep = ("127.0.0.1", server.port)
+    eps = [None] * world
+    dist.all_gather_object(eps, ep)
+    endpoints = [e for e in eps if e is not None]
+    if is_a:
+        channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s).connect()
+    dist.barrier()
+    if not is_a:
+        stream = torch.cuda.current_stream()
+        for s in range(total_steps):  # the whole run is queued up front: each job waits for its doorbell
+            for a in range(n_a):
+                sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
+    else:
+        shared = SharedExpert(dev)
+        gen = torch.Generator(device=dev).manual_seed(rank)
+        x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
+        ids, w = make_routing(T, 10 + rank, dev)
+        send_stream = torch.cuda.Stream(dev)
+        stream = torch.cuda.current_stream()
+
+        def step(xx=x, ii=ids, ww=w):
+            send_stream.wait_stream(stream)
+            t = channel.send(0, 0, xx.data_ptr(), ii.data_ptr(), ww.data_ptr(), T, send_stream.cuda_stream)
+            s = shared(xx)
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+            channel.combine(t, out.data_ptr(), stream.cuda_stream, s.data_ptr())
+            return out
+
+    def timed(fn):
+        # F ranks never synchronize here: their GPU holds every job of the run, each waiting for its doorbell
+        for _ in range(args.warmup):
+            fn()
+        if is_a:
+            torch.cuda.synchronize()
+        dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            fn()
+        t1.record()
+        if is_a:
+            torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / args.steps
+        mt = torch.tensor([ms if is_a else 0.0])
+        dist.all_reduce(mt, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        return float(mt.item())
+
+    with ClockSampler(local) as clocks:
+        ms = timed(step if is_a else (lambda: None))
+    if is_a:
+        channel.check()
+        hx, hi_, hw = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
+        hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            out = step(hx.to(dev, non_blocking=True), hi_.to(dev, non_blocking=True), hw.to(dev, non_blocking=True))
+            hout.copy_(out, non_blocking=True)
+    e2e_ms = timed(e2e_step if is_a else (lambda: None))
+    torch.cuda.synchronize()  # F: every queued job has now been answered
+    if is_a:
+        channel.check()
+    else:
+        sched.check()
+    dist.barrier()
+    if rank == 0:
+        h2d = T * H * 2 + T * K_TOP * 8
+        line = {
+            "metric": METRIC, "value": round(n_a * T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport",
+            "data": "synthetic",
+            "config": {"workload": f"{n_a}A{n_f}F: config 2 layer per A replica (T=16384, H=7168, 256 experts, "
+                                   "top-8 sigmoid, I=2048, MXFP4, 1 bf16 shared expert)", "tokens_per_replica": T,
+                       "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
+                       "expert_bounds": bounds, "l2": "inputs larger than L2, no flush"},
+            "e2e": {"value": round(n_a * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": n_a * h2d,
+                    "d2h_bytes_per_step": n_a * T * H * 2, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": args.steps * (4 * n_a + 6 * n_a * n_f),
+            "roofline": None, "cpu_baseline": None, "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    if is_a:
+        channel.close()
+    dist.barrier()
+    if not is_a:
+        sched.close()
+        server.close()
+        experts.release()
+    dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--tokens", type=int, default=T_DEFAULT)
+    ap.add_argument("--cpu-experts", type=int, default=4)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_multi(args)
+    else:
+        run_single(args)
+
+
+if __name__ == "__main__":
+    main()

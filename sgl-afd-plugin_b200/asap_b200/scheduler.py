@@ -1,0 +1,194 @@
+"""The F rank's job runner: the routed experts of every layer behind one FfnServer.
+
+Replaces what the reference's FfnScheduler (python/sgl_asap_plugin/srt/managers/scheduler.py:162-453) does per
+job, without SGLang: ``run_job`` (scheduler.py:387-436) launches libasap's fused chain -- expert-major
+permutation + MXFP8 quantisation, GEMM1 (+SwiGLU + requant), GEMM2 (+top-k weight), the weighted reduce that
+stores the reply rows straight into the A rank's ResultArena and releases its done flag (server.py:340-350) --
+and ``rows_of`` (scheduler.py:438-450) gives torch views of a row's arena region.  ``JobTimer``
+(scheduler.py:109-159) keeps its fields: per power-of-two bucket, host launch us, expert GPU ms (alone /
+queued) and reply ms (here part of the expert chain, reported as 0).
+
+Everything a job needs on the GPU is derived on the device from the job descriptor (n, seq), so a job can be
+enqueued before its doorbell rings (``run_device_wait``) and the chain can be captured in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import collections
+import ctypes
+import statistics
+import time
+from typing import Dict, Optional
+
+import torch
+
+from . import _native as N
+from .experts import Mxfp4Experts, _aligned_empty
+from .transport.layout import SEQ_MASK
+from .transport.memory import HostWords
+from .transport.server import FfnServer, Job, Row, _raw_bytes
+
+
+class JobTimer:
+    """scheduler.py:109-159: per job-size bucket, host launch time, experts GPU time (alone / queued)."""
+
+    def __init__(self, keep: int = 4096):
+        self.keep = keep
+        self.pending = collections.deque()
+        self.samples = collections.defaultdict(lambda: collections.defaultdict(list))
+        self.free = []
+
+    def event(self) -> torch.cuda.Event:
+        event = self.free.pop() if self.free else torch.cuda.Event(enable_timing=True)
+        event.record()
+        return event
+
+    def start(self) -> tuple:
+        alone = not self.pending or self.pending[-1][3].query()
+        return alone, self.event()
+
+    def add(self, n_tokens: int, started: tuple, host_s: float) -> None:
+        bucket = 1 << (n_tokens - 1).bit_length()
+        self.pending.append((bucket, *started, self.event(), host_s))
+        self.drain()
+
+    def drain(self) -> None:
+        while self.pending and self.pending[0][3].query():
+            bucket, alone, start, done, host_s = self.pending.popleft()
+            rows = self.samples[bucket]
+            if len(rows["host_us"]) < self.keep:
+                rows["host_us"].append(host_s * 1e6)
+                rows["reply_ms"].append(0.0)
+                rows[f"experts_ms_{'alone' if alone else 'queued'}"].append(start.elapsed_time(done))
+            self.free += [start, done]
+
+    def summary(self) -> dict:
+        torch.cuda.synchronize()
+        self.drain()
+        out = {}
+        for bucket, rows in sorted(self.samples.items()):
+            out[bucket] = {"jobs": len(rows["host_us"])}
+            for name, values in sorted(rows.items()):
+                out[bucket][f"{name}_p50"] = round(statistics.median(values), 4)
+                out[bucket][f"{name}_n"] = len(values)
+        return out
+
+
+class FfnScheduler:
+    """The experts of one F rank (``experts[layer_id]``) answering the jobs of ``server``."""
+
+    def __init__(self, server: FfnServer, experts: Dict[int, Mxfp4Experts], *, swiglu_limit: float = 0.0,
+                 timeout_s: float = 60.0, timing: bool = False):
+        g = server.g
+        if g.group != 1:
+            raise NotImplementedError("AFD supports attention TP size 1 only (group=1), as the reference's "
+                                      "deployment check does (srt/arg_groups/asap_hook.py:175-176)")
+        first = next(iter(experts.values()))
+        for lid, e in experts.items():
+            if (e.num_local, e.hidden, e.inter, e.expert_base) != (first.num_local, first.hidden, first.inter,
+                                                                    first.expert_base):
+                raise ValueError(f"layer {lid} serves other experts than layer {next(iter(experts))}")
+        if first.hidden != g.hidden:
+            raise ValueError(f"experts hidden {first.hidden} != geometry hidden {g.hidden}")
+        self.server, self.g, self.experts = server, g, experts
+        self.f = server.f
+        self.device = server.device
+        self.swiglu_limit = float(swiglu_limit or 0.0)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.local = range(first.expert_base, first.expert_base + first.num_local)
+        nbytes = N.lib().asap_ffn_ws_bytes(g.n_max, g.topk, first.num_local, first.hidden, first.inter)
+        self._ws_owner, self.ws = _aligned_empty(nbytes, f"cuda:{self.device}")
+        h = ctypes.c_uint64()
+        N.call("asap_ffn_ws_register", self.ws.data_ptr(), g.n_max, g.topk, first.num_local, first.hidden,
+               first.inter, ctypes.byref(h))
+        self.ws_handle = h.value
+        self.status = HostWords(1)
+        self.layer_calls = collections.Counter()
+        self.job_timer = JobTimer() if timing else None
+        arena = _raw_bytes(server.recv_base, g.recv_bytes, self.device)
+        self.recv_arena = arena
+
+    def close(self) -> None:
+        if self.ws_handle:
+            N.call("asap_ffn_ws_release", self.ws_handle)
+            self.ws_handle = 0
+        self.status.close()
+
+    def check(self) -> None:
+        word = self.status.read()
+        if word:
+            st = N.decode_status(word)
+            raise RuntimeError(f"F rank {self.f}: device {st['what']} (slot {st['slot']}, seq {st['seq']})")
+
+    # ---------------------------------------------------------------- one job
+    def _launch(self, experts: Mxfp4Experts, row: Row, reply, stream: int) -> None:
+        seg, done = reply
+        N.call("asap_ffn_job", experts.handle, self.ws_handle, row.x_ptr, row.ids_ptr, row.w_ptr, seg, done,
+               ctypes.c_float(self.swiglu_limit), self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
+
+    def run_job(self, job: Job, stream: Optional[int] = None) -> None:
+        """One expert chain for the row of one replica's micro-batch (host-poll mode); enqueues GPU work only."""
+        tic, timer = time.perf_counter(), self.job_timer
+        started = timer.start() if timer else None
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        row = job.rows[0]
+        target = self.server.reply_target(row)
+        if target is None:  # the A rank reconnected since: its reply is dropped (server.py:343-346)
+            return
+        N.call("asap_ffn_post", self.ws_handle, row.seq & SEQ_MASK, row.n_tokens, row.layer_id, row.epoch,
+               ctypes.c_void_p(stream))
+        self._launch(self.experts[job.layer_id], row, target, stream)
+        self.layer_calls[job.layer_id] += 1
+        if timer:
+            timer.add(row.n_tokens, started, time.perf_counter() - tic)
+
+    def run_device_wait(self, a: int, slot: int, seq: int, layer_id: int, stream: int) -> None:
+        """Enqueue a job for the next message of (a, slot) before it arrives: the chain starts with a bounded
+        device spin on the doorbell (libasap asap_ffn_wait), which also validates epoch and size.  The token count
+        comes from the doorbell on the device; ``seq`` is the message the host expects (backpressure forbids
+        skipping one)."""
+        server = self.server
+        peer = server.peers[a]
+        row = server.row_for(a, slot, seq, self.g.n_max, layer_id)
+        target = server.reply_target(row)
+        if target is None:
+            return
+        N.call("asap_ffn_wait", self.ws_handle, server.bell_dev(a, slot), (seq - 1) & SEQ_MASK, peer.epoch,
+               self.g.n_max, self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
+        self._launch(self.experts[layer_id], row, target, stream)
+        server.advance(a, slot, seq)
+        self.layer_calls[layer_id] += 1
+
+    def rows_of(self, row: Row):
+        """x, topk_ids and topk_weights of one row: views into the RecvArena (scheduler.py:438-450)."""
+        g, arena = self.g, self.recv_arena
+        n, off = row.n_tokens, row.x_ptr - self.server.recv_base
+        x = arena[off: off + n * g.hidden * 2].view(torch.bfloat16).view(n, g.hidden)
+        ids_off, w_off = off + g.ids_off, off + g.w_off
+        topk_ids = arena[ids_off: ids_off + n * g.topk * 4].view(torch.int32).view(n, g.topk)
+        topk_weights = arena[w_off: w_off + n * g.topk * 4].view(torch.float32).view(n, g.topk)
+        return x, topk_ids, topk_weights
+
+    def debug_tensors(self) -> dict:
+        """Device buffers of the last job (tests): per-local-expert counts and the pair permutation."""
+        vals = [ctypes.c_uint64() for _ in range(7)]
+        N.call("asap_ffn_debug_ptrs", self.ws_handle, *[ctypes.byref(v) for v in vals])
+        g, P = self.g, len(self.local)
+        e = self.experts[next(iter(self.experts))]
+        return {
+            "expert_counts": _raw_bytes(vals[0].value, 4 * P, self.device).view(torch.int32),
+            "pair_pos": _raw_bytes(vals[1].value, 4 * g.n_max * g.topk, self.device).view(torch.int32).view(
+                g.n_max, g.topk),
+            "xq": vals[2].value, "xq_sf": vals[3].value, "hq": vals[4].value, "hq_sf": vals[5].value,
+            "y2": vals[6].value, "hidden": e.hidden, "inter": e.inter,
+        }
+
+    def job_info(self, stream: Optional[int] = None) -> dict:
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        n, layer, epoch, valid = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        seq = ctypes.c_uint32()
+        N.call("asap_ffn_job_info", self.ws_handle, ctypes.byref(n), ctypes.byref(layer), ctypes.byref(seq),
+               ctypes.byref(epoch), ctypes.byref(valid), ctypes.c_void_p(stream))
+        return {"n": n.value, "layer": layer.value, "seq": seq.value, "epoch": epoch.value, "valid": valid.value}

@@ -1,0 +1,244 @@
+"""A side of the transport: one AttnChannel per A rank, connected to every F rank.
+
+Same API and protocol as the reference's python/sgl_asap_plugin/transport/channel.py (connect, send, wait,
+check, close, reconnect; JSON-over-TCP handshake; epochs; seq per slot; backpressure), with the data path
+moved onto the SMs:
+
+* send() launches the dispatch kernels on the caller's stream (libasap asap_dispatch): a bounded device spin
+  for backpressure (channel.py:337-339), the per-F-rank bucketing of the top-k, 16-byte P2P stores of the
+  routed rows straight into each F rank's RecvArena, and the 64-bit doorbell released by the last CTA
+  (channel.py:340-355, where the reference used three copy-engine copies and a stream memop per F rank).
+* combine() launches the combine kernel: a bounded spin on the F done flags (channel.py:364-377) fused with
+  the fp32 sum of the partials and the shared-expert add (token_dispatcher/asap.py:174-184).
+* A device wait never blocks forever: it gives up after ``timeout_s``, writes a status word into pinned host
+  memory and returns.  check() reads that word with a plain load (no sync) and raises ChannelPoisoned, as the
+  reference's Watchdog does after it released a parked stream (channel.py:100-167, 301-311).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import socket
+import time
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from .. import _native as N
+from .layout import PROTO_VERSION, SEQ_MASK, ChannelPoisoned, Geometry, HandshakeError
+from .memory import HostWords, Shared
+from .memory import select as select_memory
+
+MAX_HANDSHAKE_BYTES = 1 << 20
+
+
+def request(host: str, port: int, msg: dict, *, connect_timeout: float = 60.0, io_timeout: float = 30.0) -> dict:
+    """Send one JSON line to an F rank and return its JSON line answer (channel.py:43-83)."""
+    deadline = time.monotonic() + connect_timeout
+    while True:
+        try:
+            sock = socket.create_connection((host, port), timeout=2.0)
+            break
+        except OSError as exc:
+            if time.monotonic() > deadline:
+                raise HandshakeError(f"cannot reach F at {host}:{port}: {exc}") from exc
+            time.sleep(0.2)
+    with sock, sock.makefile("rwb") as f:
+        sock.settimeout(io_timeout)
+        try:
+            f.write(json.dumps(msg).encode() + b"\n")
+            f.flush()
+            line = f.readline(MAX_HANDSHAKE_BYTES)
+        except OSError as exc:
+            raise HandshakeError(f"handshake with F at {host}:{port} failed: {exc}") from exc
+    if not line:
+        raise HandshakeError(f"F at {host}:{port} closed the connection without answering")
+    reply = json.loads(line)
+    if not reply.get("ok"):
+        raise HandshakeError(f"F at {host}:{port} rejected the connection: {reply.get('reason')}")
+    return reply
+
+
+@dataclass
+class Ticket:
+    """One message in flight (channel.py:170-180)."""
+
+    slot: int
+    seq: int
+    layer_id: int
+    n_tokens: int
+    result_ptrs: List[int] = field(default_factory=list)
+
+
+class AttnChannel:
+    """A rank ``a``'s connection to every F rank (``endpoints[f]`` is F rank f's handshake address).
+
+    ``expert_bounds`` (num_f + 1 ints): F rank f owns experts [bounds[f], bounds[f+1]).  Default: the
+    reference's contiguous equal split of ``num_experts`` (srt/managers/scheduler.py:206-218), given through
+    ``hello["model"]["n_experts"]``."""
+
+    def __init__(self, a: int, geometry: Geometry, endpoints: Sequence[Tuple[str, int]], *, device: int,
+                 seq_base: int = 0, timeout_s: float = 60.0, connect_timeout_s: float = 60.0, memory: str = "auto",
+                 hello: Optional[dict] = None, expert_bounds: Optional[Sequence[int]] = None,
+                 _backpressure: bool = True, _epoch_override: Optional[int] = None, _connector=None):
+        if len(endpoints) != geometry.num_f:
+            raise ValueError(f"need one endpoint per F rank ({geometry.num_f}), got {len(endpoints)}")
+        if not 0 <= a < geometry.num_a:
+            raise ValueError(f"A rank {a} is outside [0, {geometry.num_a})")
+        if geometry.num_f > N.MAX_F:
+            raise ValueError(f"{geometry.num_f} F ranks; this build addresses at most {N.MAX_F}")
+        self.a, self.g, self.endpoints, self.seq_base = a, geometry, list(endpoints), seq_base
+        self.device, self.timeout_s, self.connect_timeout_s = device, timeout_s, connect_timeout_s
+        self.hello = dict(hello or {})
+        self._backpressure, self._epoch_override = _backpressure, _epoch_override
+        self._connector = _connector  # in-process handshake (loopback); None: TCP
+        self.memory, self.mem = memory, None
+        self.expert_bounds = list(expert_bounds) if expert_bounds is not None else None
+        self._poison: Optional[ChannelPoisoned] = None
+        self._result_mem: Optional[Shared] = None
+        self._result: Optional[int] = None
+        self._recv: List[int] = []
+        self._bells: List[int] = []
+        self._maps: List[Shared] = []
+        self._epoch: List[int] = []
+        self.replies: List[dict] = []
+        self.status = None
+        self._route_ws: List[torch.Tensor] = []
+
+    # ---------------------------------------------------------------- connect / close
+    def connect(self) -> "AttnChannel":
+        """Allocate the ResultArena, hand it to every F rank, map their RecvArenas and doorbell pages."""
+        g = self.g
+        N.call("asap_init", self.device)
+        if self.mem is None:
+            self.mem = select_memory(self.memory, self.device)
+        if self.expert_bounds is None:
+            n_exp = (self.hello.get("model") or {}).get("n_experts")
+            if n_exp is None or n_exp % g.num_f:
+                raise ValueError("expert_bounds is required unless hello['model']['n_experts'] is a multiple of "
+                                 "num_f (the reference's equal contiguous split)")
+            per = n_exp // g.num_f
+            self.expert_bounds = [f * per for f in range(g.num_f + 1)]
+        if len(self.expert_bounds) != g.num_f + 1:
+            raise ValueError("expert_bounds needs num_f + 1 entries")
+        self._result_mem = self.mem.device(g.result_bytes)
+        self._result = self._result_mem.ptr
+        stream = torch.cuda.current_stream(self.device)
+        N.call("asap_memset32", self._result, self.seq_base & SEQ_MASK, g.flags_bytes // 4,
+               ctypes.c_void_p(stream.cuda_stream))
+        stream.synchronize()
+        hello = {**self.hello, "proto": PROTO_VERSION, "a": self.a, "geometry": g.as_dict(), "pid": os.getpid(),
+                 "memory": self.mem.kind, "peer": self.mem.identity(), "result": self._result_mem.desc}
+        try:
+            for f, (host, port) in enumerate(self.endpoints):
+                if self._connector is not None:
+                    reply = self._connector(f, hello)
+                else:
+                    reply = request(host, port, hello, connect_timeout=self.connect_timeout_s)
+                if reply["seq_base"] != self.seq_base:
+                    raise HandshakeError(f"seq_base A={self.seq_base} F={reply['seq_base']}")
+                recv = self.mem.open(reply["recv"])
+                self._maps.append(recv)
+                self._recv.append(recv.ptr)
+                bells = self.mem.open_doorbells(reply["doorbells"], g.host_bytes)
+                self._maps.append(bells)
+                self._bells.append(bells.ptr)
+                self._epoch.append(reply["epoch"])
+                self.replies.append(reply)
+        except BaseException:
+            self.close()
+            raise
+        self._seq = [self.seq_base] * g.slots
+        self._poison = None
+        self.status = HostWords(1)
+        ws_bytes = N.lib().asap_route_ws_bytes(ctypes.byref(N.geometry_struct(g)))
+        self._route_ws = [torch.empty(ws_bytes, dtype=torch.uint8, device=f"cuda:{self.device}")
+                          for _ in range(g.slots)]
+        self._gs = N.geometry_struct(g)
+        F = g.num_f
+        self._c_epochs = (ctypes.c_int32 * F)(*self._epoch)
+        self._c_bounds = (ctypes.c_int32 * (F + 1))(*self.expert_bounds)
+        self._c_recv = (ctypes.c_uint64 * F)(*self._recv)
+        self._c_bells = (ctypes.c_uint64 * F)(*self._bells)
+        return self
+
+    def reconnect(self) -> "AttnChannel":
+        """The only way out of a poisoned channel: a new epoch and a fresh ResultArena on every F rank."""
+        self.close()
+        return self.connect()
+
+    def close(self) -> None:
+        """Release everything. Synchronize the streams that used the channel first."""
+        for shared in self._maps:
+            shared.release()
+        if self._result_mem is not None:
+            self._result_mem.release()
+        self._recv, self._bells, self._maps, self._epoch, self.replies = [], [], [], [], []
+        self._result_mem = self._result = None
+        self._route_ws = []
+        if self.status is not None:
+            self.status.close()
+            self.status = None
+
+    # ---------------------------------------------------------------- failure state
+    def check(self) -> None:
+        """Raise ChannelPoisoned if a device wait ran out (the reference's watchdog semantics)."""
+        if self._poison is None and self.status is not None:
+            word = self.status.read()
+            if word:
+                st = N.decode_status(word)
+                self._poison = ChannelPoisoned(
+                    f"A rank {self.a}: {st['what']} (F rank {st['f']}, slot {st['slot']}, seq {st['seq']}) did not "
+                    f"complete within {self.timeout_s}s, F is dead or stuck; the results of every pending message "
+                    "are garbage until reconnect()")
+        if self._poison is not None:
+            raise self._poison
+
+    @property
+    def result_base(self) -> int:
+        return self._result
+
+    def _done(self, f: int, slot: int) -> int:
+        return self._result + self.g.done_off(f, slot)
+
+    def route_ws(self, slot: int) -> torch.Tensor:
+        return self._route_ws[slot]
+
+    # ---------------------------------------------------------------- data path
+    def send(self, layer_id: int, slot: int, x_ptr: int, ids_ptr: int, w_ptr: int, n_tokens: int, stream: int, *,
+             ids_is_int64: bool = False, w_is_bf16: bool = False) -> Ticket:
+        """Enqueue one message on ``stream``: ``n_tokens`` contiguous rows of x (bf16 [n, hidden]), top-k ids
+        (int32 or int64 [n, topk]) and top-k weights (fp32 or bf16 [n, topk]) at the given device addresses."""
+        self.check()
+        g = self.g
+        if not (0 <= slot < g.slots and 1 <= n_tokens <= g.n_max):
+            raise ValueError(f"slot {slot} / n_tokens {n_tokens} outside the geometry {g}")
+        seq = self._seq[slot] = (self._seq[slot] + 1) & SEQ_MASK
+        epochs = self._c_epochs
+        if self._epoch_override is not None:
+            epochs = (ctypes.c_int32 * g.num_f)(*([self._epoch_override] * g.num_f))
+        N.call("asap_dispatch", ctypes.byref(self._gs), self.a, slot, seq, layer_id, epochs, x_ptr, ids_ptr,
+               int(ids_is_int64), w_ptr, int(w_is_bf16), n_tokens, self._c_bounds, self._c_recv, self._c_bells,
+               self._result, self._route_ws[slot].data_ptr(), int(self._backpressure), self.status.ptr,
+               int(self.timeout_s * 1e9), ctypes.c_void_p(stream))
+        return Ticket(slot, seq, layer_id, n_tokens)
+
+    def wait(self, ticket: Ticket, stream: int) -> List[int]:
+        """Enqueue on ``stream`` the bounded wait for every F rank's answer to ``ticket``; returns the A-device
+        addresses of the F partial sums (bf16 rows, F rank f's row j answers its region row j)."""
+        self.check()
+        g = self.g
+        N.call("asap_wait_replies", ctypes.byref(self._gs), ticket.slot, ticket.seq, self._result, self.status.ptr,
+               int(self.timeout_s * 1e9), ctypes.c_void_p(stream))
+        ticket.result_ptrs = [self._result + g.seg_off(f, ticket.slot) for f in range(g.num_f)]
+        return ticket.result_ptrs
+
+    def combine(self, ticket: Ticket, out_ptr: int, stream: int, shared_ptr: int = 0) -> None:
+        """Enqueue the bounded reply wait fused with out = bf16(sum_f partial_f) (+ shared): the A-side combine."""
+        self.check()
+        N.call("asap_combine", ctypes.byref(self._gs), ticket.slot, ticket.seq, ticket.n_tokens, self._result,
+               self._route_ws[ticket.slot].data_ptr(), shared_ptr, out_ptr, self.status.ptr,
+               int(self.timeout_s * 1e9), ctypes.c_void_p(stream))

@@ -1,0 +1,1054 @@
+// libasap F side: doorbell wait, expert-major permutation, MXFP8 activation quantisation, the two tcgen05
+// block-scaled grouped GEMMs (MXFP8 activations x MXFP4 weights) with fused epilogues, and the weighted
+// reduce that writes the reply straight into the A rank's ResultArena.
+//
+// Reference behaviour replaced here (python/sgl_asap_plugin/):
+//   transport/server.py:262-320     FfnServer.poll/_row        -> ffn_wait_kernel (device-side doorbell spin)
+//   srt/managers/scheduler.py:387-450 run_job / rows_of        -> asap_ffn_job (launch chain, arena views)
+//   SGLang FusedMoE -> FlashInfer trtllm_fp4_block_scale_routed_moe (scheduler.py:410-412;
+//   srt/layers/quantization/mxfp4_flashinfer_trtllm_moe.py:68-99)
+//                                                              -> route_local / quant_permute / moe_gemm<0,1> /
+//                                                                 finalize_reply kernels
+//   transport/server.py:340-350     FfnServer.reply            -> finalize_reply epilogue (P2P rows + done flag)
+#include <cuda.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace asap {
+
+int sm_count();
+
+// ------------------------------------------------------------------ job descriptor and workspace layout
+struct JobDesc {
+  int32_t n, layer, epoch, valid;
+  uint32_t seq;
+  uint32_t sync;  // arrive counter of the finalize grid
+  uint32_t pad[10];
+};
+static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
+
+struct WsLayout {
+  int32_t n_max, topk, P, H, I;
+  int64_t m_cap;  // rows of the expert-major activation buffers (multiple of 128)
+  uint64_t desc, ecnt, mstart, pair_pos, row_tok, row_w, xq, xq_sf, hq, hq_sf, y2, total;
+};
+
+static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
+  WsLayout L;
+  L.n_max = n_max;
+  L.topk = topk;
+  L.P = P;
+  L.H = H;
+  L.I = I;
+  L.m_cap = align_up((uint64_t)n_max * topk + 128ull * P, 128);
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) {
+    uint64_t at = off;
+    off = align_up(off + bytes, 1024);
+    return at;
+  };
+  L.desc = take(sizeof(JobDesc));
+  L.ecnt = take(4ull * ASAP_MAX_LOCAL_EXPERTS);
+  L.mstart = take(4ull * (ASAP_MAX_LOCAL_EXPERTS + 1));
+  L.pair_pos = take(4ull * n_max * topk);
+  L.row_tok = take(4ull * L.m_cap);
+  L.row_w = take(4ull * L.m_cap);
+  L.xq = take((uint64_t)L.m_cap * H);
+  L.xq_sf = take((uint64_t)L.m_cap * (H / 32));
+  L.hq = take((uint64_t)L.m_cap * I);
+  L.hq_sf = take((uint64_t)L.m_cap * (I / 32));
+  L.y2 = take((uint64_t)L.m_cap * H * 2);
+  L.total = off;
+  return L;
+}
+
+// Byte offset of the E8M0 scale of (row r, 32-element block kb) inside a scale-factor atom array laid out
+// [r / 128][kb / 4][512 B], the 512-byte atom holding 128 rows x 4 blocks as the tcgen05 scale-factor copy
+// (32x128b.warpx4) reads it: byte (r % 32) * 16 + ((r / 32) % 4) * 4 + kb % 4.
+__host__ __device__ __forceinline__ uint64_t sf_atom_off(int64_t r, int kb, int kblocks) {
+  return ((uint64_t)(r >> 7) * (uint64_t)(kblocks >> 2) + (uint64_t)(kb >> 2)) * 512ull + (uint64_t)(r & 31) * 16ull +
+         (uint64_t)((r >> 5) & 3) * 4ull + (uint64_t)(kb & 3);
+}
+
+// ------------------------------------------------------------------ K3: doorbell wait / host post
+__global__ void ffn_wait_kernel(JobDesc* d, const uint64_t* bell, uint32_t last_seq, int32_t expect_epoch,
+                                int32_t n_max, uint64_t status, uint64_t timeout_ns) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t deadline = globaltimer_ns() + timeout_ns;
+  uint64_t word = 0;
+  for (;;) {
+    word = ld_relaxed_sys_u64(bell);
+    if ((int32_t)((uint32_t)word - last_seq) > 0) break;
+    if (globaltimer_ns() > deadline) {
+      report(status, status_word(ASAP_ST_DOORBELL_TIMEOUT, 0, 0, last_seq + 1u));
+      d->valid = 0;
+      d->n = 0;
+      return;
+    }
+    __nanosleep(64);
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  const uint32_t seq = (uint32_t)word;
+  const int32_t n = (int32_t)((word >> 32) & kMaxTokens);
+  const int32_t layer = (int32_t)((word >> 49) & kMaxLayer);
+  const int32_t epoch = (int32_t)(word >> 59);
+  d->seq = seq;
+  d->layer = layer;
+  d->epoch = epoch;
+  d->sync = 0;
+  if (epoch != expect_epoch || n < 1 || n > n_max) {
+    report(status, status_word(ASAP_ST_BAD_DOORBELL, 0, 0, seq));
+    d->valid = 0;
+    d->n = 0;
+    return;
+  }
+  d->n = n;
+  d->valid = 1;
+}
+
+__global__ void ffn_post_kernel(JobDesc* d, uint32_t seq, int32_t n, int32_t layer, int32_t epoch) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  d->seq = seq;
+  d->n = n;
+  d->layer = layer;
+  d->epoch = epoch;
+  d->sync = 0;
+  d->valid = 1;
+}
+
+// ------------------------------------------------------------------ K3b-1: expert-major permutation
+// Stable counting sort of the (token, slot) pairs whose expert is local, by (expert, token, slot).
+// Each expert's rows start on a 128-row boundary (one GEMM M tile never mixes experts).
+constexpr int kPermThreads = 1024;
+constexpr int kPermWarps = kPermThreads / 32;
+
+struct PermArgs {
+  const JobDesc* desc;
+  const int32_t* ids;  // [n, topk] in the RecvArena
+  const float* w;      // [n, topk]
+  int32_t topk, P, expert_base;
+  int32_t* ecnt;      // [P]
+  int32_t* mstart;    // [P + 1] first 128-row tile of every expert; mstart[P] = tiles in all
+  int32_t* pair_pos;  // [n, topk]
+  int32_t* row_tok;   // [m_cap]
+  float* row_w;       // [m_cap]
+};
+
+__global__ void __launch_bounds__(kPermThreads, 1) route_local_kernel(const __grid_constant__ PermArgs p) {
+  __shared__ int32_t hist[kPermWarps][ASAP_MAX_LOCAL_EXPERTS];
+  __shared__ int32_t s_mstart[ASAP_MAX_LOCAL_EXPERTS + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int P = p.P;
+  const int n = p.desc->valid ? p.desc->n : 0;
+  for (int i = tid; i < kPermWarps * ASAP_MAX_LOCAL_EXPERTS; i += kPermThreads) (&hist[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t total = (int64_t)n * p.topk;
+  const int64_t chunk = ((total + kPermWarps - 1) / kPermWarps + 31) / 32 * 32;
+  const int64_t q0 = min(total, (int64_t)warp * chunk), q1 = min(total, q0 + chunk);
+  // pass 1: per-warp histograms
+  for (int64_t q = q0 + lane; q < q1; q += 32) {
+    const int e = p.ids[q] - p.expert_base;
+    if (e >= 0 && e < P) atomicAdd(&hist[warp][e], 1);
+  }
+  __syncthreads();
+  // expert totals, 128-row tile counts, and per-warp bases
+  if (tid < P) {
+    int32_t c = 0;
+    for (int w = 0; w < kPermWarps; ++w) c += hist[w][tid];
+    p.ecnt[tid] = c;
+    s_mstart[tid] = (c + 127) / 128;
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive scan of tile counts, 8 experts per lane
+    int32_t v[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane * 8 + i;
+      v[i] = (e < P) ? s_mstart[e] : 0;
+      sum += v[i];
+    }
+    int32_t incl = sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += u;
+    }
+    int32_t run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane * 8 + i;
+      if (e < P) s_mstart[e] = run;
+      run += v[i];
+    }
+    if (lane == 31) s_mstart[P] = incl;
+  }
+  __syncthreads();
+  if (tid <= P) p.mstart[tid] = s_mstart[tid];
+  if (tid < P) {  // hist[w][e] becomes the first permuted row of warp w's pairs of expert e
+    int32_t base = s_mstart[tid] * 128;
+    for (int w = 0; w < kPermWarps; ++w) {
+      const int32_t c = hist[w][tid];
+      hist[w][tid] = base;
+      base += c;
+    }
+    // padding rows of this expert: no token
+    const int32_t end = s_mstart[tid + 1] * 128;
+    for (int32_t r = base; r < end; ++r) {
+      p.row_tok[r] = -1;
+      p.row_w[r] = 0.f;
+    }
+  }
+  __syncthreads();
+  // pass 2: stable placement (pairs in ascending (token, slot) order within each warp's range)
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int64_t qb = q0; qb < q1; qb += 32) {
+    const int64_t q = qb + lane;
+    int e = -1;
+    if (q < q1) {
+      e = p.ids[q] - p.expert_base;
+      if (e < 0 || e >= P) e = -1;
+    }
+    const uint32_t active = __ballot_sync(0xffffffffu, e >= 0);
+    const uint32_t peers = __match_any_sync(0xffffffffu, e) & active;
+    int32_t pos = -1;
+    if (e >= 0) pos = hist[warp][e] + __popc(peers & lt_mask);
+    __syncwarp();
+    if (e >= 0 && (peers & lt_mask) == 0) hist[warp][e] += __popc(peers);
+    __syncwarp();
+    if (q < q1) {
+      p.pair_pos[q] = pos;
+      if (pos >= 0) {
+        p.row_tok[pos] = (int32_t)(q / p.topk);
+        p.row_w[pos] = p.w[q];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ K3b-2: gather + MXFP8 quantisation
+struct QuantArgs {
+  const JobDesc* desc;
+  const int32_t* mstart;
+  int32_t P, H;
+  const __nv_bfloat16* x;  // [n, H] in the RecvArena
+  const int32_t* row_tok;
+  uint8_t* xq;     // [m_cap, H] E4M3
+  uint8_t* xq_sf;  // scale atoms [m_cap/128][H/128][512]
+};
+
+// Quantise 32 consecutive fp32 values to E4M3 with one E8M0 scale; returns the scale byte.
+__device__ __forceinline__ uint32_t mx_quant32(const float (&v)[32], uint4& lo, uint4& hi) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const uint32_t sb = mx_e4m3_scale_byte(amax);
+  const float inv = mx_inv_scale(sb);
+  uint32_t wv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t a = cvt_e4m3x2(v[4 * i] * inv, v[4 * i + 1] * inv);
+    const uint32_t b = cvt_e4m3x2(v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+    wv[i] = a | (b << 16);
+  }
+  lo = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  hi = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+  return sb;
+}
+
+__global__ void __launch_bounds__(256) quant_permute_kernel(const __grid_constant__ QuantArgs p) {
+  if (!p.desc->valid) return;
+  const int64_t rows = (int64_t)p.mstart[p.P] * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int H = p.H, kblocks = H / 32;
+  for (int64_t r = gwarp; r < rows; r += nwarps) {
+    const int32_t t = p.row_tok[r];
+    if (t < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)t * H);
+    for (int kb = lane; kb < kblocks; kb += 32) {
+      float v[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 u = src[kb * 4 + c];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          v[c * 8 + 2 * i] = f.x;
+          v[c * 8 + 2 * i + 1] = f.y;
+        }
+      }
+      uint4 lo, hi;
+      const uint32_t sb = mx_quant32(v, lo, hi);
+      uint4* dst = reinterpret_cast<uint4*>(p.xq + r * H + (int64_t)kb * 32);
+      dst[0] = lo;
+      dst[1] = hi;
+      p.xq_sf[sf_atom_off(r, kb, kblocks)] = (uint8_t)sb;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ K4/K5: grouped block-scaled GEMM
+namespace gemm {
+constexpr int BM = 128, BN = 256, BK = 128;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;        // E4M3 tile
+constexpr int B_BYTES = BN * BK;        // E2M1 tile as the MMA reads it: 16 values per 16 bytes
+constexpr int B_TX = BN * BK / 2;       // bytes the TMA moves for it (packed in global memory)
+constexpr int SFA_BYTES = 512, SFB_BYTES = 1024;
+constexpr uint32_t STAGE_TX = A_BYTES + B_TX + SFA_BYTES + SFB_BYTES;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int THREADS = 32 * (2 + NUM_EPI_WARPS);
+constexpr uint32_t TMEM_COLS = 512, TMEM_ACC = 0, TMEM_SFA = 256, TMEM_SFB = 264;
+constexpr int SMEM_TILES = STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES);
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + SMEM_TILES + 1024 /*barriers*/ + 4 * (ASAP_MAX_LOCAL_EXPERTS + 8);
+
+// tcgen05 instruction descriptor, kind::mxf8f6f4 block-scaled: A = E4M3, B = E2M1, both K-major,
+// UE8M0 scales, M x N.  Scale-factor byte ids are OR-ed in per MMA.
+__host__ __device__ constexpr uint32_t idesc_mxf8f6f4(int M, int N) {
+  return (0u << 7) | (5u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_sw128(const void* p) {
+  const uint64_t a = smem_u32(p);
+  return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Descriptor of one 512-byte scale-factor atom (32 rows x 16 bytes, no swizzle) for tcgen05.cp.
+__device__ __forceinline__ uint64_t sdesc_sf(const void* p) {
+  const uint64_t a = smem_u32(p);
+  return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
+}
+
+struct Params {
+  CUtensorMap tmap_a;  // activations [m_cap, K] bytes (E4M3)
+  CUtensorMap tmap_b;  // weights [P * N, K] E2M1 (4-bit, unpacked to 16 B per 16 values in smem)
+  const uint8_t* sfa;  // activation scale atoms [m_cap/128][K/128][512]
+  const uint8_t* sfb;  // weight scale atoms per expert [K/128][N/128][512]
+  uint64_t sfb_expert_stride;
+  const JobDesc* desc;
+  const int32_t* mstart;   // [P + 1]
+  const int32_t* row_tok;  // [m_cap]
+  const float* row_w;      // [m_cap]
+  uint8_t* out_q;          // GEMM1: [m_cap, N/2] E4M3
+  uint8_t* out_sf;         // GEMM1: scale atoms [m_cap/128][(N/2)/128][512]
+  __nv_bfloat16* out_bf;   // GEMM2: [m_cap, N]
+  int32_t P, N, K;
+  float swiglu_limit;
+  uint64_t status, timeout_ns;
+};
+
+__device__ __forceinline__ void decode_tile(const int32_t* s_mstart, int P, int NT, int tile, int& e, int& m_blk,
+                                            int& n_t) {
+  const int v = tile / NT;  // lies in [mstart[e], mstart[e+1]) of its expert
+  int lo = 0, hi = P;       // first index with mstart > v, minus one
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (s_mstart[mid] <= v) lo = mid + 1;
+    else hi = mid;
+  }
+  e = lo - 1;
+  const int mt = s_mstart[e + 1] - s_mstart[e];
+  const int local = tile - NT * s_mstart[e];
+  n_t = local / mt;
+  m_blk = s_mstart[e] + local % mt;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
+
+// EPI 0: h = silu(gate) * up, quantised to MXFP8 (GEMM1).  EPI 1: bf16(acc * w[row]) (GEMM2).
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sSFA = sB + STAGES * B_BYTES;
+  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * SFB_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_mstart = reinterpret_cast<int32_t*>(tmem_slot + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = p.P;
+  const bool valid_job = p.desc->valid != 0;
+  for (int i = threadIdx.x; i <= P; i += THREADS) s_mstart[i] = valid_job ? p.mstart[i] : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, NUM_EPI_WARPS);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tmap_a);
+    prefetch_tmap(&p.tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int NT = p.N / BN, KT = p.K / BK;
+  const int num_tiles = s_mstart[P] * NT;
+  const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int e, m_blk, n_t;
+        decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
+        const int a_row = m_blk * BM;
+        const int b_row = e * p.N + n_t * BN;
+        const uint8_t* sfa = p.sfa + (uint64_t)m_blk * KT * SFA_BYTES;
+        const uint8_t* sfb = p.sfb + (uint64_t)e * p.sfb_expert_stride + (uint64_t)n_t * SFB_BYTES;
+        const uint64_t sfb_kstride = (uint64_t)(p.N / 128) * 512;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, deadline, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_TX);
+          tma_load_2d(sA + stage * A_BYTES, &p.tmap_a, kt * BK, a_row, &full[stage]);
+          tma_load_2d(sB + stage * B_BYTES, &p.tmap_b, kt * BK, b_row, &full[stage]);
+          bulk_load(sSFA + stage * SFA_BYTES, sfa + (uint64_t)kt * SFA_BYTES, SFA_BYTES, &full[stage]);
+          bulk_load(sSFB + stage * SFB_BYTES, sfb + (uint64_t)kt * sfb_kstride, SFB_BYTES, &full[stage]);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the copies of the last armed stages must land before this CTA may exit.
+      const uint64_t drain_deadline = globaltimer_ns() + 200000000ull;
+      const int n_drain = issued < STAGES ? issued : STAGES;
+      volatile int no_abort = 0;
+      for (int i = 0; i < n_drain; ++i) {
+        int s = stage - 1 - i;
+        uint32_t ph = phase;
+        if (s < 0) {
+          s += STAGES;
+          ph ^= 1u;
+        }
+        mbar_wait(&full[s], ph, drain_deadline, &no_abort);
+      }
+      if (!ok) report(p.status, status_word(ASAP_ST_PIPELINE_TIMEOUT, 0, 0, EPI));
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      const uint32_t idesc = idesc_mxf8f6f4(BM, BN);
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(acc_empty, acc_phase ^ 1u, deadline, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&full[stage], phase, deadline, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          tc_cp_32x128b_warpx4(tmem_base + TMEM_SFA, sdesc_sf(sSFA + stage * SFA_BYTES));
+          tc_cp_32x128b_warpx4(tmem_base + TMEM_SFB, sdesc_sf(sSFB + stage * SFB_BYTES));
+          tc_cp_32x128b_warpx4(tmem_base + TMEM_SFB + 4, sdesc_sf(sSFB + stage * SFB_BYTES + 512));
+          const uint64_t adesc = sdesc_sw128(sA + stage * A_BYTES);
+          const uint64_t bdesc = sdesc_sw128(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            const uint32_t id = idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4);
+            tc_mma_mxf8f6f4(tmem_base + TMEM_ACC, adesc + 2ull * k, bdesc + 2ull * k, id, (kt | k) != 0,
+                            (tmem_base + TMEM_SFA) | ((uint32_t)k << 30), (tmem_base + TMEM_SFB) | ((uint32_t)k << 30));
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(acc_full);
+        acc_phase ^= 1u;
+      }
+      // every MMA this thread issued has completed before TMEM is released
+      tc_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, globaltimer_ns() + 200000000ull, &no_abort);
+    }
+  } else {
+    // ---------------- epilogue warps
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // which half of the tile's columns
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int e, m_blk, n_t;
+      decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
+      if (!mbar_wait(acc_full, acc_phase, deadline, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)m_blk * BM + row_in_tile;
+      const bool valid = p.row_tok[row] >= 0;
+      if constexpr (EPI == 0) {
+        const int I = p.N / 2;
+        const int kblocks = I / 32;
+        const float lim = p.swiglu_limit;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int col = half * 64 + c * 32;
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_lane + TMEM_ACC + col, g);
+          tmem_ld_32x32b_x32(t_lane + TMEM_ACC + 128 + col, u);
+          tmem_wait_ld();
+          if (c == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+          }
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+            if (lim > 0.f) {
+              gv = fminf(gv, lim);
+              uv = fminf(fmaxf(uv, -lim), lim);
+            }
+            h[i] = silu_f(gv) * uv;
+          }
+          uint4 lo, hi;
+          const uint32_t sb = mx_quant32(h, lo, hi);
+          if (valid) {
+            const int hcol = n_t * 128 + col;
+            uint4* dst = reinterpret_cast<uint4*>(p.out_q + row * I + hcol);
+            dst[0] = lo;
+            dst[1] = hi;
+            p.out_sf[sf_atom_off(row, hcol / 32, kblocks)] = (uint8_t)sb;
+          }
+        }
+      } else {
+        const float wr = p.row_w[row];
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int col = half * 128 + c * 32;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_lane + TMEM_ACC + col, v);
+          tmem_wait_ld();
+          if (c == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+          }
+          if (valid) {
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const __nv_bfloat162 b2 =
+                  __floats2bfloat162_rn(__uint_as_float(v[2 * i]) * wr, __uint_as_float(v[2 * i + 1]) * wr);
+              o[i] = *reinterpret_cast<const uint32_t*>(&b2);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(p.out_bf + row * p.N + (int64_t)n_t * BN + col);
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+            dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+          }
+        }
+      }
+      acc_phase ^= 1u;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+}  // namespace gemm
+
+// ------------------------------------------------------------------ K5b: weighted reduce + reply
+struct FinalArgs {
+  const JobDesc* desc;
+  int32_t topk, H;
+  const int32_t* pair_pos;    // [n, topk]
+  const __nv_bfloat16* y2;    // [m_cap, H], rows already weighted
+  __nv_bfloat16* reply_seg;   // A's ResultArena seg(f, slot) (peer memory in a multi-GPU deployment)
+  uint32_t* reply_done;       // A's done flag (f, slot); NULL: no flag
+  JobDesc* desc_rw;
+};
+
+__global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_constant__ FinalArgs p) {
+  if (!p.desc->valid) return;
+  const int n = p.desc->n;
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int H = p.H, nvec = H / 8;
+  for (int64_t t = gwarp; t < n; t += nwarps) {
+    int32_t pos[32];
+    for (int j = 0; j < p.topk; ++j) pos[j] = p.pair_pos[t * p.topk + j];
+    for (int c = lane; c < nvec; c += 32) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int j = 0; j < p.topk; ++j) {
+        if (pos[j] < 0) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(p.y2 + (int64_t)pos[j] * H + (int64_t)c * 8);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          acc[2 * i] += f.x;
+          acc[2 * i + 1] += f.y;
+        }
+      }
+      uint4 r;
+      __nv_bfloat162* rh = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      *reinterpret_cast<uint4*>(p.reply_seg + t * H + (int64_t)c * 8) = r;
+    }
+  }
+  // Reply rows visible to A before its done flag (server.py:347-350 ordering).
+  __syncthreads();
+  __shared__ uint32_t last;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = (atomicAdd(&p.desc_rw->sync, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0 && p.reply_done) {
+    __threadfence_system();
+    st_release_sys_u32(p.reply_done, p.desc->seq);
+  }
+}
+
+// ------------------------------------------------------------------ host side: tensor maps, handles
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return ASAP_ECUDA;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled(%s) failed: %d", what, (int)r);
+    return ASAP_ECUDA;
+  }
+  return ASAP_OK;
+}
+
+struct ExpertsHandle {
+  asap_mxfp4_experts_t e;
+  CUtensorMap w13_map, w2_map;
+};
+constexpr int kTimedKernels = 5;  // route_local, quant_permute, gemm1, gemm2, finalize_reply
+constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
+struct WsHandle {
+  uint8_t* base;
+  WsLayout L;
+  CUtensorMap xq_map, hq_map;
+  bool timing = false;
+  int jobs = 0;  // jobs recorded since enable
+  cudaEvent_t ev[kTimedJobs][kTimedKernels + 1] = {};
+};
+
+static std::mutex g_mu;
+static std::unordered_map<uint64_t, ExpertsHandle*> g_experts;
+static std::unordered_map<uint64_t, WsHandle*> g_ws;
+static uint64_t g_next = 1;
+
+static ExpertsHandle* get_experts(uint64_t h) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_experts.find(h);
+  return it == g_experts.end() ? nullptr : it->second;
+}
+static WsHandle* get_ws(uint64_t h) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_ws.find(h);
+  return it == g_ws.end() ? nullptr : it->second;
+}
+
+static bool gemm_attr_set = false;
+
+static int ensure_gemm_attrs() {
+  if (gemm_attr_set) return ASAP_OK;
+  ASAP_CUDA(cudaFuncSetAttribute(gemm::moe_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemm::moe_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm::SMEM_BYTES));
+  gemm_attr_set = true;
+  return ASAP_OK;
+}
+
+}  // namespace asap
+
+using namespace asap;
+
+extern "C" {
+
+int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
+  if (!e || !handle) {
+    set_error("asap_experts_register: NULL argument");
+    return ASAP_EINVAL;
+  }
+  if (e->num_local < 1 || e->num_local > ASAP_MAX_LOCAL_EXPERTS || e->hidden % 256 || e->inter % 128 ||
+      e->hidden <= 0 || e->inter <= 0 || e->expert_base < 0) {
+    set_error("asap_experts_register: need 1 <= num_local <= %d, hidden %% 256 == 0, inter %% 128 == 0 (got %d, %d, %d)",
+              ASAP_MAX_LOCAL_EXPERTS, e->num_local, e->hidden, e->inter);
+    return ASAP_EINVAL;
+  }
+  if ((e->w13 & 31) || (e->w2 & 31) || (e->w13_sf & 15) || (e->w2_sf & 15) || !e->w13 || !e->w2 || !e->w13_sf ||
+      !e->w2_sf) {
+    set_error("asap_experts_register: weights must be 32-byte and scales 16-byte aligned, non-NULL");
+    return ASAP_EINVAL;
+  }
+  ExpertsHandle* h = new ExpertsHandle;
+  h->e = *e;
+  const uint64_t P = e->num_local, H = e->hidden, I = e->inter;
+  int rc = make_tmap_2d(&h->w13_map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w13, H, P * 2 * I, H / 2,
+                        gemm::BK, gemm::BN, "w13");
+  if (!rc)
+    rc = make_tmap_2d(&h->w2_map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2, gemm::BK,
+                      gemm::BN, "w2");
+  if (rc) {
+    delete h;
+    return rc;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  *handle = g_next++;
+  g_experts[*handle] = h;
+  return ASAP_OK;
+}
+
+int asap_experts_release(uint64_t handle) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_experts.find(handle);
+  if (it == g_experts.end()) {
+    set_error("asap_experts_release: unknown handle");
+    return ASAP_EINVAL;
+  }
+  delete it->second;
+  g_experts.erase(it);
+  return ASAP_OK;
+}
+
+uint64_t asap_ffn_ws_bytes(int32_t n_max, int32_t topk, int32_t num_local, int32_t hidden, int32_t inter) {
+  if (n_max < 1 || topk < 1 || num_local < 1 || hidden < 1 || inter < 1) return 0;
+  return ws_layout(n_max, topk, num_local, hidden, inter).total;
+}
+
+int asap_ffn_ws_register(uint64_t ws, int32_t n_max, int32_t topk, int32_t num_local, int32_t hidden,
+                         int32_t inter, uint64_t* handle) {
+  if (!ws || (ws & 1023) || !handle || n_max < 1 || topk < 1 || topk > 32 || num_local < 1 ||
+      num_local > ASAP_MAX_LOCAL_EXPERTS || hidden % 256 || inter % 128 || hidden <= 0 || inter <= 0) {
+    set_error("asap_ffn_ws_register: ws must be 1024-byte aligned; 1 <= topk <= 32, 1 <= num_local <= %d, "
+              "hidden %% 256 == 0, inter %% 128 == 0",
+              ASAP_MAX_LOCAL_EXPERTS);
+    return ASAP_EINVAL;
+  }
+  WsHandle* h = new WsHandle;
+  h->base = (uint8_t*)ws;
+  h->L = ws_layout(n_max, topk, num_local, hidden, inter);
+  int rc = make_tmap_2d(&h->xq_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, h->base + h->L.xq, hidden, h->L.m_cap, hidden,
+                        gemm::BK, gemm::BM, "xq");
+  if (!rc)
+    rc = make_tmap_2d(&h->hq_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, h->base + h->L.hq, inter, h->L.m_cap, inter,
+                      gemm::BK, gemm::BM, "hq");
+  if (rc) {
+    delete h;
+    return rc;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  *handle = g_next++;
+  g_ws[*handle] = h;
+  return ASAP_OK;
+}
+
+int asap_ffn_ws_release(uint64_t handle) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_ws.find(handle);
+  if (it == g_ws.end()) {
+    set_error("asap_ffn_ws_release: unknown handle");
+    return ASAP_EINVAL;
+  }
+  for (int j = 0; j < kTimedJobs; ++j)
+    for (int i = 0; i <= kTimedKernels; ++i)
+      if (it->second->ev[j][i]) cudaEventDestroy(it->second->ev[j][i]);
+  delete it->second;
+  g_ws.erase(it);
+  return ASAP_OK;
+}
+
+int asap_ffn_wait(uint64_t ws_handle, uint64_t bell, uint32_t last_seq, int32_t expect_epoch, int32_t n_max,
+                  uint64_t status, uint64_t timeout_ns, void* stream) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w || !bell || (bell & 7)) {
+    set_error("asap_ffn_wait: unknown workspace handle or misaligned doorbell");
+    return ASAP_EINVAL;
+  }
+  if (n_max < 1 || n_max > w->L.n_max) {
+    set_error("asap_ffn_wait: n_max %d outside the workspace's %d", n_max, w->L.n_max);
+    return ASAP_EINVAL;
+  }
+  ffn_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((JobDesc*)(w->base + w->L.desc), (const uint64_t*)bell,
+                                                       last_seq, expect_epoch, n_max, status, timeout_ns);
+  ASAP_CHECK_LAUNCH("ffn_wait_kernel");
+  return ASAP_OK;
+}
+
+int asap_ffn_post(uint64_t ws_handle, uint32_t seq, int32_t n, int32_t layer_id, int32_t epoch, void* stream) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w) {
+    set_error("asap_ffn_post: unknown workspace handle");
+    return ASAP_EINVAL;
+  }
+  if (n < 1 || n > w->L.n_max) {
+    set_error("asap_ffn_post: n_tokens %d outside [1, %d]", n, w->L.n_max);
+    return ASAP_EINVAL;
+  }
+  ffn_post_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((JobDesc*)(w->base + w->L.desc), seq, n, layer_id, epoch);
+  ASAP_CHECK_LAUNCH("ffn_post_kernel");
+  return ASAP_OK;
+}
+
+int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64_t ids, uint64_t w,
+                 uint64_t reply_seg, uint64_t reply_done, float swiglu_limit, uint64_t status, uint64_t timeout_ns,
+                 void* stream) {
+  ExpertsHandle* eh = get_experts(experts_handle);
+  WsHandle* wh = get_ws(ws_handle);
+  if (!eh || !wh) {
+    set_error("asap_ffn_job: unknown experts or workspace handle");
+    return ASAP_EINVAL;
+  }
+  const asap_mxfp4_experts_t& E = eh->e;
+  const WsLayout& L = wh->L;
+  if (E.num_local != L.P || E.hidden != L.H || E.inter != L.I) {
+    set_error("asap_ffn_job: experts (P=%d H=%d I=%d) and workspace (P=%d H=%d I=%d) disagree", E.num_local,
+              E.hidden, E.inter, L.P, L.H, L.I);
+    return ASAP_EINVAL;
+  }
+  if (!x || !ids || !w || !reply_seg || (x & 15) || (reply_seg & 15) || (reply_done & 3)) {
+    set_error("asap_ffn_job: x/reply_seg must be 16-byte aligned and non-NULL");
+    return ASAP_EINVAL;
+  }
+  int rc = ensure_gemm_attrs();
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* B = wh->base;
+  JobDesc* desc = (JobDesc*)(B + L.desc);
+  const int sms = sm_count();
+
+  PermArgs pa;
+  pa.desc = desc;
+  pa.ids = (const int32_t*)ids;
+  pa.w = (const float*)w;
+  pa.topk = L.topk;
+  pa.P = L.P;
+  pa.expert_base = E.expert_base;
+  pa.ecnt = (int32_t*)(B + L.ecnt);
+  pa.mstart = (int32_t*)(B + L.mstart);
+  pa.pair_pos = (int32_t*)(B + L.pair_pos);
+  pa.row_tok = (int32_t*)(B + L.row_tok);
+  pa.row_w = (float*)(B + L.row_w);
+  const int slot_ev = wh->jobs % kTimedJobs;
+  if (wh->timing) ++wh->jobs;
+  auto mark = [&](int i) {
+    if (wh->timing) cudaEventRecord(wh->ev[slot_ev][i], st);
+  };
+  mark(0);
+  route_local_kernel<<<1, kPermThreads, 0, st>>>(pa);
+  ASAP_CHECK_LAUNCH("route_local_kernel");
+  mark(1);
+
+  QuantArgs qa;
+  qa.desc = desc;
+  qa.mstart = pa.mstart;
+  qa.P = L.P;
+  qa.H = L.H;
+  qa.x = (const __nv_bfloat16*)x;
+  qa.row_tok = pa.row_tok;
+  qa.xq = B + L.xq;
+  qa.xq_sf = B + L.xq_sf;
+  quant_permute_kernel<<<sms * 4, 256, 0, st>>>(qa);
+  ASAP_CHECK_LAUNCH("quant_permute_kernel");
+  mark(2);
+
+  gemm::Params g1;
+  memset(&g1, 0, sizeof(g1));
+  g1.tmap_a = wh->xq_map;
+  g1.tmap_b = eh->w13_map;
+  g1.sfa = B + L.xq_sf;
+  g1.sfb = (const uint8_t*)E.w13_sf;
+  g1.sfb_expert_stride = (uint64_t)(L.H / 32) * (2 * L.I);
+  g1.desc = desc;
+  g1.mstart = pa.mstart;
+  g1.row_tok = pa.row_tok;
+  g1.row_w = pa.row_w;
+  g1.out_q = B + L.hq;
+  g1.out_sf = B + L.hq_sf;
+  g1.P = L.P;
+  g1.N = 2 * L.I;
+  g1.K = L.H;
+  g1.swiglu_limit = swiglu_limit;
+  g1.status = status;
+  g1.timeout_ns = timeout_ns;
+  gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
+  ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
+  mark(3);
+
+  gemm::Params g2 = g1;
+  g2.tmap_a = wh->hq_map;
+  g2.tmap_b = eh->w2_map;
+  g2.sfa = B + L.hq_sf;
+  g2.sfb = (const uint8_t*)E.w2_sf;
+  g2.sfb_expert_stride = (uint64_t)(L.I / 32) * L.H;
+  g2.out_q = nullptr;
+  g2.out_sf = nullptr;
+  g2.out_bf = (__nv_bfloat16*)(B + L.y2);
+  g2.N = L.H;
+  g2.K = L.I;
+  gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
+  ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
+  mark(4);
+
+  FinalArgs fa;
+  fa.desc = desc;
+  fa.topk = L.topk;
+  fa.H = L.H;
+  fa.pair_pos = pa.pair_pos;
+  fa.y2 = (const __nv_bfloat16*)(B + L.y2);
+  fa.reply_seg = (__nv_bfloat16*)reply_seg;
+  fa.reply_done = (uint32_t*)reply_done;
+  fa.desc_rw = desc;
+  finalize_reply_kernel<<<sms * 4, 256, 0, st>>>(fa);
+  ASAP_CHECK_LAUNCH("finalize_reply_kernel");
+  mark(5);
+  return ASAP_OK;
+}
+
+int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w) {
+    set_error("asap_ffn_enable_timing: unknown workspace handle");
+    return ASAP_EINVAL;
+  }
+  if (enable && !w->ev[0][0])
+    for (int j = 0; j < kTimedJobs; ++j)
+      for (int i = 0; i <= kTimedKernels; ++i) ASAP_CUDA(cudaEventCreate(&w->ev[j][i]));
+  w->timing = enable != 0;
+  w->jobs = 0;
+  return ASAP_OK;
+}
+
+int asap_ffn_last_timing(uint64_t ws_handle, float* ms, int32_t n) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w || !ms || n < kTimedKernels || !w->ev[0][0] || w->jobs == 0) {
+    set_error("asap_ffn_last_timing: timing not enabled, no job recorded, or buffer smaller than %d",
+              kTimedKernels);
+    return ASAP_EINVAL;
+  }
+  const int count = std::min(w->jobs, kTimedJobs);
+  for (int i = 0; i < kTimedKernels; ++i) ms[i] = 0.f;
+  for (int j = 0; j < count; ++j) {
+    const int s = (w->jobs - 1 - j) % kTimedJobs;
+    ASAP_CUDA(cudaEventSynchronize(w->ev[s][kTimedKernels]));
+    for (int i = 0; i < kTimedKernels; ++i) {
+      float t = 0.f;
+      ASAP_CUDA(cudaEventElapsedTime(&t, w->ev[s][i], w->ev[s][i + 1]));
+      ms[i] += t / count;
+    }
+  }
+  return ASAP_OK;
+}
+
+int asap_ffn_job_info(uint64_t ws_handle, int32_t* n, int32_t* layer_id, uint32_t* seq, int32_t* epoch,
+                      int32_t* valid, void* stream) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w) {
+    set_error("asap_ffn_job_info: unknown workspace handle");
+    return ASAP_EINVAL;
+  }
+  JobDesc d;
+  ASAP_CUDA(cudaMemcpyAsync(&d, w->base + w->L.desc, sizeof(d), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  ASAP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  if (n) *n = d.n;
+  if (layer_id) *layer_id = d.layer;
+  if (seq) *seq = d.seq;
+  if (epoch) *epoch = d.epoch;
+  if (valid) *valid = d.valid;
+  return ASAP_OK;
+}
+
+int asap_ffn_debug_ptrs(uint64_t ws_handle, uint64_t* expert_counts, uint64_t* pair_pos, uint64_t* xq,
+                        uint64_t* xq_sf, uint64_t* hq, uint64_t* hq_sf, uint64_t* y2) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w) {
+    set_error("asap_ffn_debug_ptrs: unknown workspace handle");
+    return ASAP_EINVAL;
+  }
+  const uint64_t b = (uint64_t)w->base;
+  if (expert_counts) *expert_counts = b + w->L.ecnt;
+  if (pair_pos) *pair_pos = b + w->L.pair_pos;
+  if (xq) *xq = b + w->L.xq;
+  if (xq_sf) *xq_sf = b + w->L.xq_sf;
+  if (hq) *hq = b + w->L.hq;
+  if (hq_sf) *hq_sf = b + w->L.hq_sf;
+  if (y2) *y2 = b + w->L.y2;
+  return ASAP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,631 @@
+// libasap transport: context/memory entry points, A-side dispatch (route + pack + doorbell) and combine.
+//
+// Reference behaviour replaced here (python/sgl_asap_plugin/transport/):
+//   channel.py:317-362  AttnChannel.send   -> asap_dispatch (K1 route, K2 pack + doorbell release)
+//   channel.py:364-377  AttnChannel.wait   -> asap_combine prologue (bounded device spin on done flags)
+//   srt/layers/moe/token_dispatcher/asap.py:174-184 AsapBuffer.recv -> asap_combine body (fp32 sum -> bf16)
+//   cuda_wrapper.py / memory.py IPC + host-register calls -> asap_arena_* / asap_host_*
+#include <stdarg.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace asap {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  set_error("%s failed: %d %s", what, (int)err, cudaGetErrorString(err));
+  return ASAP_ECUDA;
+}
+
+static int check_geometry(const asap_geometry_t* g) {
+  if (!g) {
+    set_error("geometry is NULL");
+    return ASAP_EINVAL;
+  }
+  const int32_t v[7] = {g->num_a, g->group, g->slots, g->n_max, g->hidden, g->topk, g->num_f};
+  const char* names[7] = {"num_a", "group", "slots", "n_max", "hidden", "topk", "num_f"};
+  for (int i = 0; i < 7; ++i)
+    if (v[i] < 1) {
+      set_error("invalid transport geometry: %s=%d", names[i], v[i]);
+      return ASAP_EINVAL;
+    }
+  if (g->num_a % g->group) {
+    set_error("invalid transport geometry: num_a=%d is not a multiple of group=%d", g->num_a, g->group);
+    return ASAP_EINVAL;
+  }
+  if ((uint32_t)g->n_max > kMaxTokens) {
+    set_error("invalid transport geometry: n_max=%d exceeds the %u tokens a doorbell can announce", g->n_max,
+              kMaxTokens);
+    return ASAP_EINVAL;
+  }
+  return ASAP_OK;
+}
+
+// ------------------------------------------------------------------ routing workspace layout
+// [0, 256)      int32 count[ASAP_MAX_F]  (rows announced to F rank f, >= 1)
+// [256, 320)    int32 pad[ASAP_MAX_F]    (1 when f received no token and gets one row of ids -1)
+// [320, 384)    uint32 arrive counter of the pack grid
+// [384, 512)    reserved
+// [512, ...)    int32 row_of[num_f][n_max]: compacted row of token t in f's region, -1 if not routed
+constexpr uint64_t kWsCount = 0, kWsPad = 256, kWsSync = 320, kWsRows = 512;
+
+// K1: one CTA. Backpressure wait, then the per-F-rank compacted row index of every token (ascending token
+// order, a stable compaction), via a block-wide exclusive scan per F rank.
+constexpr int kRouteThreads = 1024;
+
+struct Bounds {
+  int32_t v[ASAP_MAX_F + 1];
+};
+
+__global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
+    asap_geometry_t g, int32_t slot, uint32_t seq, const void* __restrict__ ids, int32_t ids_is_int64, int32_t n,
+    const __grid_constant__ Bounds bounds_g, const uint8_t* result, uint8_t* ws, int32_t backpressure,
+    uint64_t status, uint64_t timeout_ns) {
+  __shared__ int32_t bounds[ASAP_MAX_F + 1];
+  __shared__ int32_t warp_tot[ASAP_MAX_F][32];
+  __shared__ int32_t abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int F = g.num_f;
+  if (tid <= F) bounds[tid] = bounds_g.v[tid];
+  if (tid == 0) abort_flag = 0;
+  __syncthreads();
+
+  int32_t* count = reinterpret_cast<int32_t*>(ws + kWsCount);
+  int32_t* pad = reinterpret_cast<int32_t*>(ws + kWsPad);
+  int32_t* row_of = reinterpret_cast<int32_t*>(ws + kWsRows);
+
+  // Backpressure (channel.py:337-339): the previous message of this slot must be answered by every F.
+  if (backpressure && tid < F) {
+    const uint32_t* done = reinterpret_cast<const uint32_t*>(result + done_off(g, tid, slot));
+    const uint64_t deadline = globaltimer_ns() + timeout_ns;
+    while ((int32_t)(ld_acquire_sys_u32(done) - (seq - 1u)) < 0) {
+      if (globaltimer_ns() > deadline) {
+        report(status, status_word(ASAP_ST_BACKPRESSURE_TIMEOUT, tid, slot, seq));
+        atomicExch(&abort_flag, 1);
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  __syncthreads();
+  if (abort_flag) {
+    if (tid < F) count[tid] = -1;  // pack sees -1 and sends nothing
+    return;
+  }
+
+  // Each thread owns a contiguous run of tokens; masks fit 16 F ranks.
+  const int per = (n + kRouteThreads - 1) / kRouteThreads;
+  const int t0 = min(n, tid * per), t1 = min(n, t0 + per);
+  int32_t mycnt[ASAP_MAX_F];
+#pragma unroll
+  for (int f = 0; f < ASAP_MAX_F; ++f) mycnt[f] = 0;
+  const int64_t e_end = bounds[F];
+  for (int t = t0; t < t1; ++t) {
+    uint32_t mask = 0;
+    for (int j = 0; j < g.topk; ++j) {
+      int64_t e = ids_is_int64 ? reinterpret_cast<const int64_t*>(ids)[(int64_t)t * g.topk + j]
+                               : reinterpret_cast<const int32_t*>(ids)[(int64_t)t * g.topk + j];
+      if (e < bounds[0] || e >= e_end) continue;
+      int f = 0;
+      while (f + 1 < F && e >= bounds[f + 1]) ++f;
+      mask |= 1u << f;
+    }
+#pragma unroll
+    for (int f = 0; f < ASAP_MAX_F; ++f) mycnt[f] += (mask >> f) & 1u;
+  }
+  // exclusive scan of mycnt[f] over threads, for every f
+  int32_t myoff[ASAP_MAX_F];
+#pragma unroll
+  for (int f = 0; f < ASAP_MAX_F; ++f) {
+    if (f >= F) break;
+    int32_t v = mycnt[f];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      int32_t u = __shfl_up_sync(0xffffffffu, v, d);
+      if (lane >= d) v += u;
+    }
+    if (lane == 31) warp_tot[f][warp] = v;
+    myoff[f] = v - mycnt[f];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int f = 0; f < F; ++f) {
+      int32_t v = warp_tot[f][lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        int32_t u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
+      }
+      warp_tot[f][lane] = v;  // inclusive
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int f = 0; f < ASAP_MAX_F; ++f) {
+    if (f >= F) break;
+    if (warp > 0) myoff[f] += warp_tot[f][warp - 1];
+  }
+  // second pass: write the row indices
+  for (int t = t0; t < t1; ++t) {
+    uint32_t mask = 0;
+    for (int j = 0; j < g.topk; ++j) {
+      int64_t e = ids_is_int64 ? reinterpret_cast<const int64_t*>(ids)[(int64_t)t * g.topk + j]
+                               : reinterpret_cast<const int32_t*>(ids)[(int64_t)t * g.topk + j];
+      if (e < bounds[0] || e >= e_end) continue;
+      int f = 0;
+      while (f + 1 < F && e >= bounds[f + 1]) ++f;
+      mask |= 1u << f;
+    }
+    for (int f = 0; f < F; ++f) {
+      int32_t r = -1;
+      if ((mask >> f) & 1u) r = myoff[f]++;
+      row_of[(int64_t)f * g.n_max + t] = r;
+    }
+  }
+  if (tid < F) {
+    const int32_t total = warp_tot[tid][31];
+    count[tid] = total > 0 ? total : 1;
+    pad[tid] = total > 0 ? 0 : 1;
+  }
+  if (tid == 0) *reinterpret_cast<uint32_t*>(ws + kWsSync) = 0;
+}
+
+// K2: pack every routed token into every F rank that owns one of its experts, then the last CTA to finish
+// releases the doorbells.  One warp per token; 16-byte vector loads and stores.
+struct PackArgs {
+  asap_geometry_t g;
+  int32_t a, slot, layer_id, n;
+  uint32_t seq;
+  int32_t ids_is_int64, w_is_bf16;
+  const uint8_t* x;
+  const void* ids;
+  const void* w;
+  const uint8_t* ws;
+  uint8_t* recv[ASAP_MAX_F];
+  uint64_t* bell[ASAP_MAX_F];
+  uint32_t epoch[ASAP_MAX_F];
+};
+
+__global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constant__ PackArgs p) {
+  const asap_geometry_t& g = p.g;
+  const int F = g.num_f;
+  const int32_t* count = reinterpret_cast<const int32_t*>(p.ws + kWsCount);
+  const int32_t* pad = reinterpret_cast<const int32_t*>(p.ws + kWsPad);
+  const int32_t* row_of = reinterpret_cast<const int32_t*>(p.ws + kWsRows);
+  if (count[0] < 0) return;  // backpressure timed out: send nothing
+  const Offsets o = offsets_of(g);
+  const int lane = threadIdx.x & 31;
+  const int warps_per_cta = blockDim.x >> 5;
+  const int64_t gwarp = (int64_t)blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * warps_per_cta;
+  const uint64_t row_bytes = (uint64_t)g.hidden * 2;
+  const int nvec = (int)(row_bytes / 16);
+  const uint64_t roff = region_off(g, o, p.a, p.slot);
+
+  for (int64_t t = gwarp; t < p.n; t += nwarps) {
+    int32_t rows[ASAP_MAX_F];
+    uint32_t mask = 0;
+    for (int f = 0; f < F; ++f) {
+      rows[f] = row_of[(int64_t)f * g.n_max + t];
+      if (rows[f] >= 0) mask |= 1u << f;
+    }
+    if (!mask) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (uint64_t)t * row_bytes);
+    for (int c = lane; c < nvec; c += 32) {
+      const uint4 v = __ldg(src + c);
+      for (uint32_t m = mask; m; m &= m - 1) {
+        const int f = __ffs(m) - 1;
+        uint4* dst = reinterpret_cast<uint4*>(p.recv[f] + roff + (uint64_t)rows[f] * row_bytes);
+        dst[c] = v;
+      }
+    }
+    if (lane < g.topk) {
+      int32_t id;
+      float wt;
+      if (p.ids_is_int64)
+        id = (int32_t)reinterpret_cast<const int64_t*>(p.ids)[(int64_t)t * g.topk + lane];
+      else
+        id = reinterpret_cast<const int32_t*>(p.ids)[(int64_t)t * g.topk + lane];
+      if (p.w_is_bf16)
+        wt = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.w)[(int64_t)t * g.topk + lane]);
+      else
+        wt = reinterpret_cast<const float*>(p.w)[(int64_t)t * g.topk + lane];
+      for (uint32_t m = mask; m; m &= m - 1) {
+        const int f = __ffs(m) - 1;
+        uint8_t* base = p.recv[f] + roff;
+        reinterpret_cast<int32_t*>(base + o.ids_off)[(uint64_t)rows[f] * g.topk + lane] = id;
+        reinterpret_cast<float*>(base + o.w_off)[(uint64_t)rows[f] * g.topk + lane] = wt;
+      }
+    }
+  }
+  // F ranks that got no token: one row whose ids name no expert (F's experts skip it, the reply row is 0).
+  if (blockIdx.x == 0 && threadIdx.x < 32) {
+    for (int f = 0; f < F; ++f) {
+      if (!pad[f]) continue;
+      uint8_t* base = p.recv[f] + roff;
+      if (lane < g.topk) {
+        reinterpret_cast<int32_t*>(base + o.ids_off)[lane] = -1;
+        reinterpret_cast<float*>(base + o.w_off)[lane] = 0.f;
+      }
+    }
+  }
+  // Completion: payload visible system-wide before the doorbells (channel.py:350 ordering).
+  __syncthreads();
+  __shared__ uint32_t last;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    uint32_t* sync = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(p.ws) + kWsSync);
+    last = (atomicAdd(sync, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (last && threadIdx.x < F) {
+    __threadfence_system();
+    const int f = threadIdx.x;
+    st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.bell[f]) + bell_off(g, p.a, p.slot)),
+                       pack_doorbell(p.seq, (uint32_t)count[f], (uint32_t)p.layer_id, p.epoch[f]));
+  }
+}
+
+// K6: combine.  The bounded wait for the done flags runs first in its own 1-CTA kernel (wait_replies_kernel),
+// so a slow F rank parks one warp, not the whole GPU; this kernel then sums the partial rows.
+struct CombineArgs {
+  asap_geometry_t g;
+  int32_t slot, n;
+  uint32_t seq;
+  const uint8_t* result;
+  const uint8_t* ws;
+  const __nv_bfloat16* shared;
+  __nv_bfloat16* out;
+  uint64_t status, timeout_ns;
+};
+
+__global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ CombineArgs p) {
+  const asap_geometry_t& g = p.g;
+  const int F = g.num_f;
+  const Offsets o = offsets_of(g);
+  const int32_t* row_of = reinterpret_cast<const int32_t*>(p.ws + kWsRows);
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int H = g.hidden;
+  const int nvec = H / 8;  // 8 bf16 per 16-byte vector
+  for (int64_t t = gwarp; t < p.n; t += nwarps) {
+    int32_t rows[ASAP_MAX_F];
+    for (int f = 0; f < F; ++f) rows[f] = row_of[(int64_t)f * g.n_max + t];
+    for (int c = lane; c < nvec; c += 32) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int f = 0; f < F; ++f) {
+        if (rows[f] < 0) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(p.result + seg_off(g, o, f, p.slot) +
+                                                        (uint64_t)rows[f] * H * 2 + (uint64_t)c * 16);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 ff = __bfloat1622float2(h[i]);
+          acc[2 * i] += ff.x;
+          acc[2 * i + 1] += ff.y;
+        }
+      }
+      uint4 r;
+      __nv_bfloat162* rh = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      if (p.shared) {
+        const uint4 s = *reinterpret_cast<const uint4*>(p.shared + (uint64_t)t * H + (uint64_t)c * 8);
+        const __nv_bfloat162* sh = reinterpret_cast<const __nv_bfloat162*>(&s);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a = __bfloat1622float2(rh[i]);
+          const float2 b = __bfloat1622float2(sh[i]);
+          rh[i] = __floats2bfloat162_rn(a.x + b.x, a.y + b.y);
+        }
+      }
+      *reinterpret_cast<uint4*>(p.out + (uint64_t)t * H + (uint64_t)c * 8) = r;
+    }
+  }
+}
+
+__global__ void wait_replies_kernel(asap_geometry_t g, int32_t slot, uint32_t seq, const uint8_t* result,
+                                    uint64_t status, uint64_t timeout_ns) {
+  if (threadIdx.x >= g.num_f) return;
+  const uint32_t* done = reinterpret_cast<const uint32_t*>(result + done_off(g, threadIdx.x, slot));
+  const uint64_t deadline = globaltimer_ns() + timeout_ns;
+  while ((int32_t)(ld_acquire_sys_u32(done) - seq) < 0) {
+    if (globaltimer_ns() > deadline) {
+      report(status, status_word(ASAP_ST_REPLY_TIMEOUT, threadIdx.x, slot, seq));
+      return;
+    }
+    __nanosleep(128);
+  }
+}
+
+__global__ void write32_kernel(uint32_t* p, uint32_t v) {
+  __threadfence_system();
+  st_release_sys_u32(p, v);
+}
+
+__global__ void memset32_kernel(uint32_t* p, uint32_t v, uint64_t count) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+}  // namespace asap
+
+using namespace asap;
+
+extern "C" {
+
+const char* asap_last_error_string(void) { return g_err; }
+
+const char* asap_version(void) { return "libasap 0.1 sm_100a"; }
+
+int asap_geometry_offsets(const asap_geometry_t* g, asap_offsets_t* out) {
+  int rc = check_geometry(g);
+  if (rc) return rc;
+  if (!out) {
+    set_error("out is NULL");
+    return ASAP_EINVAL;
+  }
+  const Offsets o = offsets_of(*g);
+  out->ids_off = o.ids_off;
+  out->w_off = o.w_off;
+  out->region_bytes = o.region_bytes;
+  out->recv_bytes = o.recv_bytes;
+  out->host_bytes = o.host_bytes;
+  out->flags_bytes = o.flags_bytes;
+  out->seg_bytes = o.seg_bytes;
+  out->result_bytes = o.result_bytes;
+  return ASAP_OK;
+}
+
+int asap_pack_doorbell(uint32_t seq, uint32_t n_tokens, uint32_t layer_id, uint32_t epoch, uint64_t* word) {
+  if (!(1 <= n_tokens && n_tokens <= kMaxTokens && layer_id <= kMaxLayer && 1 <= epoch && epoch <= kMaxEpoch)) {
+    set_error("doorbell field out of range: n_tokens=%u layer_id=%u epoch=%u", n_tokens, layer_id, epoch);
+    return ASAP_EINVAL;
+  }
+  *word = pack_doorbell(seq, n_tokens, layer_id, epoch);
+  return ASAP_OK;
+}
+
+void asap_unpack_doorbell(uint64_t word, uint32_t* seq, uint32_t* n_tokens, uint32_t* layer_id, uint32_t* epoch) {
+  if (seq) *seq = (uint32_t)(word & 0xffffffffull);
+  if (n_tokens) *n_tokens = (uint32_t)((word >> 32) & kMaxTokens);
+  if (layer_id) *layer_id = (uint32_t)((word >> 49) & kMaxLayer);
+  if (epoch) *epoch = (uint32_t)(word >> 59);
+}
+
+int asap_init(int device) {
+  ASAP_CUDA(cudaSetDevice(device));
+  ASAP_CUDA(cudaFree(0));  // create / bind the primary context
+  return ASAP_OK;
+}
+
+int asap_arena_alloc(uint64_t bytes, uint64_t* dev_ptr, uint8_t ipc_handle[64]) {
+  if (!bytes || !dev_ptr) {
+    set_error("asap_arena_alloc: bytes must be > 0 and dev_ptr non-NULL");
+    return ASAP_EINVAL;
+  }
+  void* p = nullptr;
+  ASAP_CUDA(cudaMalloc(&p, bytes));
+  if (ipc_handle) {
+    cudaIpcMemHandle_t h;
+    cudaError_t err = cudaIpcGetMemHandle(&h, p);
+    if (err != cudaSuccess) {
+      cudaFree(p);
+      return cuda_fail(err, "cudaIpcGetMemHandle");
+    }
+    memcpy(ipc_handle, &h, 64);
+  }
+  *dev_ptr = (uint64_t)p;
+  return ASAP_OK;
+}
+
+int asap_arena_free(uint64_t dev_ptr) {
+  ASAP_CUDA(cudaFree((void*)dev_ptr));
+  return ASAP_OK;
+}
+
+int asap_arena_open(const uint8_t ipc_handle[64], uint64_t* dev_ptr) {
+  if (!ipc_handle || !dev_ptr) {
+    set_error("asap_arena_open: NULL argument");
+    return ASAP_EINVAL;
+  }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, 64);
+  void* p = nullptr;
+  ASAP_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *dev_ptr = (uint64_t)p;
+  return ASAP_OK;
+}
+
+int asap_arena_close(uint64_t dev_ptr) {
+  ASAP_CUDA(cudaIpcCloseMemHandle((void*)dev_ptr));
+  return ASAP_OK;
+}
+
+int asap_host_register(uint64_t host_ptr, uint64_t bytes, uint64_t* dev_ptr) {
+  if (!host_ptr || !bytes || !dev_ptr) {
+    set_error("asap_host_register: NULL pointer or zero size");
+    return ASAP_EINVAL;
+  }
+  ASAP_CUDA(cudaHostRegister((void*)host_ptr, bytes, cudaHostRegisterPortable | cudaHostRegisterMapped));
+  void* d = nullptr;
+  cudaError_t err = cudaHostGetDevicePointer(&d, (void*)host_ptr, 0);
+  if (err != cudaSuccess) {
+    cudaHostUnregister((void*)host_ptr);
+    return cuda_fail(err, "cudaHostGetDevicePointer");
+  }
+  *dev_ptr = (uint64_t)d;
+  return ASAP_OK;
+}
+
+int asap_host_unregister(uint64_t host_ptr) {
+  ASAP_CUDA(cudaHostUnregister((void*)host_ptr));
+  return ASAP_OK;
+}
+
+int asap_memset32(uint64_t dev_ptr, uint32_t value, uint64_t count, void* stream) {
+  if (!count) return ASAP_OK;
+  const int blocks = (int)std::min<uint64_t>((count + 255) / 256, 4096);
+  memset32_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((uint32_t*)dev_ptr, value, count);
+  ASAP_CHECK_LAUNCH("memset32_kernel");
+  return ASAP_OK;
+}
+
+int asap_write32(uint64_t dev_ptr, uint32_t value, void* stream) {
+  write32_kernel<<<1, 1, 0, (cudaStream_t)stream>>>((uint32_t*)dev_ptr, value);
+  ASAP_CHECK_LAUNCH("write32_kernel");
+  return ASAP_OK;
+}
+
+uint64_t asap_route_ws_bytes(const asap_geometry_t* g) {
+  if (!g || g->num_f < 1 || g->n_max < 1) return 0;
+  return kWsRows + (uint64_t)g->num_f * g->n_max * 4;
+}
+
+int asap_dispatch(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                  const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                  int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                  const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
+                  uint64_t status, uint64_t timeout_ns, void* stream) {
+  int rc = check_geometry(g);
+  if (rc) return rc;
+  if (g->num_f > ASAP_MAX_F || g->topk > 32) {
+    set_error("asap_dispatch: num_f=%d (max %d) / topk=%d (max 32) unsupported", g->num_f, ASAP_MAX_F, g->topk);
+    return ASAP_EINVAL;
+  }
+  if (a < 0 || a >= g->num_a || slot < 0 || slot >= g->slots || n < 1 || n > g->n_max) {
+    set_error("slot %d / n_tokens %d / A rank %d outside the geometry", slot, n, a);
+    return ASAP_EINVAL;
+  }
+  if ((uint32_t)layer_id > kMaxLayer) {
+    set_error("doorbell field out of range: layer_id=%d", layer_id);
+    return ASAP_EINVAL;
+  }
+  if (g->hidden % 8) {
+    set_error("asap_dispatch: hidden=%d must be a multiple of 8", g->hidden);
+    return ASAP_EINVAL;
+  }
+  if (!x || !ids || !w || !result || !route_ws || !recv || !bells || !epochs || !expert_bounds) {
+    set_error("asap_dispatch: NULL pointer argument");
+    return ASAP_EINVAL;
+  }
+  if ((x & 15) || (route_ws & 15)) {
+    set_error("asap_dispatch: x and route_ws must be 16-byte aligned");
+    return ASAP_EINVAL;
+  }
+  for (int f = 0; f < g->num_f; ++f) {
+    if (epochs[f] < 1 || (uint32_t)epochs[f] > kMaxEpoch) {
+      set_error("doorbell field out of range: epoch=%d (F rank %d)", epochs[f], f);
+      return ASAP_EINVAL;
+    }
+    if (expert_bounds[f + 1] < expert_bounds[f]) {
+      set_error("asap_dispatch: expert_bounds must be non-decreasing");
+      return ASAP_EINVAL;
+    }
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  Bounds bounds;
+  memset(&bounds, 0, sizeof(bounds));
+  for (int f = 0; f <= g->num_f; ++f) bounds.v[f] = expert_bounds[f];
+  dispatch_route_kernel<<<1, kRouteThreads, 0, st>>>(*g, slot, seq, (const void*)ids, ids_is_int64, n, bounds,
+                                                     (const uint8_t*)result, (uint8_t*)route_ws, backpressure,
+                                                     status, timeout_ns);
+  ASAP_CHECK_LAUNCH("dispatch_route_kernel");
+  PackArgs p;
+  memset(&p, 0, sizeof(p));
+  p.g = *g;
+  p.a = a;
+  p.slot = slot;
+  p.layer_id = layer_id;
+  p.n = n;
+  p.seq = seq;
+  p.ids_is_int64 = ids_is_int64;
+  p.w_is_bf16 = w_is_bf16;
+  p.x = (const uint8_t*)x;
+  p.ids = (const void*)ids;
+  p.w = (const void*)w;
+  p.ws = (const uint8_t*)route_ws;
+  for (int f = 0; f < g->num_f; ++f) {
+    p.recv[f] = (uint8_t*)recv[f];
+    p.bell[f] = (uint64_t*)bells[f];
+    p.epoch[f] = (uint32_t)epochs[f];
+  }
+  const int warps = 8;
+  int blocks = (n + warps - 1) / warps;
+  blocks = std::min(blocks, sm_count() * 4);
+  dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
+  ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
+  return ASAP_OK;
+}
+
+int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n, uint64_t result,
+                 uint64_t route_ws, uint64_t shared, uint64_t out, uint64_t status, uint64_t timeout_ns,
+                 void* stream) {
+  int rc = check_geometry(g);
+  if (rc) return rc;
+  if (g->num_f > ASAP_MAX_F || slot < 0 || slot >= g->slots || n < 1 || n > g->n_max) {
+    set_error("asap_combine: slot %d / n_tokens %d outside the geometry", slot, n);
+    return ASAP_EINVAL;
+  }
+  if (g->hidden % 8 || !result || !route_ws || !out || (out & 15) || (shared & 15)) {
+    set_error("asap_combine: hidden must be a multiple of 8 and out/shared 16-byte aligned, non-NULL");
+    return ASAP_EINVAL;
+  }
+  CombineArgs p;
+  p.g = *g;
+  p.slot = slot;
+  p.n = n;
+  p.seq = seq;
+  p.result = (const uint8_t*)result;
+  p.ws = (const uint8_t*)route_ws;
+  p.shared = (const __nv_bfloat16*)shared;
+  p.out = (__nv_bfloat16*)out;
+  p.status = status;
+  p.timeout_ns = timeout_ns;
+  wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns);
+  ASAP_CHECK_LAUNCH("wait_replies_kernel");
+  const int warps = 8;
+  int blocks = std::min((n + warps - 1) / warps, sm_count() * 4);
+  combine_kernel<<<blocks, warps * 32, 0, (cudaStream_t)stream>>>(p);
+  ASAP_CHECK_LAUNCH("combine_kernel");
+  return ASAP_OK;
+}
+
+int asap_wait_replies(const asap_geometry_t* g, int32_t slot, uint32_t seq, uint64_t result, uint64_t status,
+                      uint64_t timeout_ns, void* stream) {
+  int rc = check_geometry(g);
+  if (rc) return rc;
+  if (g->num_f > ASAP_MAX_F || slot < 0 || slot >= g->slots || !result) {
+    set_error("asap_wait_replies: slot %d outside the geometry or NULL result", slot);
+    return ASAP_EINVAL;
+  }
+  wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns);
+  ASAP_CHECK_LAUNCH("wait_replies_kernel");
+  return ASAP_OK;
+}
+
+}  // extern "C"

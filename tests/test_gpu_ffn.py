@@ -1,0 +1,155 @@
+"""F-rank expert chain (libasap asap_ffn_job) against the oracle, stage by stage: expert counts and the
+expert-major permutation bit-exact, MXFP8 activation codes and scales bit-exact, GEMM1 (SwiGLU + requant) and
+GEMM2 (top-k weighted) within relative L2 1e-2 of the oracle evaluated on the kernel's own quantised inputs, and
+the reply rows within relative L2 1e-2 of the reference semantics with the same activation quantisation."""
+
+import numpy as np
+import pytest
+import torch
+
+from asap_b200.experts import Mxfp4Experts
+from asap_b200.quant import mxfp4_quantize
+from gpu_util import FfnHarness, bf16_tensor_from_np, device_bytes, experts_to_oracle, np_from_bf16, random_inputs
+from oracle import moe, mx
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2  # relative L2
+
+
+def check_chain(h: FfnHarness, x, ids, w, gate, up, w2, e0, P, swiglu_limit=None):
+    n, k = ids.shape
+    H, I = h.e.hidden, h.e.inter
+    # counts and permutation: bit-exact
+    pos_ref, mstart_ref, counts_ref = moe.expert_permutation(ids, e0, P)
+    counts = device_bytes(h.ptrs["ecnt"], 4 * P).view(np.int32)
+    np.testing.assert_array_equal(counts, counts_ref)
+    pos = device_bytes(h.ptrs["pair_pos"], 4 * n * k).view(np.int32).reshape(n, k)
+    np.testing.assert_array_equal(pos, pos_ref)
+    rows = int(mstart_ref[-1]) * 128
+    tt, jj = np.nonzero(pos_ref >= 0)
+    prow = pos_ref[tt, jj]
+    # activation quantisation: bit-exact
+    xq = device_bytes(h.ptrs["xq"], rows * H).reshape(rows, H)
+    xsf = mx.sf_from_atoms(device_bytes(h.ptrs["xq_sf"], rows * H // 32), rows, H // 32)
+    q_ref, s_ref = mx.mx_quantize(x[tt])
+    np.testing.assert_array_equal(xq[prow], q_ref)
+    np.testing.assert_array_equal(xsf[prow], s_ref)
+    # GEMM1 + SwiGLU + requant, against the oracle on the same quantised activations
+    xa = mx.mx_dequantize(xq[prow], xsf[prow])
+    e_of = ids[tt, jj] - e0
+    g = np.zeros((len(prow), I), np.float32)
+    u = np.zeros((len(prow), I), np.float32)
+    for ex in range(P):  # per expert: never materialise weights per pair
+        sel = e_of == ex
+        if sel.any():
+            g[sel] = xa[sel] @ gate[ex].T
+            u[sel] = xa[sel] @ up[ex].T
+    if swiglu_limit:
+        g = np.minimum(g, swiglu_limit)
+        u = np.clip(u, -swiglu_limit, swiglu_limit)
+    h_ref = (moe.silu(g) * u).astype(np.float32)
+    hq = device_bytes(h.ptrs["hq"], rows * I).reshape(rows, I)
+    hsf = mx.sf_from_atoms(device_bytes(h.ptrs["hq_sf"], rows * I // 32), rows, I // 32)
+    h_gpu = mx.mx_dequantize(hq[prow], hsf[prow])
+    assert moe.rel_l2(h_gpu, h_ref) < TOL
+    # GEMM2 + top-k weight, on the kernel's own h
+    y_ref = np.zeros((len(prow), H), np.float32)
+    for ex in range(P):
+        sel = e_of == ex
+        if sel.any():
+            y_ref[sel] = h_gpu[sel] @ w2[ex].T
+    y_ref *= w[tt, jj][:, None]
+    y2 = device_bytes(h.ptrs["y2"], rows * H * 2).view(np.uint16).reshape(rows, H)
+    y_gpu = mx.bf16_from_bits(y2[prow])
+    assert moe.rel_l2(y_gpu, y_ref) < TOL
+    # reply rows: reference semantics with the same activation quantisation
+    out_ref = moe.ffn_rank(x, ids, w, gate, up, w2, e0, P, act_quant=True, swiglu_limit=swiglu_limit)
+    out = np_from_bf16(h.reply[:n])
+    assert moe.rel_l2(out, out_ref) < TOL
+    return out, out_ref
+
+
+@pytest.mark.parametrize("n,k,P,H,I,e0", [
+    (64, 2, 4, 256, 128, 4),       # one tile each way, non-zero expert base
+    (300, 4, 6, 512, 256, 0),      # several experts > 128 rows, two n-tiles in GEMM1/GEMM2
+])
+def test_ffn_chain_random_weights(cuda_ok, n, k, P, H, I, e0):
+    rng = np.random.default_rng(n)
+    e = Mxfp4Experts.random(P, H, I, expert_base=e0, seed=n)
+    gate, up, w2 = experts_to_oracle(e)
+    x, ids, w = random_inputs(rng, n, H, k, e0 - 2, e0 + P + 2, bias_expert=e0)  # some ids are not local
+    h = FfnHarness(e, n_max=n, topk=k)
+    h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), seq=41)
+    check_chain(h, x, ids, w, gate, up, w2, e0, P)
+    assert int(h.done[0].item()) == 41
+    h.release()
+    e.release()
+
+
+def test_ffn_chain_config1_weights(cuda_ok):
+    """BASELINE config 1's F rank 1 (experts 8..15 of 16, H=1024, I=512, top-2 softmax, T=512): fp32 weights
+    N(0, 0.02) quantised to MXFP4 on the host, through the logical -> device layout packer."""
+    rng = np.random.default_rng(0)
+    T, H, I, E, k = 512, 1024, 512, 16, 2
+    e0, P = 8, 8
+    w13 = rng.standard_normal((P, 2 * I, H)).astype(np.float32) * 0.02
+    w2f = rng.standard_normal((P, H, I)).astype(np.float32) * 0.02
+    c13, s13 = mxfp4_quantize(w13)
+    c2, s2 = mxfp4_quantize(w2f)
+    e = Mxfp4Experts.from_logical(c13, s13, c2, s2, expert_base=e0)
+    deq13 = mx.e2m1_decode(c13).reshape(P, 2 * I, H // 32, 32) * mx.e8m0_value(s13)[..., None]
+    deq13 = deq13.reshape(P, 2 * I, H)
+    gate, up = deq13[:, :I], deq13[:, I:]
+    w2 = (mx.e2m1_decode(c2).reshape(P, H, I // 32, 32) * mx.e8m0_value(s2)[..., None]).reshape(P, H, I)
+    x = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    ids, w = moe.topk_routing(rng.standard_normal((T, E)), k, "softmax")
+    h = FfnHarness(e, n_max=T, topk=k)
+    h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+    out, out_ref = check_chain(h, x, ids, w, gate, up, w2, e0, P)
+    # against the bf16 result of the same dequantised weights without activation quantisation (reported bound)
+    plain = moe.ffn_rank(x, ids, w, gate, up, w2, e0, P, act_quant=False)
+    assert moe.rel_l2(out, plain) < 8e-2
+    h.release()
+    e.release()
+
+
+def test_ffn_chain_swiglu_limit(cuda_ok):
+    rng = np.random.default_rng(3)
+    n, k, P, H, I = 128, 2, 4, 256, 128
+    e = Mxfp4Experts.random(P, H, I, seed=3, scale_lo=121, scale_hi=123)  # large activations: the clamp bites
+    gate, up, w2 = experts_to_oracle(e)
+    x, ids, w = random_inputs(rng, n, H, k, 0, P)
+    h = FfnHarness(e, n_max=n, topk=k)
+    h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), swiglu_limit=2.0)
+    check_chain(h, x, ids, w, gate, up, w2, 0, P, swiglu_limit=2.0)
+    h.release()
+    e.release()
+
+
+def test_ffn_chain_no_local_pair(cuda_ok):
+    """A padding row (ids -1, what dispatch sends an F rank that got no token): the reply row is exactly 0."""
+    e = Mxfp4Experts.random(4, 256, 128, seed=9)
+    h = FfnHarness(e, n_max=4, topk=2)
+    h.reply.fill_(1.0)
+    x = torch.randn(1, 256, device="cuda").to(torch.bfloat16)
+    ids = torch.full((1, 2), -1, dtype=torch.int32, device="cuda")
+    w = torch.zeros(1, 2, device="cuda")
+    h.run(x, ids, w, seq=5)
+    assert torch.count_nonzero(h.reply[0]).item() == 0
+    assert int(h.done[0].item()) == 5
+    h.release()
+    e.release()
+
+
+def test_ffn_chain_deepseek_dims(cuda_ok):
+    """DeepSeek-V3 expert shape (H=7168, I=2048: 56 K-tiles in GEMM1, 16 N-tiles / 28 N-tiles) on 8 experts."""
+    rng = np.random.default_rng(11)
+    n, k, P, H, I = 256, 8, 8, 7168, 2048
+    e = Mxfp4Experts.random(P, H, I, seed=11, scale_lo=117, scale_hi=120)
+    gate, up, w2 = experts_to_oracle(e)
+    x, ids, w = random_inputs(rng, n, H, k, 0, 12)  # 8 of 12 experts local
+    h = FfnHarness(e, n_max=n, topk=k)
+    h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+    check_chain(h, x, ids, w, gate, up, w2, 0, P)
+    h.release()
+    e.release()

@@ -1,0 +1,153 @@
+"""The whole A->F->A round trip on one GPU (one A rank and one F rank, loopback arenas), through the
+reference-facing API (AsapMoE.forward / AsapDispatcher.dispatch + combine / AsapBuffer), against the oracle:
+relative L2 <= 1e-2 of the reference semantics with the same MXFP8 activation quantisation; the F rank's
+region bytes, the doorbell word in its host page and the per-F-rank token table bit-exact."""
+
+import numpy as np
+import pytest
+import torch
+
+from asap_b200.dispatcher import AsapDispatcher
+from asap_b200.experts import Mxfp4Experts
+from asap_b200.layer import AsapMoE
+from asap_b200.loopback import Loopback
+from asap_b200.quant import mxfp4_quantize
+from asap_b200.sglang_shim import StandardTopKOutput
+from asap_b200.transport.layout import Geometry, pack_doorbell
+from gpu_util import bf16_tensor_from_np, experts_to_oracle, np_from_bf16
+from oracle import moe, mx
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def config1_experts(rng, E=16, H=1024, I=512):
+    w13 = rng.standard_normal((E, 2 * I, H)).astype(np.float32) * 0.02
+    w2 = rng.standard_normal((E, H, I)).astype(np.float32) * 0.02
+    c13, s13 = mxfp4_quantize(w13)
+    c2, s2 = mxfp4_quantize(w2)
+    return Mxfp4Experts.from_logical(c13, s13, c2, s2)
+
+
+@pytest.fixture(scope="module")
+def pair(cuda_ok):
+    rng = np.random.default_rng(0)
+    experts = {0: config1_experts(rng), 5: config1_experts(rng)}
+    lb = Loopback(Geometry(1, 1, 2, 512, 1024, 2, 1), experts, timeout_s=5.0)
+    lb.install()
+    oracle_w = {lid: experts_to_oracle(e) for lid, e in experts.items()}
+    yield lb, oracle_w
+    lb.close()
+    for e in experts.values():
+        e.release()
+
+
+def run_layer(lb, layer_id, x, ids, w, shared=None, micro_batch=None):
+    disp = AsapDispatcher(layer_id)
+    topk = StandardTopKOutput(torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda())
+    out = disp.dispatch(bf16_tensor_from_np(x), topk, micro_batch=micro_batch)
+    res = disp.combine(out, shared=None if shared is None else bf16_tensor_from_np(shared))
+    torch.cuda.synchronize()
+    lb.check()
+    return np_from_bf16(res)
+
+
+def test_config1_round_trip(pair):
+    """BASELINE config 1 (T=512, H=1024, 16 experts, top-2 softmax, I=512), plus a bf16 shared expert output."""
+    lb, ow = pair
+    rng = np.random.default_rng(1)
+    T = 512
+    x = mx.bf16_round(rng.standard_normal((T, 1024)).astype(np.float32))
+    ids, w = moe.topk_routing(rng.standard_normal((T, 16)), 2, "softmax")
+    shared = mx.bf16_round(rng.standard_normal((T, 1024)).astype(np.float32) * 0.1)
+    got = run_layer(lb, 0, x, ids, w, shared)
+    ref = moe.round_trip(x, ids, w, [0, 16], [ow[0]], shared=shared)
+    assert moe.rel_l2(got, ref) < TOL
+    plain = moe.round_trip(x, ids, w, [0, 16], [ow[0]], shared=shared, act_quant=False)
+    assert moe.rel_l2(got, plain) < 8e-2
+    # wire bytes of the message: region rows, doorbell word, routing table
+    g = lb.g
+    seq = lb.channel._seq[0]
+    reg = torch.as_tensor(lb.sched.recv_arena[g.region_off(0, 0): g.region_off(0, 1)]).cpu().numpy()
+    np.testing.assert_array_equal(reg[: T * 1024 * 2].view(np.uint16).reshape(T, 1024), mx.bf16_bits(x))
+    np.testing.assert_array_equal(reg[g.ids_off: g.ids_off + T * 2 * 4].view(np.int32).reshape(T, 2), ids)
+    word = int(lb.server._bells[0])
+    assert word == pack_doorbell(seq, T, 0, lb.channel._epoch[0])
+    row_of = lb.channel.route_ws(0)[512: 512 + 4 * T].view(torch.int32).cpu().numpy()
+    np.testing.assert_array_equal(row_of, np.arange(T))
+
+
+def test_asap_moe_forward_layers_and_slots(pair):
+    """AsapMoE.forward on two layers (different weights) and both slots, many messages (seq advances,
+    backpressure on each slot is satisfied by the previous answer)."""
+    lb, ow = pair
+    rng = np.random.default_rng(2)
+    for it in range(6):
+        layer = (0, 5)[it % 2]
+        T = int(rng.integers(1, 513))
+        x = mx.bf16_round(rng.standard_normal((T, 1024)).astype(np.float32))
+        ids, w = moe.topk_routing(rng.standard_normal((T, 16)), 2, "softmax")
+        if it % 3 == 0:
+            moe_layer = AsapMoE(16, 1024, 512, layer, top_k=2)
+            topk = StandardTopKOutput(torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda())
+            got = np_from_bf16(moe_layer(bf16_tensor_from_np(x), topk))
+            torch.cuda.synchronize()
+            lb.check()
+        else:
+            got = run_layer(lb, layer, x, ids, w, micro_batch=it % 2)
+        ref = moe.round_trip(x, ids, w, [0, 16], [ow[layer]])
+        assert moe.rel_l2(got, ref) < TOL, (it, T)
+
+
+def test_tokens_routed_nowhere_and_empty_batch(pair):
+    lb, ow = pair
+    rng = np.random.default_rng(3)
+    T = 64
+    x = mx.bf16_round(rng.standard_normal((T, 1024)).astype(np.float32))
+    ids = np.full((T, 2), -1, np.int32)
+    w = np.zeros((T, 2), np.float32)
+    shared = mx.bf16_round(rng.standard_normal((T, 1024)).astype(np.float32))
+    got = run_layer(lb, 0, x, ids, w, shared)
+    np.testing.assert_array_equal(got, shared)  # F got one padding row; every token's routed output is 0
+    ids[::2, 0] = 3  # half the tokens routed
+    w[::2, 0] = 1.0
+    got = run_layer(lb, 0, x, ids, w)
+    ref = moe.round_trip(x, ids, w, [0, 16], [ow[0]])
+    assert moe.rel_l2(got, ref) < TOL
+    assert not got[1::2].any()
+    # an empty batch never reaches the transport
+    disp = AsapDispatcher(0)
+    empty = torch.empty(0, 1024, dtype=torch.bfloat16, device="cuda")
+    topk = StandardTopKOutput(torch.empty(0, 2, device="cuda"), torch.empty(0, 2, dtype=torch.int32, device="cuda"))
+    assert disp.combine(disp.dispatch(empty, topk)).shape == (0, 1024)
+
+
+def test_exchange_splits_batches_larger_than_n_max(pair):
+    lb, ow = pair
+    rng = np.random.default_rng(4)
+    T = 1100  # > n_max = 512: three pieces
+    x = mx.bf16_round(rng.standard_normal((T, 1024)).astype(np.float32))
+    ids, w = moe.topk_routing(rng.standard_normal((T, 16)), 2, "softmax")
+    got = run_layer(lb, 5, x, ids, w)
+    ref = moe.round_trip(x, ids, w, [0, 16], [ow[5]])
+    assert moe.rel_l2(got, ref) < TOL
+
+
+def test_deepseek_v3_layer_shape(cuda_ok):
+    """A DeepSeek-V3-shape layer (H=7168, I=2048, top-8 sigmoid) on 16 routed experts, 192 tokens."""
+    rng = np.random.default_rng(5)
+    E, H, I, T, k = 16, 7168, 2048, 192, 8
+    e = Mxfp4Experts.random(E, H, I, seed=5, scale_lo=117, scale_hi=120)
+    lb = Loopback(Geometry(1, 1, 1, 256, H, k, 1), {0: e}, timeout_s=5.0)
+    lb.install()
+    try:
+        gate, up, w2 = experts_to_oracle(e)
+        x = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        ids, w = moe.topk_routing(rng.standard_normal((T, E)), k, "sigmoid")
+        shared = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        got = run_layer(lb, 0, x, ids, w, shared)
+        ref = moe.round_trip(x, ids, w, [0, E], [(gate, up, w2)], shared=shared)
+        assert moe.rel_l2(got, ref) < TOL
+    finally:
+        lb.close()
+        e.release()
