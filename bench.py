@@ -57,7 +57,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                          "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -206,29 +206,32 @@ def run_single(args):
     lb.check()
 
     # e2e: the public API (AsapMoE.forward) on pinned host buffers, copies inside the timed region
-    moe = AsapMoE(E, H, I, 0, top_k=K_TOP)
-    hx, hids, hw = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
-    hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    e2e = None
+    if not args.no_e2e:
+        moe = AsapMoE(E, H, I, 0, top_k=K_TOP)
+        hx, hids, hw = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
+        hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
 
-    def e2e_step():
-        dx = hx.to(dev, non_blocking=True)
-        di = hids.to(dev, non_blocking=True)
-        dw = hw.to(dev, non_blocking=True)
-        out = moe(dx, StandardTopKOutput(dw, di))
-        hout.copy_(out, non_blocking=True)
+        def e2e_step():
+            dx = hx.to(dev, non_blocking=True)
+            di = hids.to(dev, non_blocking=True)
+            dw = hw.to(dev, non_blocking=True)
+            out = moe(dx, StandardTopKOutput(dw, di))
+            hout.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    t0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    t1.record(stream)
-    torch.cuda.synchronize()
-    lb.check()
-    e2e_ms = t0.elapsed_time(t1) / args.steps
-    h2d = hx.numel() * 2 + hids.numel() * 4 + hw.numel() * 4
-    d2h = hout.numel() * 2
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        lb.check()
+        e2e_ms = t0.elapsed_time(t1) / args.steps
+        e2e = {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": hx.numel() * 2 + hids.numel() * 4 + hw.numel() * 4,
+               "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(e2e_ms, 4)}
 
     peaks, peak_kind = load_peaks()
     g1_flops, g2_flops = gemm_flops(pairs)
@@ -242,13 +245,12 @@ def run_single(args):
         "metric": METRIC, "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport", "data": "synthetic",
-        "config": {"workload": "1 GPU loopback A+F: config 2 layer (T=16384, H=7168, 256 experts, top-8 sigmoid, "
+        "config": {"workload": f"1 GPU loopback A+F: config 2 layer (T={T}, H=7168, {E} experts, top-8 sigmoid, "
                                "I=2048, MXFP4 weights, 1 bf16 shared expert)", "tokens_per_replica": T,
                    "a_replicas": 1, "f_ranks": 1, "parallelism": "1A1F loopback",
                    "l2": "inputs larger than L2 (x 235 MB, weights 6.0 GB), no flush"},
-        "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps * 9,
+        "e2e": e2e,
+        "gpu_launches": args.steps * 10,
         "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / fp8_peak, 4), "traffic": traffic,
@@ -471,15 +473,19 @@ def run_multi(args):
 
 
 def main():
+    global E
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--tokens", type=int, default=T_DEFAULT)
+    ap.add_argument("--experts", type=int, default=E, help="routed experts (small profiling cases)")
     ap.add_argument("--cpu-experts", type=int, default=4)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
+    E = args.experts
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

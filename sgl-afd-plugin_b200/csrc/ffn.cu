@@ -7,7 +7,7 @@
 //   srt/managers/scheduler.py:387-450 run_job / rows_of        -> asap_ffn_job (launch chain, arena views)
 //   SGLang FusedMoE -> FlashInfer trtllm_fp4_block_scale_routed_moe (scheduler.py:410-412;
 //   srt/layers/quantization/mxfp4_flashinfer_trtllm_moe.py:68-99)
-//                                                              -> route_local / quant_permute / moe_gemm<0,1> /
+//                                                              -> route_count/scan/place, quant_permute, moe_gemm<0,1>,
 //                                                                 finalize_reply kernels
 //   transport/server.py:340-350     FfnServer.reply            -> finalize_reply epilogue (P2P rows + done flag)
 #include <cuda.h>
@@ -32,10 +32,12 @@ struct JobDesc {
 };
 static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
 
+constexpr int kPermChunks = 128;  // chunks of pairs the permutation is split into (upper bound)
+
 struct WsLayout {
   int32_t n_max, topk, P, H, I;
   int64_t m_cap;  // rows of the expert-major activation buffers (multiple of 128)
-  uint64_t desc, ecnt, mstart, pair_pos, row_tok, row_w, xq, xq_sf, hq, hq_sf, y2, total;
+  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, xq, xq_sf, hq, hq_sf, y2, total;
 };
 
 static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
@@ -55,6 +57,7 @@ static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
   L.desc = take(sizeof(JobDesc));
   L.ecnt = take(4ull * ASAP_MAX_LOCAL_EXPERTS);
   L.mstart = take(4ull * (ASAP_MAX_LOCAL_EXPERTS + 1));
+  L.hist = take(4ull * kPermChunks * ASAP_MAX_LOCAL_EXPERTS);
   L.pair_pos = take(4ull * n_max * topk);
   L.row_tok = take(4ull * L.m_cap);
   L.row_w = take(4ull * L.m_cap);
@@ -122,10 +125,9 @@ __global__ void ffn_post_kernel(JobDesc* d, uint32_t seq, int32_t n, int32_t lay
 }
 
 // ------------------------------------------------------------------ K3b-1: expert-major permutation
-// Stable counting sort of the (token, slot) pairs whose expert is local, by (expert, token, slot).
-// Each expert's rows start on a 128-row boundary (one GEMM M tile never mixes experts).
-constexpr int kPermThreads = 1024;
-constexpr int kPermWarps = kPermThreads / 32;
+// Stable counting sort of the (token, slot) pairs whose expert is local, by (expert, token, slot), over many
+// CTAs: count (per-chunk histograms) -> scan (tile-aligned expert bases, per-chunk bases) -> place.  Each
+// expert's rows start on a 128-row boundary (one GEMM M tile never mixes experts).
 
 struct PermArgs {
   const JobDesc* desc;
@@ -137,88 +139,103 @@ struct PermArgs {
   int32_t* pair_pos;  // [n, topk]
   int32_t* row_tok;   // [m_cap]
   float* row_w;       // [m_cap]
+  int32_t* hist;      // [kPermChunks][ASAP_MAX_LOCAL_EXPERTS] chunk histograms, then chunk bases
 };
 
-__global__ void __launch_bounds__(kPermThreads, 1) route_local_kernel(const __grid_constant__ PermArgs p) {
-  __shared__ int32_t hist[kPermWarps][ASAP_MAX_LOCAL_EXPERTS];
-  __shared__ int32_t s_mstart[ASAP_MAX_LOCAL_EXPERTS + 1];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int P = p.P;
+__device__ __forceinline__ void perm_chunking(const PermArgs& p, int64_t& total, int64_t& chunk, int& chunks) {
   const int n = p.desc->valid ? p.desc->n : 0;
-  for (int i = tid; i < kPermWarps * ASAP_MAX_LOCAL_EXPERTS; i += kPermThreads) (&hist[0][0])[i] = 0;
+  total = (int64_t)n * p.topk;
+  chunk = ((total + kPermChunks - 1) / kPermChunks + 31) / 32 * 32;
+  if (chunk < 32) chunk = 32;
+  chunks = (int)((total + chunk - 1) / chunk);
+}
+
+__global__ void __launch_bounds__(256) route_count_kernel(const __grid_constant__ PermArgs p) {
+  __shared__ int32_t h[ASAP_MAX_LOCAL_EXPERTS];
+  int64_t total, chunk;
+  int chunks;
+  perm_chunking(p, total, chunk, chunks);
+  if ((int)blockIdx.x >= chunks) return;
+  for (int i = threadIdx.x; i < p.P; i += blockDim.x) h[i] = 0;
   __syncthreads();
-  const int64_t total = (int64_t)n * p.topk;
-  const int64_t chunk = ((total + kPermWarps - 1) / kPermWarps + 31) / 32 * 32;
-  const int64_t q0 = min(total, (int64_t)warp * chunk), q1 = min(total, q0 + chunk);
-  // pass 1: per-warp histograms
-  for (int64_t q = q0 + lane; q < q1; q += 32) {
+  const int64_t q0 = blockIdx.x * chunk, q1 = min(total, q0 + chunk);
+  for (int64_t q = q0 + threadIdx.x; q < q1; q += blockDim.x) {
     const int e = p.ids[q] - p.expert_base;
-    if (e >= 0 && e < P) atomicAdd(&hist[warp][e], 1);
+    if (e >= 0 && e < p.P) atomicAdd(&h[e], 1);
   }
   __syncthreads();
-  // expert totals, 128-row tile counts, and per-warp bases
-  if (tid < P) {
-    int32_t c = 0;
-    for (int w = 0; w < kPermWarps; ++w) c += hist[w][tid];
-    p.ecnt[tid] = c;
-    s_mstart[tid] = (c + 127) / 128;
+  for (int i = threadIdx.x; i < p.P; i += blockDim.x) p.hist[(int64_t)blockIdx.x * ASAP_MAX_LOCAL_EXPERTS + i] = h[i];
+}
+
+__global__ void __launch_bounds__(ASAP_MAX_LOCAL_EXPERTS) route_scan_kernel(const __grid_constant__ PermArgs p) {
+  __shared__ int32_t wsum[ASAP_MAX_LOCAL_EXPERTS / 32];
+  int64_t total, chunk;
+  int chunks;
+  perm_chunking(p, total, chunk, chunks);
+  const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+  int32_t c = 0;
+  if (e < p.P) {
+#pragma unroll 8
+    for (int g = 0; g < chunks; ++g) c += p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + e];
   }
-  __syncthreads();
-  if (warp == 0) {  // exclusive scan of tile counts, 8 experts per lane
-    int32_t v[8], sum = 0;
+  const int32_t tiles = (e < p.P) ? (c + 127) / 128 : 0;
+  int32_t v = tiles;  // block exclusive scan of tiles over experts
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane * 8 + i;
-      v[i] = (e < P) ? s_mstart[e] : 0;
-      sum += v[i];
-    }
-    int32_t incl = sum;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int32_t u = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += u;
-    }
-    int32_t run = incl - sum;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane * 8 + i;
-      if (e < P) s_mstart[e] = run;
-      run += v[i];
-    }
-    if (lane == 31) s_mstart[P] = incl;
+  for (int d = 1; d < 32; d <<= 1) {
+    const int32_t u = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += u;
   }
+  if (lane == 31) wsum[warp] = v;
   __syncthreads();
-  if (tid <= P) p.mstart[tid] = s_mstart[tid];
-  if (tid < P) {  // hist[w][e] becomes the first permuted row of warp w's pairs of expert e
-    int32_t base = s_mstart[tid] * 128;
-    for (int w = 0; w < kPermWarps; ++w) {
-      const int32_t c = hist[w][tid];
-      hist[w][tid] = base;
-      base += c;
+  int32_t before = 0;
+  for (int w = 0; w < warp; ++w) before += wsum[w];
+  const int32_t mst = before + v - tiles;
+  if (e < p.P) {
+    p.ecnt[e] = c;
+    p.mstart[e] = mst;
+    int32_t base = mst * 128;
+    for (int g0 = 0; g0 < chunks; g0 += 8) {  // chunk bases, in place; 8 loads in flight
+      int32_t t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = (g0 + i < chunks) ? p.hist[(int64_t)(g0 + i) * ASAP_MAX_LOCAL_EXPERTS + e] : 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (g0 + i < chunks) p.hist[(int64_t)(g0 + i) * ASAP_MAX_LOCAL_EXPERTS + e] = base;
+        base += t[i];
+      }
     }
-    // padding rows of this expert: no token
-    const int32_t end = s_mstart[tid + 1] * 128;
-    for (int32_t r = base; r < end; ++r) {
+    for (int32_t r = base; r < (mst + tiles) * 128; ++r) {  // padding rows: no token
       p.row_tok[r] = -1;
       p.row_w[r] = 0.f;
     }
   }
-  __syncthreads();
-  // pass 2: stable placement (pairs in ascending (token, slot) order within each warp's range)
+  if (e == p.P - 1) p.mstart[p.P] = mst + tiles;
+}
+
+__global__ void __launch_bounds__(32) route_place_kernel(const __grid_constant__ PermArgs p) {
+  __shared__ int32_t off[ASAP_MAX_LOCAL_EXPERTS];
+  int64_t total, chunk;
+  int chunks;
+  perm_chunking(p, total, chunk, chunks);
+  if ((int)blockIdx.x >= chunks) return;
+  const int lane = threadIdx.x;
+  for (int i = lane; i < p.P; i += 32) off[i] = p.hist[(int64_t)blockIdx.x * ASAP_MAX_LOCAL_EXPERTS + i];
+  __syncwarp();
   const uint32_t lt_mask = (1u << lane) - 1u;
+  const int64_t q0 = blockIdx.x * chunk, q1 = min(total, q0 + chunk);
   for (int64_t qb = q0; qb < q1; qb += 32) {
     const int64_t q = qb + lane;
     int e = -1;
     if (q < q1) {
       e = p.ids[q] - p.expert_base;
-      if (e < 0 || e >= P) e = -1;
+      if (e < 0 || e >= p.P) e = -1;
     }
     const uint32_t active = __ballot_sync(0xffffffffu, e >= 0);
     const uint32_t peers = __match_any_sync(0xffffffffu, e) & active;
     int32_t pos = -1;
-    if (e >= 0) pos = hist[warp][e] + __popc(peers & lt_mask);
+    if (e >= 0) pos = off[e] + __popc(peers & lt_mask);
     __syncwarp();
-    if (e >= 0 && (peers & lt_mask) == 0) hist[warp][e] += __popc(peers);
+    if (e >= 0 && (peers & lt_mask) == 0) off[e] += __popc(peers);
     __syncwarp();
     if (q < q1) {
       p.pair_pos[q] = pos;
@@ -419,6 +436,22 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
+      // L2 prefetch runs PF k-tiles ahead of the loads (into the next tile at the end of one), so the TMA loads
+      // that feed the 4-stage ring mostly hit L2.
+      constexpr int PF = 8;
+      int pf_tile = blockIdx.x, pf_kt = 0;
+      auto prefetch_next = [&]() {
+        if (pf_tile >= num_tiles) return;
+        int pe, pm, pn;
+        decode_tile(s_mstart, P, NT, pf_tile, pe, pm, pn);
+        tma_prefetch_2d(&p.tmap_a, pf_kt * BK, pm * BM);
+        tma_prefetch_2d(&p.tmap_b, pf_kt * BK, pe * p.N + pn * BN);
+        if (++pf_kt == KT) {
+          pf_kt = 0;
+          pf_tile += gridDim.x;
+        }
+      };
+      for (int i = 0; i < PF; ++i) prefetch_next();
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int e, m_blk, n_t;
         decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
@@ -437,6 +470,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
           tma_load_2d(sB + stage * B_BYTES, &p.tmap_b, kt * BK, b_row, &full[stage]);
           bulk_load(sSFA + stage * SFA_BYTES, sfa + (uint64_t)kt * SFA_BYTES, SFA_BYTES, &full[stage]);
           bulk_load(sSFB + stage * SFB_BYTES, sfb + (uint64_t)kt * sfb_kstride, SFB_BYTES, &full[stage]);
+          prefetch_next();
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -514,30 +548,38 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int e, m_blk, n_t;
       decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
-      if (!mbar_wait(acc_full, acc_phase, deadline, abort_flag)) break;
-      tc_fence_after();
       const int64_t row = (int64_t)m_blk * BM + row_in_tile;
       const bool valid = p.row_tok[row] >= 0;
+      if (!mbar_wait(acc_full, acc_phase, deadline, abort_flag)) break;
+      tc_fence_after();
+      // Drain this warp's slice of the accumulator into registers and hand TMEM back at once: the MMA warp
+      // starts the next tile while this warp does the epilogue math and stores.
+      uint32_t v[4][32];
+      if constexpr (EPI == 0) {  // gate cols [64h, 64h+64) and the matching up cols 128 further
+        tmem_ld_32x32b_x32(t_lane + TMEM_ACC + half * 64, v[0]);
+        tmem_ld_32x32b_x32(t_lane + TMEM_ACC + half * 64 + 32, v[1]);
+        tmem_ld_32x32b_x32(t_lane + TMEM_ACC + 128 + half * 64, v[2]);
+        tmem_ld_32x32b_x32(t_lane + TMEM_ACC + 128 + half * 64 + 32, v[3]);
+      } else {  // output cols [128h, 128h+128)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_lane + TMEM_ACC + half * 128 + c * 32, v[c]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      acc_phase ^= 1u;
+      if (!valid) continue;
       if constexpr (EPI == 0) {
         const int I = p.N / 2;
         const int kblocks = I / 32;
         const float lim = p.swiglu_limit;
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < 2; ++c) {
-          const int col = half * 64 + c * 32;
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(t_lane + TMEM_ACC + col, g);
-          tmem_ld_32x32b_x32(t_lane + TMEM_ACC + 128 + col, u);
-          tmem_wait_ld();
-          if (c == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
-          }
           float h[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+            float gv = __uint_as_float(v[c][i]), uv = __uint_as_float(v[2 + c][i]);
             if (lim > 0.f) {
               gv = fminf(gv, lim);
               uv = fminf(fmaxf(uv, -lim), lim);
@@ -546,44 +588,30 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
           }
           uint4 lo, hi;
           const uint32_t sb = mx_quant32(h, lo, hi);
-          if (valid) {
-            const int hcol = n_t * 128 + col;
-            uint4* dst = reinterpret_cast<uint4*>(p.out_q + row * I + hcol);
-            dst[0] = lo;
-            dst[1] = hi;
-            p.out_sf[sf_atom_off(row, hcol / 32, kblocks)] = (uint8_t)sb;
-          }
+          const int hcol = n_t * 128 + half * 64 + c * 32;
+          uint4* dst = reinterpret_cast<uint4*>(p.out_q + row * I + hcol);
+          dst[0] = lo;
+          dst[1] = hi;
+          p.out_sf[sf_atom_off(row, hcol / 32, kblocks)] = (uint8_t)sb;
         }
       } else {
         const float wr = p.row_w[row];
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          const int col = half * 128 + c * 32;
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_lane + TMEM_ACC + col, v);
-          tmem_wait_ld();
-          if (c == 3) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
-          }
-          if (valid) {
-            uint32_t o[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const __nv_bfloat162 b2 =
-                  __floats2bfloat162_rn(__uint_as_float(v[2 * i]) * wr, __uint_as_float(v[2 * i + 1]) * wr);
-              o[i] = *reinterpret_cast<const uint32_t*>(&b2);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(p.out_bf + row * p.N + (int64_t)n_t * BN + col);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-            dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
-            dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const __nv_bfloat162 b2 =
+                __floats2bfloat162_rn(__uint_as_float(v[c][2 * i]) * wr, __uint_as_float(v[c][2 * i + 1]) * wr);
+            o[i] = *reinterpret_cast<const uint32_t*>(&b2);
           }
+          uint4* dst = reinterpret_cast<uint4*>(p.out_bf + row * p.N + (int64_t)n_t * BN + half * 128 + c * 32);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+          dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
         }
       }
-      acc_phase ^= 1u;
     }
   }
   tc_fence_before();
@@ -695,7 +723,7 @@ struct ExpertsHandle {
   asap_mxfp4_experts_t e;
   CUtensorMap w13_map, w2_map;
 };
-constexpr int kTimedKernels = 5;  // route_local, quant_permute, gemm1, gemm2, finalize_reply
+constexpr int kTimedKernels = 5;  // routing (count+scan+place), quant_permute, gemm1, gemm2, finalize_reply
 constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
 struct WsHandle {
   uint8_t* base;
@@ -892,7 +920,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   JobDesc* desc = (JobDesc*)(B + L.desc);
   const int sms = sm_count();
 
-  PermArgs pa;
+  PermArgs pa{};
   pa.desc = desc;
   pa.ids = (const int32_t*)ids;
   pa.w = (const float*)w;
@@ -904,17 +932,27 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   pa.pair_pos = (int32_t*)(B + L.pair_pos);
   pa.row_tok = (int32_t*)(B + L.row_tok);
   pa.row_w = (float*)(B + L.row_w);
+  pa.hist = (int32_t*)(B + L.hist);
   const int slot_ev = wh->jobs % kTimedJobs;
   if (wh->timing) ++wh->jobs;
   auto mark = [&](int i) {
     if (wh->timing) cudaEventRecord(wh->ev[slot_ev][i], st);
   };
   mark(0);
-  route_local_kernel<<<1, kPermThreads, 0, st>>>(pa);
-  ASAP_CHECK_LAUNCH("route_local_kernel");
+  if (!pa.desc || !pa.ids || !pa.w || !pa.ecnt || !pa.mstart || !pa.pair_pos || !pa.row_tok || !pa.row_w ||
+      !pa.hist) {
+    set_error("asap_ffn_job: internal error, a permutation buffer is unset");
+    return ASAP_EINVAL;
+  }
+  route_count_kernel<<<kPermChunks, 256, 0, st>>>(pa);
+  ASAP_CHECK_LAUNCH("route_count_kernel");
+  route_scan_kernel<<<1, ASAP_MAX_LOCAL_EXPERTS, 0, st>>>(pa);
+  ASAP_CHECK_LAUNCH("route_scan_kernel");
+  route_place_kernel<<<kPermChunks, 32, 0, st>>>(pa);
+  ASAP_CHECK_LAUNCH("route_place_kernel");
   mark(1);
 
-  QuantArgs qa;
+  QuantArgs qa{};
   qa.desc = desc;
   qa.mstart = pa.mstart;
   qa.P = L.P;
@@ -965,7 +1003,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
   mark(4);
 
-  FinalArgs fa;
+  FinalArgs fa{};
   fa.desc = desc;
   fa.topk = L.topk;
   fa.H = L.H;

@@ -59,7 +59,7 @@ static int check_geometry(const asap_geometry_t* g) {
 constexpr uint64_t kWsCount = 0, kWsPad = 256, kWsSync = 320, kWsRows = 512;
 
 // K1: one CTA. Backpressure wait, then the per-F-rank compacted row index of every token (ascending token
-// order, a stable compaction), via a block-wide exclusive scan per F rank.
+// order, a stable compaction).
 constexpr int kRouteThreads = 1024;
 
 struct Bounds {
@@ -71,7 +71,6 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
     const __grid_constant__ Bounds bounds_g, const uint8_t* result, uint8_t* ws, int32_t backpressure,
     uint64_t status, uint64_t timeout_ns) {
   __shared__ int32_t bounds[ASAP_MAX_F + 1];
-  __shared__ int32_t warp_tot[ASAP_MAX_F][32];
   __shared__ int32_t abort_flag;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int F = g.num_f;
@@ -102,77 +101,62 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
     return;
   }
 
-  // Each thread owns a contiguous run of tokens; masks fit 16 F ranks.
-  const int per = (n + kRouteThreads - 1) / kRouteThreads;
-  const int t0 = min(n, tid * per), t1 = min(n, t0 + per);
-  int32_t mycnt[ASAP_MAX_F];
-#pragma unroll
-  for (int f = 0; f < ASAP_MAX_F; ++f) mycnt[f] = 0;
-  const int64_t e_end = bounds[F];
-  for (int t = t0; t < t1; ++t) {
-    uint32_t mask = 0;
-    for (int j = 0; j < g.topk; ++j) {
-      int64_t e = ids_is_int64 ? reinterpret_cast<const int64_t*>(ids)[(int64_t)t * g.topk + j]
-                               : reinterpret_cast<const int32_t*>(ids)[(int64_t)t * g.topk + j];
-      if (e < bounds[0] || e >= e_end) continue;
-      int f = 0;
-      while (f + 1 < F && e >= bounds[f + 1]) ++f;
-      mask |= 1u << f;
-    }
-#pragma unroll
-    for (int f = 0; f < ASAP_MAX_F; ++f) mycnt[f] += (mask >> f) & 1u;
-  }
-  // exclusive scan of mycnt[f] over threads, for every f
-  int32_t myoff[ASAP_MAX_F];
-#pragma unroll
-  for (int f = 0; f < ASAP_MAX_F; ++f) {
-    if (f >= F) break;
-    int32_t v = mycnt[f];
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      int32_t u = __shfl_up_sync(0xffffffffu, v, d);
-      if (lane >= d) v += u;
-    }
-    if (lane == 31) warp_tot[f][warp] = v;
-    myoff[f] = v - mycnt[f];
-  }
+  // Rounds of 1024 consecutive tokens (thread i takes token base + i, so the id loads and the row-index stores
+  // of a warp are contiguous): per-F-rank warp ballots, a scan over the 32 warps, a running total per F rank.
+  __shared__ int32_t wcnt[32][ASAP_MAX_F];
+  __shared__ int32_t run[ASAP_MAX_F];
+  if (tid < ASAP_MAX_F) run[tid] = 0;
   __syncthreads();
-  if (warp == 0) {
-    for (int f = 0; f < F; ++f) {
-      int32_t v = warp_tot[f][lane];
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        int32_t u = __shfl_up_sync(0xffffffffu, v, d);
-        if (lane >= d) v += u;
+  const uint32_t lt = (1u << lane) - 1u;
+  const int64_t e_lo = bounds[0], e_end = bounds[F];
+  for (int base = 0; base < n; base += kRouteThreads) {
+    const int t = base + tid;
+    uint32_t mask = 0;
+    if (t < n) {
+      for (int j = 0; j < g.topk; ++j) {
+        const int64_t e = ids_is_int64 ? reinterpret_cast<const int64_t*>(ids)[(int64_t)t * g.topk + j]
+                                       : reinterpret_cast<const int32_t*>(ids)[(int64_t)t * g.topk + j];
+        if (e < e_lo || e >= e_end) continue;
+        int f = 0;
+        while (f + 1 < F && e >= bounds[f + 1]) ++f;
+        mask |= 1u << f;
       }
-      warp_tot[f][lane] = v;  // inclusive
     }
-  }
-  __syncthreads();
+    uint32_t bal[ASAP_MAX_F];
 #pragma unroll
-  for (int f = 0; f < ASAP_MAX_F; ++f) {
-    if (f >= F) break;
-    if (warp > 0) myoff[f] += warp_tot[f][warp - 1];
-  }
-  // second pass: write the row indices
-  for (int t = t0; t < t1; ++t) {
-    uint32_t mask = 0;
-    for (int j = 0; j < g.topk; ++j) {
-      int64_t e = ids_is_int64 ? reinterpret_cast<const int64_t*>(ids)[(int64_t)t * g.topk + j]
-                               : reinterpret_cast<const int32_t*>(ids)[(int64_t)t * g.topk + j];
-      if (e < bounds[0] || e >= e_end) continue;
-      int f = 0;
-      while (f + 1 < F && e >= bounds[f + 1]) ++f;
-      mask |= 1u << f;
+    for (int f = 0; f < ASAP_MAX_F; ++f) {
+      bal[f] = __ballot_sync(0xffffffffu, (mask >> f) & 1u);
+      if (lane == 0) wcnt[warp][f] = __popc(bal[f]);
     }
-    for (int f = 0; f < F; ++f) {
-      int32_t r = -1;
-      if ((mask >> f) & 1u) r = myoff[f]++;
-      row_of[(int64_t)f * g.n_max + t] = r;
+    __syncthreads();
+    if (warp == 0) {
+      for (int f = 0; f < F; ++f) {
+        const int32_t c = wcnt[lane][f];
+        int32_t v = c;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int32_t u = __shfl_up_sync(0xffffffffu, v, d);
+          if (lane >= d) v += u;
+        }
+        wcnt[lane][f] = run[f] + v - c;  // exclusive, plus the rows of earlier rounds
+        __syncwarp();
+        if (lane == 31) run[f] += v;
+        __syncwarp();
+      }
     }
+    __syncthreads();
+    if (t < n) {
+#pragma unroll
+      for (int f = 0; f < ASAP_MAX_F; ++f) {
+        if (f >= F) break;
+        const int32_t r = ((mask >> f) & 1u) ? wcnt[warp][f] + __popc(bal[f] & lt) : -1;
+        row_of[(int64_t)f * g.n_max + t] = r;
+      }
+    }
+    __syncthreads();
   }
   if (tid < F) {
-    const int32_t total = warp_tot[tid][31];
+    const int32_t total = run[tid];
     count[tid] = total > 0 ? total : 1;
     pad[tid] = total > 0 ? 0 : 1;
   }

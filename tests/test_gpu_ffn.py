@@ -51,7 +51,11 @@ def check_chain(h: FfnHarness, x, ids, w, gate, up, w2, e0, P, swiglu_limit=None
     hq = device_bytes(h.ptrs["hq"], rows * I).reshape(rows, I)
     hsf = mx.sf_from_atoms(device_bytes(h.ptrs["hq_sf"], rows * I // 32), rows, I // 32)
     h_gpu = mx.mx_dequantize(hq[prow], hsf[prow])
-    assert moe.rel_l2(h_gpu, h_ref) < TOL
+    # the kernel stores h in MXFP8: compare with the oracle's MXFP8 rounding of its own h
+    hq_ref, hsf_ref = mx.mx_quantize(h_ref)
+    assert moe.rel_l2(h_gpu, mx.mx_dequantize(hq_ref, hsf_ref)) < TOL
+    assert np.mean(hq[prow] == hq_ref) > 0.9  # codes differ only where fp32 accumulation order tips a rounding
+    assert moe.rel_l2(h_gpu, h_ref) < 6e-2     # the MXFP8 rounding itself (3 mantissa bits)
     # GEMM2 + top-k weight, on the kernel's own h
     y_ref = np.zeros((len(prow), H), np.float32)
     for ex in range(P):
