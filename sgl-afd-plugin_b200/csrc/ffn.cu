@@ -436,22 +436,6 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      // L2 prefetch runs PF k-tiles ahead of the loads (into the next tile at the end of one), so the TMA loads
-      // that feed the 4-stage ring mostly hit L2.
-      constexpr int PF = 8;
-      int pf_tile = blockIdx.x, pf_kt = 0;
-      auto prefetch_next = [&]() {
-        if (pf_tile >= num_tiles) return;
-        int pe, pm, pn;
-        decode_tile(s_mstart, P, NT, pf_tile, pe, pm, pn);
-        tma_prefetch_2d(&p.tmap_a, pf_kt * BK, pm * BM);
-        tma_prefetch_2d(&p.tmap_b, pf_kt * BK, pe * p.N + pn * BN);
-        if (++pf_kt == KT) {
-          pf_kt = 0;
-          pf_tile += gridDim.x;
-        }
-      };
-      for (int i = 0; i < PF; ++i) prefetch_next();
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int e, m_blk, n_t;
         decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
@@ -470,7 +454,6 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
           tma_load_2d(sB + stage * B_BYTES, &p.tmap_b, kt * BK, b_row, &full[stage]);
           bulk_load(sSFA + stage * SFA_BYTES, sfa + (uint64_t)kt * SFA_BYTES, SFA_BYTES, &full[stage]);
           bulk_load(sSFB + stage * SFB_BYTES, sfb + (uint64_t)kt * sfb_kstride, SFB_BYTES, &full[stage]);
-          prefetch_next();
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
