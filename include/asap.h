@@ -141,6 +141,23 @@ int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n
                  uint64_t route_ws, uint64_t shared, uint64_t out, uint64_t status, uint64_t timeout_ns,
                  void* stream);
 
+/* Allocation-free asap_dispatch (no counterpart in the reference).  Some callers cannot allocate device memory:
+ * an attention rank whose free memory SGLang has already handed to the KV-cache pool, or a host that binds this
+ * ABI from another language and only holds the transport's mapped arenas.  This entry point needs no routing
+ * workspace from them: the routing table of each slot lives in a static device array inside the library (8
+ * slots, num_f * n_max <= 131072 rows per slot, about 4 MiB held by every GPU that loads the library until the
+ * process exits), and *route_ws_out returns its device address for asap_combine / asap_wait_replies.  Larger
+ * geometries or slot >= 8 are rejected with ASAP_EINVAL.  The first call on a device looks the array up
+ * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.  It calls no
+ * cudaMalloc/cudaFree.  Every call shares the array: a slot's table keeps the last call's contents until the next
+ * dispatch on that slot overwrites it, so dispatches on one slot that overlap on the GPU (or a dispatch that
+ * overlaps the combine still reading the slot's table) race.  Otherwise identical to asap_dispatch. */
+int asap_dispatch_noalloc(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                          const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                          int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                          const uint64_t* bells, uint64_t result, int32_t backpressure, uint64_t status,
+                          uint64_t timeout_ns, void* stream, uint64_t* route_ws_out);
+
 /* Wait (bounded by timeout_ns) until done[f][slot] >= seq for every f, without reading the segments
  * (replaces channel.py:364-377 AttnChannel.wait for callers that sum the segments themselves). */
 int asap_wait_replies(const asap_geometry_t* g, int32_t slot, uint32_t seq, uint64_t result, uint64_t status,

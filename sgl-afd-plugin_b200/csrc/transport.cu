@@ -8,6 +8,9 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace asap {
@@ -356,6 +359,35 @@ int sm_count() {
   return cached[dev];
 }
 
+// ------------------------------------------------------------------ allocation-free dispatch scratch
+// Routing tables of asap_dispatch_noalloc: one per slot, in a file-scope device array that every GPU loading
+// the library holds until the process exits (8 slots x 512 KiB + headers, about 4 MiB).
+constexpr int kNoAllocSlots = 8;
+constexpr uint64_t kNoAllocEntries = 1ull << 17;  // num_f * n_max routing-table rows per slot
+constexpr uint64_t kNoAllocSlotBytes = kWsRows + 4ull * kNoAllocEntries;
+static __device__ __align__(256) uint8_t g_noalloc_route[kNoAllocSlots][kNoAllocSlotBytes];
+
+// Device address of g_noalloc_route on the current device, looked up once per device (the host-side symbol is
+// only a stand-in and must never reach a kernel).
+static int noalloc_base(uint64_t* base) {
+  static std::mutex mu;
+  static uint64_t cached[64] = {0};
+  int dev = 0;
+  ASAP_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("asap_dispatch_noalloc: device ordinal %d out of range", dev);
+    return ASAP_EINVAL;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cached[dev]) {
+    void* p = nullptr;
+    ASAP_CUDA(cudaGetSymbolAddress(&p, g_noalloc_route));
+    cached[dev] = (uint64_t)p;
+  }
+  *base = cached[dev];
+  return ASAP_OK;
+}
+
 }  // namespace asap
 
 using namespace asap;
@@ -609,6 +641,42 @@ int asap_wait_replies(const asap_geometry_t* g, int32_t slot, uint32_t seq, uint
   }
   wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns);
   ASAP_CHECK_LAUNCH("wait_replies_kernel");
+  return ASAP_OK;
+}
+
+// Allocation-free variant of asap_dispatch (no counterpart in the reference): the routing table lives in
+// g_noalloc_route[slot] instead of a caller-allocated workspace; *route_ws_out receives its device address for
+// asap_combine / asap_wait_replies.  Checks, kernels and results are those of asap_dispatch.
+int asap_dispatch_noalloc(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                          const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                          int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                          const uint64_t* bells, uint64_t result, int32_t backpressure, uint64_t status,
+                          uint64_t timeout_ns, void* stream, uint64_t* route_ws_out) {
+  int rc = check_geometry(g);
+  if (rc) return rc;
+  if (!route_ws_out) {
+    set_error("asap_dispatch_noalloc: route_ws_out is NULL");
+    return ASAP_EINVAL;
+  }
+  if (slot < 0 || slot >= kNoAllocSlots) {
+    set_error("asap_dispatch_noalloc: slot %d outside the %d slots of the static routing tables", slot,
+              kNoAllocSlots);
+    return ASAP_EINVAL;
+  }
+  if ((uint64_t)g->num_f * (uint64_t)g->n_max > kNoAllocEntries) {
+    set_error("asap_dispatch_noalloc: num_f * n_max = %llu exceeds the static maximum of %llu routing-table rows "
+              "per slot; use asap_dispatch with a workspace of asap_route_ws_bytes()",
+              (unsigned long long)g->num_f * (unsigned long long)g->n_max, (unsigned long long)kNoAllocEntries);
+    return ASAP_EINVAL;
+  }
+  uint64_t base = 0;
+  rc = noalloc_base(&base);
+  if (rc) return rc;
+  const uint64_t ws = base + (uint64_t)slot * kNoAllocSlotBytes;
+  rc = asap_dispatch(g, a, slot, seq, layer_id, epochs, x, ids, ids_is_int64, w, w_is_bf16, n, expert_bounds,
+                     recv, bells, result, ws, backpressure, status, timeout_ns, stream);
+  if (rc) return rc;
+  *route_ws_out = ws;
   return ASAP_OK;
 }
 
