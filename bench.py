@@ -461,14 +461,20 @@ def run_multi(args):
             "roofline": None, "cpu_baseline": None, "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    # orderly shutdown: every process unmaps its peers' memory before any process frees its own
+    dist.barrier()
+    if is_a:
+        channel.unmap_peers()
+    else:
+        server.unmap_peers()
     dist.barrier()
     if is_a:
         channel.close()
-    dist.barrier()
-    if not is_a:
+    else:
         sched.close()
         server.close()
         experts.release()
+    dist.barrier()
     dist.destroy_process_group()
 
 

@@ -112,9 +112,9 @@ class AttnChannel:
     def connect(self) -> "AttnChannel":
         """Allocate the ResultArena, hand it to every F rank, map their RecvArenas and doorbell pages."""
         g = self.g
-        N.call("asap_init", self.device)
         if self.mem is None:
             self.mem = select_memory(self.memory, self.device)
+        self.mem.activate()
         if self.expert_bounds is None:
             n_exp = (self.hello.get("model") or {}).get("n_experts")
             if n_exp is None or n_exp % g.num_f:
@@ -126,10 +126,7 @@ class AttnChannel:
             raise ValueError("expert_bounds needs num_f + 1 entries")
         self._result_mem = self.mem.device(g.result_bytes)
         self._result = self._result_mem.ptr
-        stream = torch.cuda.current_stream(self.device)
-        N.call("asap_memset32", self._result, self.seq_base & SEQ_MASK, g.flags_bytes // 4,
-               ctypes.c_void_p(stream.cuda_stream))
-        stream.synchronize()
+        self.mem.fill32(self._result, self.seq_base & SEQ_MASK, g.flags_bytes // 4)
         hello = {**self.hello, "proto": PROTO_VERSION, "a": self.a, "geometry": g.as_dict(), "pid": os.getpid(),
                  "memory": self.mem.kind, "peer": self.mem.identity(), "result": self._result_mem.desc}
         try:
@@ -153,10 +150,9 @@ class AttnChannel:
             raise
         self._seq = [self.seq_base] * g.slots
         self._poison = None
-        self.status = HostWords(1)
+        self.status = self.mem.status_words(1)
         ws_bytes = N.lib().asap_route_ws_bytes(ctypes.byref(N.geometry_struct(g)))
-        self._route_ws = [torch.empty(ws_bytes, dtype=torch.uint8, device=f"cuda:{self.device}")
-                          for _ in range(g.slots)]
+        self._route_ws = [self.mem.workspace(ws_bytes) for _ in range(g.slots)]
         self._gs = N.geometry_struct(g)
         F = g.num_f
         self._c_epochs = (ctypes.c_int32 * F)(*self._epoch)
@@ -169,6 +165,12 @@ class AttnChannel:
         """The only way out of a poisoned channel: a new epoch and a fresh ResultArena on every F rank."""
         self.close()
         return self.connect()
+
+    def unmap_peers(self) -> None:
+        """Unmap every F rank's RecvArena and doorbell page (first step of an orderly multi-process shutdown: every
+        process unmaps its peers' memory before any process frees its own)."""
+        for shared in self._maps:
+            shared.release()
 
     def close(self) -> None:
         """Release everything. Synchronize the streams that used the channel first."""
@@ -207,6 +209,9 @@ class AttnChannel:
     def route_ws(self, slot: int) -> torch.Tensor:
         return self._route_ws[slot]
 
+    def _ws_ptr(self, slot: int) -> int:
+        return self._route_ws[slot].data_ptr()
+
     # ---------------------------------------------------------------- data path
     def send(self, layer_id: int, slot: int, x_ptr: int, ids_ptr: int, w_ptr: int, n_tokens: int, stream: int, *,
              ids_is_int64: bool = False, w_is_bf16: bool = False) -> Ticket:
@@ -222,7 +227,7 @@ class AttnChannel:
             epochs = (ctypes.c_int32 * g.num_f)(*([self._epoch_override] * g.num_f))
         N.call("asap_dispatch", ctypes.byref(self._gs), self.a, slot, seq, layer_id, epochs, x_ptr, ids_ptr,
                int(ids_is_int64), w_ptr, int(w_is_bf16), n_tokens, self._c_bounds, self._c_recv, self._c_bells,
-               self._result, self._route_ws[slot].data_ptr(), int(self._backpressure), self.status.ptr,
+               self._result, self._ws_ptr(slot), int(self._backpressure), self.status.ptr,
                int(self.timeout_s * 1e9), ctypes.c_void_p(stream))
         return Ticket(slot, seq, layer_id, n_tokens)
 
@@ -240,5 +245,5 @@ class AttnChannel:
         """Enqueue the bounded reply wait fused with out = bf16(sum_f partial_f) (+ shared): the A-side combine."""
         self.check()
         N.call("asap_combine", ctypes.byref(self._gs), ticket.slot, ticket.seq, ticket.n_tokens, self._result,
-               self._route_ws[ticket.slot].data_ptr(), shared_ptr, out_ptr, self.status.ptr,
+               self._ws_ptr(ticket.slot), shared_ptr, out_ptr, self.status.ptr,
                int(self.timeout_s * 1e9), ctypes.c_void_p(stream))

@@ -54,8 +54,30 @@ class IpcMemory:
     def __init__(self, ordinal: int, reason: str = "requested"):
         self.ordinal, self.reason = ordinal, reason
 
+    def activate(self) -> None:
+        """Make this backend's device current for the calling thread."""
+        N.call("asap_init", self.ordinal)
+
+    def fill32(self, ptr: int, value: int, count: int) -> None:
+        """Set ``count`` 32-bit words of device memory at ``ptr`` to ``value`` and wait for it."""
+        import torch
+
+        stream = torch.cuda.current_stream(self.ordinal)
+        N.call("asap_memset32", ptr, value & 0xFFFFFFFF, count, ctypes.c_void_p(stream.cuda_stream))
+        stream.synchronize()
+
     def identity(self) -> dict:
         return {"host": socket.gethostname()}
+
+    def status_words(self, count: int) -> "HostWords":
+        """Registered host words the device writes status into."""
+        return HostWords(count)
+
+    def workspace(self, nbytes: int):
+        """Private device scratch of this rank (torch-allocated)."""
+        import torch
+
+        return torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{self.ordinal}")
 
     def check_peer(self, peer: dict) -> None:
         mine = socket.gethostname()

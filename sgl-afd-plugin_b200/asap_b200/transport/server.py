@@ -100,13 +100,12 @@ class FfnServer:
     def start(self) -> "FfnServer":
         """Allocate and zero the RecvArena and the doorbell page, then listen for A ranks."""
         g = self.g
-        N.call("asap_init", self.device)
-        self.mem = select_memory(self.memory, self.device)
+        if self.mem is None:
+            self.mem = select_memory(self.memory, self.device)
+        self.mem.activate()
         self._recv = self.mem.device(g.recv_bytes)
         self.recv_base = self._recv.ptr
-        stream = torch.cuda.current_stream(self.device)
-        N.call("asap_memset32", self.recv_base, 0, g.recv_bytes // 4, ctypes.c_void_p(stream.cuda_stream))
-        stream.synchronize()
+        self.mem.fill32(self.recv_base, 0, g.recv_bytes // 4)
         self._page = self.mem.doorbells(g.host_bytes, os.path.join(self.run_dir, f"asap_f{self.f}_{os.getpid()}.slots"))
         words = np.ctypeslib.as_array((ctypes.c_uint64 * (g.host_bytes // 8)).from_address(self._page.ptr))
         self._bells = words[: g.num_a * g.slots * (BELL_STRIDE // 8)].reshape(-1, BELL_STRIDE // 8)[:, 0]
@@ -186,7 +185,7 @@ class FfnServer:
             raise HandshakeError(
                 f"A rank {a} is connected from {old.host} (pid {old.pid}), and {host} claims it too: "
                 "the attention instances sharing the FFN ranks need disjoint --asap-attn-base-replica ranges")
-        N.call("asap_init", self.device)
+        self.mem.activate()
         result = self.mem.open(hello["result"])
         with self._lock:
             old = self.peers.get(a)
@@ -293,7 +292,7 @@ class FfnServer:
                       idle_sleep_s: float = 0.0002) -> None:
         """Poll and hand every complete job to ``handler`` until ``stop`` is set (server.py:352-377)."""
         sys.setswitchinterval(1e-5)
-        N.call("asap_init", self.device)
+        self.mem.activate()
         last_job = time.monotonic()
         while not stop.is_set():
             jobs = self.poll()
@@ -303,6 +302,11 @@ class FfnServer:
                 last_job = time.monotonic()
             elif idle_sleep_s and time.monotonic() - last_job > spin_s:
                 time.sleep(idle_sleep_s)
+
+    def unmap_peers(self) -> None:
+        """Unmap every connected A rank's ResultArena (see AttnChannel.unmap_peers)."""
+        for peer in self.peers.values():
+            peer.mapping.release()
 
     def close(self) -> None:
         """Stop the handshake thread, unmap the A arenas, free the doorbell page and the RecvArena."""
