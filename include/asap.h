@@ -213,7 +213,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
                  uint64_t timeout_ns, void* stream);
 
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
- * stream around its 5 kernels (route_local, quant_permute, gemm1, gemm2, finalize_reply); last_timing waits
+ * stream around its 5 stages (routing, quantise+permute, gemm1, gemm2, reduce+reply); last_timing waits
  * for the recorded jobs (the last 64 since enable) and returns each kernel's mean duration in ms (n >= 5). */
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable);
 int asap_ffn_last_timing(uint64_t ws_handle, float* ms, int32_t n);

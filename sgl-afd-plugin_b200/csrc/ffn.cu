@@ -7,7 +7,7 @@
 //   srt/managers/scheduler.py:387-450 run_job / rows_of        -> asap_ffn_job (launch chain, arena views)
 //   SGLang FusedMoE -> FlashInfer trtllm_fp4_block_scale_routed_moe (scheduler.py:410-412;
 //   srt/layers/quantization/mxfp4_flashinfer_trtllm_moe.py:68-99)
-//                                                              -> route_count/scan/place, quant_permute, moe_gemm<0,1>,
+//                                                              -> route_count/scan/place, quant_tok, permute_copy, moe_gemm<0,1>,
 //                                                                 finalize_reply kernels
 //   transport/server.py:340-350     FfnServer.reply            -> finalize_reply epilogue (P2P rows + done flag)
 #include <cuda.h>
@@ -37,7 +37,7 @@ constexpr int kPermChunks = 128;  // chunks of pairs the permutation is split in
 struct WsLayout {
   int32_t n_max, topk, P, H, I;
   int64_t m_cap;  // rows of the expert-major activation buffers (multiple of 128)
-  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, xq, xq_sf, hq, hq_sf, y2, total;
+  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, xtok, xtok_sf, xq, xq_sf, hq, hq_sf, y2, total;
 };
 
 static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
@@ -61,6 +61,8 @@ static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
   L.pair_pos = take(4ull * n_max * topk);
   L.row_tok = take(4ull * L.m_cap);
   L.row_w = take(4ull * L.m_cap);
+  L.xtok = take((uint64_t)n_max * H);
+  L.xtok_sf = take((uint64_t)n_max * (H / 32));
   L.xq = take((uint64_t)L.m_cap * H);
   L.xq_sf = take((uint64_t)L.m_cap * (H / 32));
   L.hq = take((uint64_t)L.m_cap * I);
@@ -254,8 +256,10 @@ struct QuantArgs {
   int32_t P, H;
   const __nv_bfloat16* x;  // [n, H] in the RecvArena
   const int32_t* row_tok;
-  uint8_t* xq;     // [m_cap, H] E4M3
-  uint8_t* xq_sf;  // scale atoms [m_cap/128][H/128][512]
+  uint8_t* xtok;     // [n_max, H] E4M3, one row per token
+  uint8_t* xtok_sf;  // [n_max, H/32] E8M0, row-major
+  uint8_t* xq;       // [m_cap, H] E4M3, expert-major
+  uint8_t* xq_sf;    // scale atoms [m_cap/128][H/128][512]
 };
 
 // Quantise 32 consecutive fp32 values to E4M3 with one E8M0 scale; returns the scale byte.
@@ -277,17 +281,17 @@ __device__ __forceinline__ uint32_t mx_quant32(const float (&v)[32], uint4& lo, 
   return sb;
 }
 
-__global__ void __launch_bounds__(256) quant_permute_kernel(const __grid_constant__ QuantArgs p) {
+// Every token once: bf16 row -> E4M3 row + E8M0 scale per 32 (OCP MX rule).  One warp per token, a lane per
+// 32-value block.
+__global__ void __launch_bounds__(256) quant_tok_kernel(const __grid_constant__ QuantArgs p) {
   if (!p.desc->valid) return;
-  const int64_t rows = (int64_t)p.mstart[p.P] * 128;
+  const int n = p.desc->n;
   const int lane = threadIdx.x & 31;
   const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = p.H, kblocks = H / 32;
-  for (int64_t r = gwarp; r < rows; r += nwarps) {
-    const int32_t t = p.row_tok[r];
-    if (t < 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)t * H);
+  for (int64_t t = gwarp; t < n; t += nwarps) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + t * H);
     for (int kb = lane; kb < kblocks; kb += 32) {
       float v[32];
 #pragma unroll
@@ -303,11 +307,32 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const __grid_constan
       }
       uint4 lo, hi;
       const uint32_t sb = mx_quant32(v, lo, hi);
-      uint4* dst = reinterpret_cast<uint4*>(p.xq + r * H + (int64_t)kb * 32);
+      uint4* dst = reinterpret_cast<uint4*>(p.xtok + t * H + (int64_t)kb * 32);
       dst[0] = lo;
       dst[1] = hi;
-      p.xq_sf[sf_atom_off(r, kb, kblocks)] = (uint8_t)sb;
+      p.xtok_sf[t * kblocks + kb] = (uint8_t)sb;
     }
+  }
+}
+
+// Expert-major copy of the quantised rows: permuted row r <- token row_tok[r] (rows and their scale atoms).
+__global__ void __launch_bounds__(256) permute_copy_kernel(const __grid_constant__ QuantArgs p) {
+  if (!p.desc->valid) return;
+  const int64_t rows = (int64_t)p.mstart[p.P] * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int H = p.H, kblocks = H / 32, nvec = H / 16;
+  for (int64_t r = gwarp; r < rows; r += nwarps) {
+    const int32_t t = p.row_tok[r];
+    if (t < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xtok + (int64_t)t * H);
+    uint4* dst = reinterpret_cast<uint4*>(p.xq + r * H);
+    for (int c = lane; c < nvec; c += 32) dst[c] = src[c];
+    // the 4 scales of one 128-value chunk are 4 consecutive bytes of the atom: one 32-bit store each
+    const uint32_t* sf = reinterpret_cast<const uint32_t*>(p.xtok_sf + (int64_t)t * kblocks);
+    for (int kc = lane; kc < kblocks / 4; kc += 32)
+      *reinterpret_cast<uint32_t*>(p.xq_sf + sf_atom_off(r, kc * 4, kblocks)) = sf[kc];
   }
 }
 
@@ -322,7 +347,10 @@ constexpr int SFA_BYTES = 512, SFB_BYTES = 1024;
 constexpr uint32_t STAGE_TX = A_BYTES + B_TX + SFA_BYTES + SFB_BYTES;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + NUM_EPI_WARPS);
-constexpr uint32_t TMEM_COLS = 512, TMEM_ACC = 0, TMEM_SFA = 256, TMEM_SFB = 264;
+// TMEM columns: the 256-column accumulator, then one set of scale-factor columns per pipeline stage (SFA 4,
+// SFB 8), so the scale copy of stage s+1 never waits for the MMAs still reading stage s's scales.
+constexpr uint32_t TMEM_COLS = 512, TMEM_ACC = 0, TMEM_SFA = 256, TMEM_SFB = TMEM_SFA + 4 * STAGES;
+static_assert(TMEM_SFB + 8 * STAGES <= TMEM_COLS, "scale-factor columns exceed TMEM");
 constexpr int SMEM_TILES = STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES);
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + SMEM_TILES + 1024 /*barriers*/ + 4 * (ASAP_MAX_LOCAL_EXPERTS + 8);
 
@@ -495,16 +523,17 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
             break;
           }
           tc_fence_after();
-          tc_cp_32x128b_warpx4(tmem_base + TMEM_SFA, sdesc_sf(sSFA + stage * SFA_BYTES));
-          tc_cp_32x128b_warpx4(tmem_base + TMEM_SFB, sdesc_sf(sSFB + stage * SFB_BYTES));
-          tc_cp_32x128b_warpx4(tmem_base + TMEM_SFB + 4, sdesc_sf(sSFB + stage * SFB_BYTES + 512));
+          const uint32_t t_sfa = tmem_base + TMEM_SFA + 4 * stage, t_sfb = tmem_base + TMEM_SFB + 8 * stage;
+          tc_cp_32x128b_warpx4(t_sfa, sdesc_sf(sSFA + stage * SFA_BYTES));
+          tc_cp_32x128b_warpx4(t_sfb, sdesc_sf(sSFB + stage * SFB_BYTES));
+          tc_cp_32x128b_warpx4(t_sfb + 4, sdesc_sf(sSFB + stage * SFB_BYTES + 512));
           const uint64_t adesc = sdesc_sw128(sA + stage * A_BYTES);
           const uint64_t bdesc = sdesc_sw128(sB + stage * B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
             const uint32_t id = idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4);
             tc_mma_mxf8f6f4(tmem_base + TMEM_ACC, adesc + 2ull * k, bdesc + 2ull * k, id, (kt | k) != 0,
-                            (tmem_base + TMEM_SFA) | ((uint32_t)k << 30), (tmem_base + TMEM_SFB) | ((uint32_t)k << 30));
+                            t_sfa | ((uint32_t)k << 30), t_sfb | ((uint32_t)k << 30));
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -625,21 +654,46 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = p.H, nvec = H / 8;
   for (int64_t t = gwarp; t < n; t += nwarps) {
-    int32_t pos[32];
-    for (int j = 0; j < p.topk; ++j) pos[j] = p.pair_pos[t * p.topk + j];
+    // this token's local pairs, in ascending slot order (the summation order)
+    const int32_t mine = lane < p.topk ? p.pair_pos[t * p.topk + lane] : -1;
+    const uint32_t vmask = __ballot_sync(0xffffffffu, mine >= 0);
+    const int cnt = __popc(vmask);
+    const __nv_bfloat16* rowp[8];  // the first 8 rows, resolved once per token
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int src = __fns(vmask, 0, i + 1);
+      const int32_t pos = __shfl_sync(0xffffffffu, mine, src & 31);
+      rowp[i] = p.y2 + (int64_t)(i < cnt ? pos : 0) * H;
+    }
+    int32_t extra[24];  // rows 8.. (more than 8 local experts of one token; cnt is warp-uniform)
+    for (int i = 8; i < cnt; ++i) extra[i - 8] = __shfl_sync(0xffffffffu, mine, __fns(vmask, 0, i + 1) & 31);
     for (int c = lane; c < nvec; c += 32) {
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int j = 0; j < p.topk; ++j) {
-        if (pos[j] < 0) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(p.y2 + (int64_t)pos[j] * H + (int64_t)c * 8);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+      uint4 v[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h[i]);
-          acc[2 * i] += f.x;
-          acc[2 * i + 1] += f.y;
+      for (int i = 0; i < 8; ++i)  // all loads in flight, then the adds in slot order
+        if (i < cnt) v[i] = *reinterpret_cast<const uint4*>(rowp[i] + (int64_t)c * 8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i >= cnt) break;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
+        }
+      }
+      for (int i = 8; i < cnt; ++i) {  // more than 8 local experts of one token: the rest one by one
+        const uint4 u = *reinterpret_cast<const uint4*>(p.y2 + (int64_t)extra[i - 8] * H + (int64_t)c * 8);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
         }
       }
       uint4 r;
@@ -706,7 +760,7 @@ struct ExpertsHandle {
   asap_mxfp4_experts_t e;
   CUtensorMap w13_map, w2_map;
 };
-constexpr int kTimedKernels = 5;  // routing (count+scan+place), quant_permute, gemm1, gemm2, finalize_reply
+constexpr int kTimedKernels = 5;  // routing (count+scan+place), quantise+permute, gemm1, gemm2, finalize_reply
 constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
 struct WsHandle {
   uint8_t* base;
@@ -942,10 +996,14 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   qa.H = L.H;
   qa.x = (const __nv_bfloat16*)x;
   qa.row_tok = pa.row_tok;
+  qa.xtok = B + L.xtok;
+  qa.xtok_sf = B + L.xtok_sf;
   qa.xq = B + L.xq;
   qa.xq_sf = B + L.xq_sf;
-  quant_permute_kernel<<<sms * 4, 256, 0, st>>>(qa);
-  ASAP_CHECK_LAUNCH("quant_permute_kernel");
+  quant_tok_kernel<<<sms * 4, 256, 0, st>>>(qa);
+  ASAP_CHECK_LAUNCH("quant_tok_kernel");
+  permute_copy_kernel<<<sms * 4, 256, 0, st>>>(qa);
+  ASAP_CHECK_LAUNCH("permute_copy_kernel");
   mark(2);
 
   gemm::Params g1;

@@ -28,7 +28,7 @@ def check_chain(h: FfnHarness, x, ids, w, gate, up, w2, e0, P, swiglu_limit=None
     rows = int(mstart_ref[-1]) * 128
     tt, jj = np.nonzero(pos_ref >= 0)
     prow = pos_ref[tt, jj]
-    # activation quantisation: bit-exact
+    # activation quantisation: bit-exact (expert-major rows and scale atoms)
     xq = device_bytes(h.ptrs["xq"], rows * H).reshape(rows, H)
     xsf = mx.sf_from_atoms(device_bytes(h.ptrs["xq_sf"], rows * H // 32), rows, H // 32)
     q_ref, s_ref = mx.mx_quantize(x[tt])
@@ -76,6 +76,7 @@ def check_chain(h: FfnHarness, x, ids, w, gate, up, w2, e0, P, swiglu_limit=None
 @pytest.mark.parametrize("n,k,P,H,I,e0", [
     (64, 2, 4, 256, 128, 4),       # one tile each way, non-zero expert base
     (300, 4, 6, 512, 256, 0),      # several experts > 128 rows, two n-tiles in GEMM1/GEMM2
+    (64, 12, 16, 256, 128, 0),     # more than 8 local experts per token (the reduce's long path)
 ])
 def test_ffn_chain_random_weights(cuda_ok, n, k, P, H, I, e0):
     rng = np.random.default_rng(n)
