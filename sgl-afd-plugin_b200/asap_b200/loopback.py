@@ -1,4 +1,4 @@
-"""One GPU holding one A rank and one F rank: the 1-GPU deployment of the round trip.
+"""One GPU holding one A rank and one or more F ranks: the 1-GPU deployment of the round trip.
 
 The A side and the F side use the same transport as across GPUs -- the dispatch kernels store into the F
 rank's RecvArena and ring its doorbell page, the F chain starts with the device-side doorbell wait and stores
@@ -11,7 +11,7 @@ finds its flag already set.
 from __future__ import annotations
 
 import tempfile
-from typing import Dict, Optional
+from typing import Dict, List, Optional, Union
 
 import torch
 
@@ -24,10 +24,11 @@ from .transport.server import FfnServer
 
 
 class LocalFfn:
-    """The F rank of a loopback pair, driven from the A rank's send/recv calls."""
+    """The F ranks of a loopback deployment, driven from the A rank's send/recv calls; their jobs run one after
+    the other on one stream."""
 
-    def __init__(self, scheduler: FfnScheduler, a: int, slots: int, device: int):
-        self.sched, self.a, self.device = scheduler, a, device
+    def __init__(self, schedulers: List[FfnScheduler], a: int, slots: int, device: int):
+        self.scheds, self.a, self.device = schedulers, a, device
         self.stream = torch.cuda.Stream(device)
         self.sent = [torch.cuda.Event() for _ in range(slots)]
         self.done = [torch.cuda.Event() for _ in range(slots)]
@@ -41,7 +42,8 @@ class LocalFfn:
         s = ticket.slot
         self.sent[s].record(send_stream)
         self.stream.wait_event(self.sent[s])
-        self.sched.run_device_wait(self.a, s, ticket.seq, ticket.layer_id, self.stream.cuda_stream)
+        for sched in self.scheds:
+            sched.run_device_wait(self.a, s, ticket.seq, ticket.layer_id, self.stream.cuda_stream)
         self.done[s].record(self.stream)
 
     def before_combine(self, ticket, stream: torch.cuda.Stream) -> None:
@@ -49,41 +51,56 @@ class LocalFfn:
 
 
 class Loopback:
-    """A + F on ``device``.  ``experts[layer_id]`` are all routed experts [0, n_experts) of that layer."""
+    """One A rank and ``num_f`` F ranks on ``device``.  ``experts``: for one F rank, ``{layer_id: Mxfp4Experts}``;
+    for several, a list of such dicts, F rank f owning its experts' [expert_base, expert_base + num_local) --
+    contiguous, in F order, possibly uneven (the 2A6F split 43/43/43/43/42/42)."""
 
-    def __init__(self, geometry: Geometry, experts: Dict[int, Mxfp4Experts], *, device: int = 0,
-                 timeout_s: float = 10.0, swiglu_limit: float = 0.0, run_dir: Optional[str] = None,
-                 timing: bool = False):
-        if geometry.num_a != 1 or geometry.num_f != 1 or geometry.group != 1:
-            raise ValueError("a loopback pair is one A rank and one F rank (num_a = num_f = group = 1)")
-        first = next(iter(experts.values()))
-        self.g, self.device = geometry, device
-        self.n_experts = first.num_local
+    def __init__(self, geometry: Geometry, experts: Union[Dict[int, Mxfp4Experts], List[Dict[int, Mxfp4Experts]]],
+                 *, device: int = 0, timeout_s: float = 10.0, swiglu_limit: float = 0.0,
+                 run_dir: Optional[str] = None, timing: bool = False):
+        per_f = [experts] if isinstance(experts, dict) else list(experts)
+        if geometry.num_a != 1 or geometry.group != 1 or geometry.num_f != len(per_f):
+            raise ValueError("a loopback deployment is one A rank (num_a = group = 1) and num_f F ranks, one experts "
+                             "dict per F rank")
+        firsts = [next(iter(d.values())) for d in per_f]
+        bounds = [firsts[0].expert_base]
+        for f, e in enumerate(firsts):
+            if e.expert_base != bounds[-1]:
+                raise ValueError(f"F rank {f}'s experts start at {e.expert_base}, expected {bounds[-1]} (contiguous)")
+            bounds.append(e.expert_base + e.num_local)
+        self.g, self.device, self.expert_bounds = geometry, device, bounds
+        self.n_experts = bounds[-1] - bounds[0]
         run_dir = run_dir or ("/dev/shm" if _writable("/dev/shm") else tempfile.gettempdir())
-        self.server = FfnServer(0, geometry, device=device, run_dir=run_dir, listen=False).start()
-        self.channel = AttnChannel(0, geometry, [("in-process", 0)], device=device, timeout_s=timeout_s,
-                                   expert_bounds=[first.expert_base, first.expert_base + first.num_local],
-                                   _connector=lambda f, hello: self.server.handshake(hello)).connect()
-        self.sched = FfnScheduler(self.server, experts, swiglu_limit=swiglu_limit, timeout_s=timeout_s,
-                                  timing=timing)
-        self.local = LocalFfn(self.sched, 0, geometry.slots, device)
+        self.servers = [FfnServer(f, geometry, device=device, run_dir=run_dir, listen=False).start()
+                        for f in range(len(per_f))]
+        self.server = self.servers[0]
+        self.channel = AttnChannel(0, geometry, [("in-process", f) for f in range(len(per_f))], device=device,
+                                   timeout_s=timeout_s, expert_bounds=bounds,
+                                   _connector=lambda f, hello: self.servers[f].handshake(hello)).connect()
+        self.scheds = [FfnScheduler(srv, d, swiglu_limit=swiglu_limit, timeout_s=timeout_s, timing=timing)
+                       for srv, d in zip(self.servers, per_f)]
+        self.sched = self.scheds[0]
+        self.local = LocalFfn(self.scheds, 0, geometry.slots, device)
         self.buffer = AsapBuffer(self.channel, device, local_ffn=self.local)
 
     def install(self) -> AsapBuffer:
-        """Make this pair's buffer the process's AsapBuffer (what AsapDispatcher uses)."""
+        """Make this deployment's buffer the process's AsapBuffer (what AsapDispatcher uses)."""
         return AsapBuffer.install(self.buffer)
 
     def check(self) -> None:
         self.channel.check()
-        self.sched.check()
+        for sched in self.scheds:
+            sched.check()
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)
         if AsapBuffer._buffer is self.buffer:
             AsapBuffer.install(None)
-        self.sched.close()
+        for sched in self.scheds:
+            sched.close()
         self.channel.close()
-        self.server.close()
+        for srv in self.servers:
+            srv.close()
 
 
 def _writable(path: str) -> bool:

@@ -151,3 +151,67 @@ def test_deepseek_v3_layer_shape(cuda_ok):
     finally:
         lb.close()
         e.release()
+
+
+def _from_fp32(rng, E, H, I, base):
+    w13 = rng.standard_normal((E, 2 * I, H)).astype(np.float32) * 0.02
+    w2 = rng.standard_normal((E, H, I)).astype(np.float32) * 0.02
+    c13, s13 = mxfp4_quantize(w13)
+    c2, s2 = mxfp4_quantize(w2)
+    return Mxfp4Experts.from_logical(c13, s13, c2, s2, expert_base=base)
+
+
+def test_config1_two_f_ranks(cuda_ok):
+    """BASELINE config 1 exactly: 1 A replica + 2 F ranks with 8 experts each (T=512, H=1024, top-2 softmax over
+    16 experts, I=512, fp32 N(0, 0.02) weights as MXFP4, x ~ N(0,1) bf16, seed 0)."""
+    rng = np.random.default_rng(0)
+    T, H, I = 512, 1024, 512
+    per_f = [{0: _from_fp32(rng, 8, H, I, 0)}, {0: _from_fp32(rng, 8, H, I, 8)}]
+    lb = Loopback(Geometry(1, 1, 2, T, H, 2, 2), per_f, timeout_s=5.0)
+    lb.install()
+    try:
+        ow = [experts_to_oracle(d[0]) for d in per_f]
+        x = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        ids, w = moe.topk_routing(rng.standard_normal((T, 16)), 2, "softmax")
+        got = run_layer(lb, 0, x, ids, w)
+        ref = moe.round_trip(x, ids, w, [0, 8, 16], ow)
+        assert moe.rel_l2(got, ref) < TOL
+        # every token to F rank 0 only: F rank 1 gets the one padding row and answers it with zeros
+        ids0 = np.stack([rng.permutation(8)[:2] for _ in range(T)]).astype(np.int32)
+        got0 = run_layer(lb, 0, x, ids0, w)
+        ref0 = moe.round_trip(x, ids0, w, [0, 8, 16], ow)
+        assert moe.rel_l2(got0, ref0) < TOL
+        row_of = lb.channel.route_ws(0)[512: 512 + 4 * 2 * T].view(torch.int32).view(2, T).cpu().numpy()
+        np.testing.assert_array_equal(row_of, moe.f_rank_tables(ids0, [0, 8, 16])[0])
+    finally:
+        lb.close()
+        for d in per_f:
+            d[0].release()
+
+
+def test_uneven_six_f_ranks(cuda_ok):
+    """The 2A6F-style uneven contiguous split (here 6/6/5/5/5/5 of 32 experts), top-8 sigmoid routing."""
+    rng = np.random.default_rng(7)
+    T, H, I, k = 300, 256, 128, 8
+    sizes = [6, 6, 5, 5, 5, 5]
+    bases = np.concatenate([[0], np.cumsum(sizes)])
+    per_f = [{3: Mxfp4Experts.random(sz, H, I, expert_base=int(b), seed=10 + f)}
+             for f, (sz, b) in enumerate(zip(sizes, bases[:-1]))]
+    lb = Loopback(Geometry(1, 1, 1, T, H, k, 6), per_f, timeout_s=5.0)
+    lb.install()
+    try:
+        ow = [experts_to_oracle(d[3]) for d in per_f]
+        x = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        ids, w = moe.topk_routing(rng.standard_normal((T, 32)), k, "sigmoid")
+        shared = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        got = run_layer(lb, 3, x, ids, w, shared)
+        ref = moe.round_trip(x, ids, w, [int(b) for b in bases], ow, shared=shared)
+        assert moe.rel_l2(got, ref) < TOL
+        counts = [lb.scheds[f].debug_tensors()["expert_counts"].cpu().numpy() for f in range(6)]
+        for f in range(6):
+            sel = moe.f_rank_tables(ids, [int(b) for b in bases])[0][f] >= 0
+            np.testing.assert_array_equal(counts[f], moe.expert_counts(ids[sel], int(bases[f]), sizes[f]))
+    finally:
+        lb.close()
+        for d in per_f:
+            d[3].release()
