@@ -33,6 +33,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "MoE layer tokens/s A->F->A (DeepSeek-V3-shape MXFP4 layer, T=16384 per A replica)"
 H, I, E, K_TOP, T_DEFAULT = 7168, 2048, 256, 8, 16384
+SWEEP_T = [256, 1024, 4096, 16384]
+ZIPF_S = 1.2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -109,6 +111,35 @@ def make_routing(T, seed, device):
     w, ids = torch.topk(scores, K_TOP, dim=1)
     w = w / w.sum(1, keepdim=True)
     return ids.to(torch.int32).contiguous(), w.float().contiguous()
+
+
+def zipf_routing(T, seed, device, s=ZIPF_S, perm_seed=1234):
+    """Skewed routing: expert popularity p ~ 1/r^s over a seeded permutation of the experts (the same for every
+    replica), each token's top-8 drawn without replacement with probabilities p (Gumbel top-k), weights
+    sigmoid(N(0,1)) normalised over the 8."""
+    import torch
+
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(perm_seed))
+    logp = torch.empty(E)
+    logp[perm] = -s * torch.log(torch.arange(1, E + 1, dtype=torch.float32))
+    g = torch.Generator(device=device).manual_seed(seed)
+    u = torch.rand(T, E, device=device, generator=g).clamp_(1e-12, 1.0 - 1e-7)
+    scores = logp.to(device) - torch.log(-torch.log(u))
+    ids = torch.topk(scores, K_TOP, dim=1).indices
+    w = torch.sigmoid(torch.randn(T, K_TOP, device=device, generator=g))
+    w = w / w.sum(1, keepdim=True)
+    return ids.to(torch.int32).contiguous(), w.float().contiguous()
+
+
+def topology(name, world):
+    """(A replicas, F ranks) of a ``world``-GPU run: 'half' = world/2 each (1A1F, 2A2F, 4A4F), '2a6f' on 8 GPUs,
+    '2a4f' on 6."""
+    if name == "half":
+        return world // 2, world - world // 2
+    n_a, n_f = int(name[0]), int(name[2])
+    if name[1] != "a" or name[3] != "f" or n_a + n_f != world:
+        raise SystemExit(f"topology {name} does not fit {world} GPUs")
+    return n_a, n_f
 
 
 class SharedExpert:
@@ -397,12 +428,100 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------ 1 GPU, Zipf sweep
+def run_sweep(args):
+    """Routing skew and job size on one GPU: one A rank and 4 F ranks (64 experts each, the 4A4F split) in
+    loopback, Zipf(s=1.2) popularity, T in SWEEP_T.  Per T: tokens/s over K timed steps, the per-F row counts and
+    their imbalance (max / mean), and from device timestamps (one globaltimer, one GPU) the doorbell latency --
+    dispatch released the doorbells -> F rank 0's wait saw its doorbell -- and the F ranks' rows per second of
+    busy time."""
+    import torch
+
+    from asap_b200.dispatcher import AsapDispatcher
+    from asap_b200.experts import Mxfp4Experts
+    from asap_b200.loopback import Loopback
+    from asap_b200.sglang_shim import StandardTopKOutput
+    from asap_b200.transport.layout import Geometry
+
+    dev = "cuda:0"
+    torch.cuda.set_device(0)
+    n_f = 4
+    bounds = expert_bounds(n_f)
+    per_f = [{0: Mxfp4Experts.random(bounds[f + 1] - bounds[f], H, I, expert_base=bounds[f], seed=100 + f,
+                                     scale_lo=117, scale_hi=120)} for f in range(n_f)]
+    T_max = max(SWEEP_T)
+    lb = Loopback(Geometry(1, 1, 2, T_max, H, K_TOP, n_f), per_f, timeout_s=30.0)
+    lb.install()
+    shared = SharedExpert(dev)
+    x_all = torch.randn(T_max, H, device=dev, generator=torch.Generator(device=dev).manual_seed(0)).to(torch.bfloat16)
+    disp = AsapDispatcher(0)
+    stream = torch.cuda.current_stream()
+    for T in SWEEP_T:
+        x = x_all[:T]
+        ids, w = zipf_routing(T, 3, dev) if args.routing == "zipf" else make_routing(T, 3, dev)
+        topk = StandardTopKOutput(w, ids)
+
+        def step():
+            d = disp.dispatch(x, topk)
+            return disp.combine(d, shared=shared(x)), d.ticket
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        lb.check()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clocks:
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for _ in range(args.steps):
+                step()
+            t1.record(stream)
+            torch.cuda.synchronize()
+        lb.check()
+        ms = t0.elapsed_time(t1) / args.steps
+        lat, busy, rows = [], [], None
+        for _ in range(max(args.latency_iters, 1)):
+            _, ticket = step()
+            torch.cuda.synchronize()
+            info = lb.channel.dispatch_info(ticket.slot, stream.cuda_stream)
+            jobs = [sc.job_info(stream.cuda_stream) for sc in lb.scheds]
+            rows = info["counts"]
+            lat.append((jobs[0]["t_seen_ns"] - info["t_ring_ns"]) * 1e-3)
+            busy.append(sum(j["t_reply_ns"] - j["t_seen_ns"] for j in jobs) * 1e-9)
+        lb.check()
+        mean_f = sum(rows) / n_f
+        line = {
+            "metric": METRIC, "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport",
+            "data": "synthetic", "workload_mode": "zipf-sweep",
+            "config": {"workload": f"1 GPU loopback 1A{n_f}F: config 2 layer, T={T}, top-8 "
+                                   f"{'Zipf(s=1.2) popularity over a seeded expert permutation' if args.routing == 'zipf' else 'sigmoid'}",
+                       "tokens_per_replica": T, "a_replicas": 1, "f_ranks": n_f, "expert_bounds": bounds,
+                       "parallelism": f"1A{n_f}F loopback", "routing": args.routing},
+            "f_rows": rows, "f_imbalance": round(max(rows) / mean_f, 4),
+            "doorbell_to_f_start_us_p50": round(statistics.median(lat), 2),
+            "f_rows_per_s": round(sum(rows) / statistics.median(busy), 1),
+            "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4),
+            "weights_gb_read_per_step": round(E * (2 * I * H + H * I) * (0.5 + 1 / 32) / 1e9, 3),
+            "e2e": None, "gpu_launches": args.steps * (4 + 8 * n_f), "roofline": None, "cpu_baseline": None,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    lb.close()
+    for d in per_f:
+        d[0].release()
+
+
 # ------------------------------------------------------------------------------------------ N GPUs
 def expert_bounds(num_f):
     return [(f * E) // num_f for f in range(num_f + 1)]
 
 
 def run_multi(args):
+    """N GPUs, one process each: ranks [0, n_a) are A replicas, the rest F ranks (--topology, default half/half).
+    Each F rank's jobs are enqueued by a feeder thread (each job starts with a bounded device wait for its
+    doorbell), so the main thread stays free for the gloo barriers even when the launch queue is full."""
     import ctypes
     from datetime import timedelta
 
@@ -420,13 +539,16 @@ def run_multi(args):
     dist.init_process_group("gloo", timeout=timedelta(seconds=90))
     torch.cuda.set_device(local)
     dev = f"cuda:{local}"
-    n_a = world // 2
-    n_f = world - n_a
-    T = args.tokens
-    g = Geometry(n_a, 1, 2, T, H, K_TOP, n_f)
+    n_a, n_f = topology(args.topology, world)
+    sweep = args.workload == "zipf-sweep"
+    t_list = SWEEP_T if sweep else [args.tokens]
+    T_max = max(t_list)
+    g = Geometry(n_a, 1, 2, T_max, H, K_TOP, n_f)
     bounds = expert_bounds(n_f)
     is_a = rank < n_a
-    total_steps = 2 * (args.warmup + args.steps)  # device-timed run, then the e2e run
+    lat_iters = args.latency_iters if sweep else 0
+    phases = len(t_list) * (1 if sweep else 2)  # timed (+ e2e) per token count
+    steps_per_phase = args.warmup + args.steps
     timeout_s = 120.0
     ep = None
     if not is_a:
@@ -443,29 +565,27 @@ def run_multi(args):
     if is_a:
         channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s).connect()
     dist.barrier()
+    feeder = None
     if not is_a:
-        stream = torch.cuda.current_stream()
-        for s in range(total_steps):  # the whole run is queued up front: each job waits for its doorbell
-            for a in range(n_a):
-                sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
+        stream = torch.cuda.Stream(dev)
+        queued = phases * steps_per_phase
+
+        def feed():
+            torch.cuda.set_device(local)
+            for s in range(queued):
+                for a in range(n_a):
+                    sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
+
+        feeder = threading.Thread(target=feed, daemon=True)
+        feeder.start()
     else:
         shared = SharedExpert(dev)
         gen = torch.Generator(device=dev).manual_seed(rank)
-        x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
-        ids, w = make_routing(T, 10 + rank, dev)
+        x_all = torch.randn(T_max, H, device=dev, generator=gen).to(torch.bfloat16)
         send_stream = torch.cuda.Stream(dev)
         stream = torch.cuda.current_stream()
 
-        def step(xx=x, ii=ids, ww=w):
-            send_stream.wait_stream(stream)
-            t = channel.send(0, 0, xx.data_ptr(), ii.data_ptr(), ww.data_ptr(), T, send_stream.cuda_stream)
-            s = shared(xx)
-            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-            channel.combine(t, out.data_ptr(), stream.cuda_stream, s.data_ptr())
-            return out
-
     def timed(fn, finish=None):
-        # F ranks never synchronize here: their GPU holds every job of the run, each waiting for its doorbell
         for _ in range(args.warmup):
             fn()
         if is_a:
@@ -487,38 +607,122 @@ def run_multi(args):
         dist.barrier()
         return float(mt.item())
 
-    with ClockSampler(local) as clocks:
-        ms = timed(step if is_a else (lambda: None))
+    results = []
+    clock_summary = None
+    for T in t_list:
+        if is_a:
+            x = x_all[:T]
+            ids, w = (zipf_routing(T, 10 + rank, dev) if args.routing == "zipf" else make_routing(T, 10 + rank, dev))
+
+            def step(xx=x, ii=ids, ww=w, TT=T):
+                send_stream.wait_stream(stream)
+                t = channel.send(0, 0, xx.data_ptr(), ii.data_ptr(), ww.data_ptr(), TT, send_stream.cuda_stream)
+                s = shared(xx)
+                out = torch.empty(TT, H, dtype=torch.bfloat16, device=dev)
+                channel.combine(t, out.data_ptr(), stream.cuda_stream, s.data_ptr())
+                return out
+        with ClockSampler(local) as clocks:
+            ms = timed(step if is_a else (lambda: None))
+        clock_summary = clocks.summary()
+        res = {"T": T, "ms": ms}
+        if is_a:
+            channel.check()
+            counts = channel.dispatch_info(0, stream.cuda_stream)["counts"]
+        else:
+            counts = None
+        allc = [None] * world
+        dist.all_gather_object(allc, counts)
+        per_f = [sum(c[f] for c in allc[:n_a]) for f in range(n_f)]
+        res["f_rows"] = per_f
+        if not sweep:
+            if is_a:
+                pipe = HostPipeline(x, ids, w, dev, lambda dx, di, dw: step(dx, di, dw))
+
+                def e2e_step():
+                    pipe.run(1)
+            res["e2e_ms"] = timed(e2e_step if is_a else (lambda: None), pipe.finish if is_a else None)
+        results.append(res)
+    if feeder is not None:
+        feeder.join()
+    torch.cuda.synchronize()  # F: every queued job has now been answered
     if is_a:
         channel.check()
-        pipe = HostPipeline(x, ids, w, dev, lambda dx, di, dw: step(dx, di, dw))
-
-        def e2e_step():
-            pipe.run(1)
-    e2e_ms = timed(e2e_step if is_a else (lambda: None), pipe.finish if is_a else None)
-    torch.cuda.synchronize()  # F: every queued job has now been answered
+    else:
+        sched.check()
+    # doorbell latency: one message at a time from A rank 0, F ranks idle and already spinning on their doorbell
+    lat = []
+    seq_next = phases * steps_per_phase + 1
+    for r in range(lat_iters):
+        T = t_list[0]
+        if not is_a:
+            sched.run_device_wait(0, 0, seq_next + r, 0, stream.cuda_stream)
+        dist.barrier()
+        info = None
+        if rank == 0:
+            ids, w = zipf_routing(T, 10, dev) if args.routing == "zipf" else make_routing(T, 10, dev)
+            step(x_all[:T], ids, w, T)
+            torch.cuda.synchronize()
+            info = channel.dispatch_info(0, stream.cuda_stream)
+        elif not is_a:
+            torch.cuda.synchronize()
+            info = sched.job_info(stream.cuda_stream)
+        infos = [None] * world
+        dist.all_gather_object(infos, info)
+        if rank == 0:
+            a0 = infos[0]
+            fi = [i for i in infos[n_a:]]
+            busy = [(i["t_reply_ns"] - i["t_seen_ns"]) * 1e-3 for i in fi]
+            rt = (a0["t_replies_ns"] - a0["t_ring_ns"]) * 1e-3
+            lat.append({"round_trip_us": rt, "f_busy_us": busy, "signal_us": rt - max(busy),
+                        "ring_to_seen_cross_clock_us": [(i["t_seen_ns"] - a0["t_ring_ns"]) * 1e-3 for i in fi]})
     if is_a:
         channel.check()
     else:
         sched.check()
     dist.barrier()
     if rank == 0:
-        h2d = T * H * 2 + T * K_TOP * 8
-        line = {
-            "metric": METRIC, "value": round(n_a * T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport",
-            "data": "synthetic",
-            "config": {"workload": f"{n_a}A{n_f}F: config 2 layer per A replica (T=16384, H=7168, 256 experts, "
-                                   "top-8 sigmoid, I=2048, MXFP4, 1 bf16 shared expert)", "tokens_per_replica": T,
-                       "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
-                       "expert_bounds": bounds, "l2": "inputs larger than L2, no flush"},
-            "e2e": {"value": round(n_a * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": n_a * h2d,
-                    "d2h_bytes_per_step": n_a * T * H * 2, "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": args.steps * (4 * n_a + 8 * n_a * n_f),
-            "roofline": None, "cpu_baseline": None, "clocks": clocks.summary(),
+        h2d = T_max * H * 2 + T_max * K_TOP * 8
+        base = {
+            "metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport", "data": "synthetic",
+            "gpu_launches": args.steps * (4 * n_a + 8 * n_a * n_f), "roofline": None, "cpu_baseline": None,
+            "clocks": clock_summary,
         }
-        print(json.dumps(line), flush=True)
+        for res in results:
+            T, ms = res["T"], res["ms"]
+            mean_f = sum(res["f_rows"]) / n_f
+            line = dict(base, value=round(n_a * T / (ms * 1e-3), 1), ms_per_step=round(ms, 4))
+            line["config"] = {
+                "workload": (f"{n_a}A{n_f}F: config 2 layer per A replica (T={T}, H=7168, 256 experts, "
+                             f"top-8 {'Zipf(s=1.2) popularity' if args.routing == 'zipf' else 'sigmoid'}, I=2048, "
+                             "MXFP4, 1 bf16 shared expert)"),
+                "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
+                "expert_bounds": bounds, "routing": args.routing, "l2": "inputs larger than L2, no flush"
+                if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
+            line["f_rows"] = res["f_rows"]
+            line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
+            if "e2e_ms" in res:
+                e = res["e2e_ms"]
+                line["e2e"] = {"value": round(n_a * T / (e * 1e-3), 1), "unit": "tokens/s",
+                               "h2d_bytes_per_step": n_a * h2d, "d2h_bytes_per_step": n_a * T * H * 2,
+                               "ms_per_step": round(e, 4)}
+            else:
+                line["e2e"] = None
+            if sweep:
+                line["workload_mode"] = "zipf-sweep"
+            print(json.dumps(line), flush=True)
+        if lat:
+            print(json.dumps({"workload_mode": "doorbell-latency", "n_gpus": world, "parallelism": f"{n_a}A{n_f}F",
+                              "tokens": t_list[0], "iters": len(lat),
+                              "round_trip_us_p50": round(statistics.median(l["round_trip_us"] for l in lat), 2),
+                              "signal_us_p50": round(statistics.median(l["signal_us"] for l in lat), 2),
+                              "f_busy_us_p50": round(statistics.median(max(l["f_busy_us"]) for l in lat), 2),
+                              "ring_to_seen_cross_clock_us_p50": round(statistics.median(
+                                  min(l["ring_to_seen_cross_clock_us"]) for l in lat), 2),
+                              "note": "signal = A round trip (doorbell release -> combine saw every done flag, A "
+                                      "clock) - slowest F's busy time (doorbell seen -> done flag released, F clock): "
+                                      "one doorbell plus one done-flag hop; no cross-GPU clock needed"}), flush=True)
     # orderly shutdown: every process unmaps its peers' memory before any process frees its own
     dist.barrier()
     if is_a:
@@ -548,14 +752,24 @@ def main():
     ap.add_argument("--cpu-experts", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", choices=("layer", "zipf-sweep"), default="layer",
+                    help="zipf-sweep: T in 256/1024/4096/16384 with skewed routing (config 5), one line per T")
+    ap.add_argument("--routing", choices=("sigmoid", "zipf"), default=None,
+                    help="default: sigmoid for the layer workload, zipf for the sweep")
+    ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
+    ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
     args = ap.parse_args()
     E = args.experts
     if args.warmup < 3:
         args.warmup = 3
+    if args.routing is None:
+        args.routing = "zipf" if args.workload == "zipf-sweep" else "sigmoid"
     if args.impl == "reference":
         run_reference(args)
     elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_multi(args)
+    elif args.workload == "zipf-sweep":
+        run_sweep(args)
     else:
         run_single(args)
 

@@ -141,6 +141,12 @@ int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n
                  uint64_t route_ws, uint64_t shared, uint64_t out, uint64_t status, uint64_t timeout_ns,
                  void* stream);
 
+/* Read back a routing workspace after a dispatch and its combine (debug/measurement): the row count announced to
+ * each F rank, the globaltimer (ns) at which the doorbells were released and the one at which asap_combine's wait
+ * saw every done flag. Synchronizes `stream`. */
+int asap_dispatch_info(uint64_t route_ws, int32_t num_f, int32_t* counts, uint64_t* t_ring_ns,
+                       uint64_t* t_replies_ns, void* stream);
+
 /* Allocation-free asap_dispatch (no counterpart in the reference).  Some callers cannot allocate device memory:
  * an attention rank whose free memory SGLang has already handed to the KV-cache pool, or a host that binds this
  * ABI from another language and only holds the transport's mapped arenas.  This entry point needs no routing
@@ -218,9 +224,11 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable);
 int asap_ffn_last_timing(uint64_t ws_handle, float* ms, int32_t n);
 
-/* Read back the job descriptor (debug/tests): n, layer, seq, epoch, valid. Synchronizes `stream`. */
+/* Read back the job descriptor (debug/measurement): n, layer, seq, epoch, valid, the globaltimer (ns) at which
+ * asap_ffn_wait saw the doorbell (0 when the job was posted by the host) and the one at which the reply's done
+ * flag was released. Synchronizes `stream`. */
 int asap_ffn_job_info(uint64_t ws_handle, int32_t* n, int32_t* layer_id, uint32_t* seq, int32_t* epoch,
-                      int32_t* valid, void* stream);
+                      int32_t* valid, uint64_t* t_seen_ns, uint64_t* t_reply_ns, void* stream);
 
 /* Per-local-expert token-pair counts of the last job (int32 [num_local]) and the expert-major
  * permutation (int32 [n, topk] permuted row of pair (t, j), -1 when not local). Debug/tests; these are

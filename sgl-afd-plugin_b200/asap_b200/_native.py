@@ -85,7 +85,10 @@ _SIGS = {
     "asap_ffn_enable_timing": (c_int32, [c_uint64, c_int32]),
     "asap_ffn_last_timing": (c_int32, [c_uint64, POINTER(c_float), c_int32]),
     "asap_ffn_job_info": (c_int32, [c_uint64, POINTER(c_int32), POINTER(c_int32), POINTER(c_uint32),
-                                    POINTER(c_int32), POINTER(c_int32), c_void_p]),
+                                    POINTER(c_int32), POINTER(c_int32), POINTER(c_uint64), POINTER(c_uint64),
+                                    c_void_p]),
+    "asap_dispatch_info": (c_int32, [c_uint64, c_int32, POINTER(c_int32), POINTER(c_uint64), POINTER(c_uint64),
+                                     c_void_p]),
     "asap_ffn_debug_ptrs": (c_int32, [c_uint64] + [POINTER(c_uint64)] * 7),
 }
 

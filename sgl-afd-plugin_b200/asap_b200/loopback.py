@@ -25,11 +25,12 @@ from .transport.server import FfnServer
 
 class LocalFfn:
     """The F ranks of a loopback deployment, driven from the A rank's send/recv calls; their jobs run one after
-    the other on one stream."""
+    the other on one stream.  That stream has the highest priority: the F chain is the critical path of the step,
+    so its kernels take SMs ahead of A-side work queued beside them (the shared expert)."""
 
     def __init__(self, schedulers: List[FfnScheduler], a: int, slots: int, device: int):
         self.scheds, self.a, self.device = schedulers, a, device
-        self.stream = torch.cuda.Stream(device)
+        self.stream = torch.cuda.Stream(device, priority=-1)
         self.sent = [torch.cuda.Event() for _ in range(slots)]
         self.done = [torch.cuda.Event() for _ in range(slots)]
 

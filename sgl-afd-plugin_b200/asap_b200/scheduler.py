@@ -188,7 +188,9 @@ class FfnScheduler:
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
         n, layer, epoch, valid = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
-        seq = ctypes.c_uint32()
+        seq, t_seen, t_reply = ctypes.c_uint32(), ctypes.c_uint64(), ctypes.c_uint64()
         N.call("asap_ffn_job_info", self.ws_handle, ctypes.byref(n), ctypes.byref(layer), ctypes.byref(seq),
-               ctypes.byref(epoch), ctypes.byref(valid), ctypes.c_void_p(stream))
-        return {"n": n.value, "layer": layer.value, "seq": seq.value, "epoch": epoch.value, "valid": valid.value}
+               ctypes.byref(epoch), ctypes.byref(valid), ctypes.byref(t_seen), ctypes.byref(t_reply),
+               ctypes.c_void_p(stream))
+        return {"n": n.value, "layer": layer.value, "seq": seq.value, "epoch": epoch.value, "valid": valid.value,
+                "t_seen_ns": t_seen.value, "t_reply_ns": t_reply.value}

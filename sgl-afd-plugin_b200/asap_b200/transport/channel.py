@@ -209,6 +209,16 @@ class AttnChannel:
     def route_ws(self, slot: int) -> torch.Tensor:
         return self._route_ws[slot]
 
+    def dispatch_info(self, slot: int, stream: int) -> dict:
+        """Rows announced to each F rank by the last dispatch on ``slot``, the device time (globaltimer ns) its
+        doorbells were released and the one at which the combine's wait saw every reply (synchronizes
+        ``stream``)."""
+        counts = (ctypes.c_int32 * self.g.num_f)()
+        t, t_back = ctypes.c_uint64(), ctypes.c_uint64()
+        N.call("asap_dispatch_info", self._ws_ptr(slot), self.g.num_f, counts, ctypes.byref(t), ctypes.byref(t_back),
+               ctypes.c_void_p(stream))
+        return {"counts": list(counts), "t_ring_ns": t.value, "t_replies_ns": t_back.value}
+
     def _ws_ptr(self, slot: int) -> int:
         return self._route_ws[slot].data_ptr()
 

@@ -27,8 +27,10 @@ int sm_count();
 struct JobDesc {
   int32_t n, layer, epoch, valid;
   uint32_t seq;
-  uint32_t sync;  // arrive counter of the finalize grid
-  uint32_t pad[10];
+  uint32_t sync;     // arrive counter of the finalize grid
+  uint64_t t_seen;   // globaltimer (ns) when the doorbell wait saw the message (0: posted by the host)
+  uint64_t t_reply;  // globaltimer (ns) when the reply's done flag was released
+  uint32_t pad[6];
 };
 static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
 
@@ -98,6 +100,7 @@ __global__ void ffn_wait_kernel(JobDesc* d, const uint64_t* bell, uint32_t last_
     __nanosleep(64);
   }
   asm volatile("fence.acq_rel.sys;" ::: "memory");
+  d->t_seen = globaltimer_ns();
   const uint32_t seq = (uint32_t)word;
   const int32_t n = (int32_t)((word >> 32) & kMaxTokens);
   const int32_t layer = (int32_t)((word >> 49) & kMaxLayer);
@@ -123,6 +126,7 @@ __global__ void ffn_post_kernel(JobDesc* d, uint32_t seq, int32_t n, int32_t lay
   d->layer = layer;
   d->epoch = epoch;
   d->sync = 0;
+  d->t_seen = 0;
   d->valid = 1;
 }
 
@@ -711,9 +715,12 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
     last = (atomicAdd(&p.desc_rw->sync, 1u) == gridDim.x - 1);
   }
   __syncthreads();
-  if (last && threadIdx.x == 0 && p.reply_done) {
-    __threadfence_system();
-    st_release_sys_u32(p.reply_done, p.desc->seq);
+  if (last && threadIdx.x == 0) {
+    p.desc_rw->t_reply = globaltimer_ns();
+    if (p.reply_done) {
+      __threadfence_system();
+      st_release_sys_u32(p.reply_done, p.desc->seq);
+    }
   }
 }
 
@@ -1095,7 +1102,7 @@ int asap_ffn_last_timing(uint64_t ws_handle, float* ms, int32_t n) {
 }
 
 int asap_ffn_job_info(uint64_t ws_handle, int32_t* n, int32_t* layer_id, uint32_t* seq, int32_t* epoch,
-                      int32_t* valid, void* stream) {
+                      int32_t* valid, uint64_t* t_seen_ns, uint64_t* t_reply_ns, void* stream) {
   WsHandle* w = get_ws(ws_handle);
   if (!w) {
     set_error("asap_ffn_job_info: unknown workspace handle");
@@ -1109,6 +1116,8 @@ int asap_ffn_job_info(uint64_t ws_handle, int32_t* n, int32_t* layer_id, uint32_
   if (seq) *seq = d.seq;
   if (epoch) *epoch = d.epoch;
   if (valid) *valid = d.valid;
+  if (t_seen_ns) *t_seen_ns = d.t_seen;
+  if (t_reply_ns) *t_reply_ns = d.t_reply;
   return ASAP_OK;
 }
 

@@ -57,9 +57,11 @@ static int check_geometry(const asap_geometry_t* g) {
 // [0, 256)      int32 count[ASAP_MAX_F]  (rows announced to F rank f, >= 1)
 // [256, 320)    int32 pad[ASAP_MAX_F]    (1 when f received no token and gets one row of ids -1)
 // [320, 384)    uint32 arrive counter of the pack grid
-// [384, 512)    reserved
+// [384, 392)    uint64 globaltimer (ns) when the doorbells were released
+// [392, 400)    uint64 globaltimer (ns) when the combine's wait saw every done flag
+// [400, 512)    reserved
 // [512, ...)    int32 row_of[num_f][n_max]: compacted row of token t in f's region, -1 if not routed
-constexpr uint64_t kWsCount = 0, kWsPad = 256, kWsSync = 320, kWsRows = 512;
+constexpr uint64_t kWsCount = 0, kWsPad = 256, kWsSync = 320, kWsRing = 384, kWsRows = 512;
 
 // K1: one CTA. Backpressure wait, then the per-F-rank compacted row index of every token (ascending token
 // order, a stable compaction).
@@ -257,6 +259,7 @@ __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constan
   if (last && threadIdx.x < F) {
     __threadfence_system();
     const int f = threadIdx.x;
+    if (f == 0) *reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(p.ws) + kWsRing) = globaltimer_ns();
     st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.bell[f]) + bell_off(g, p.a, p.slot)),
                        pack_doorbell(p.seq, (uint32_t)count[f], (uint32_t)p.layer_id, p.epoch[f]));
   }
@@ -324,17 +327,20 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ Co
 }
 
 __global__ void wait_replies_kernel(asap_geometry_t g, int32_t slot, uint32_t seq, const uint8_t* result,
-                                    uint64_t status, uint64_t timeout_ns) {
-  if (threadIdx.x >= g.num_f) return;
-  const uint32_t* done = reinterpret_cast<const uint32_t*>(result + done_off(g, threadIdx.x, slot));
-  const uint64_t deadline = globaltimer_ns() + timeout_ns;
-  while ((int32_t)(ld_acquire_sys_u32(done) - seq) < 0) {
-    if (globaltimer_ns() > deadline) {
-      report(status, status_word(ASAP_ST_REPLY_TIMEOUT, threadIdx.x, slot, seq));
-      return;
+                                    uint64_t status, uint64_t timeout_ns, uint64_t* t_seen) {
+  if (threadIdx.x < g.num_f) {
+    const uint32_t* done = reinterpret_cast<const uint32_t*>(result + done_off(g, threadIdx.x, slot));
+    const uint64_t deadline = globaltimer_ns() + timeout_ns;
+    while ((int32_t)(ld_acquire_sys_u32(done) - seq) < 0) {
+      if (globaltimer_ns() > deadline) {
+        report(status, status_word(ASAP_ST_REPLY_TIMEOUT, threadIdx.x, slot, seq));
+        break;
+      }
+      __nanosleep(64);
     }
-    __nanosleep(128);
   }
+  __syncwarp();
+  if (threadIdx.x == 0 && t_seen) *t_seen = globaltimer_ns();
 }
 
 __global__ void write32_kernel(uint32_t* p, uint32_t v) {
@@ -622,12 +628,28 @@ int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n
   p.out = (__nv_bfloat16*)out;
   p.status = status;
   p.timeout_ns = timeout_ns;
-  wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns);
+  wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns,
+                                                          reinterpret_cast<uint64_t*>(route_ws + kWsRing + 8));
   ASAP_CHECK_LAUNCH("wait_replies_kernel");
   const int warps = 8;
   int blocks = std::min((n + warps - 1) / warps, sm_count() * 4);
   combine_kernel<<<blocks, warps * 32, 0, (cudaStream_t)stream>>>(p);
   ASAP_CHECK_LAUNCH("combine_kernel");
+  return ASAP_OK;
+}
+
+int asap_dispatch_info(uint64_t route_ws, int32_t num_f, int32_t* counts, uint64_t* t_ring_ns,
+                       uint64_t* t_replies_ns, void* stream) {
+  if (!route_ws || num_f < 1 || num_f > ASAP_MAX_F) {
+    set_error("asap_dispatch_info: NULL workspace or num_f %d outside [1, %d]", num_f, ASAP_MAX_F);
+    return ASAP_EINVAL;
+  }
+  uint8_t head[kWsRows];
+  ASAP_CUDA(cudaMemcpyAsync(head, (const void*)route_ws, kWsRows, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  ASAP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  if (counts) memcpy(counts, head + kWsCount, sizeof(int32_t) * num_f);
+  if (t_ring_ns) memcpy(t_ring_ns, head + kWsRing, sizeof(uint64_t));
+  if (t_replies_ns) memcpy(t_replies_ns, head + kWsRing + 8, sizeof(uint64_t));
   return ASAP_OK;
 }
 
@@ -639,7 +661,8 @@ int asap_wait_replies(const asap_geometry_t* g, int32_t slot, uint32_t seq, uint
     set_error("asap_wait_replies: slot %d outside the geometry or NULL result", slot);
     return ASAP_EINVAL;
   }
-  wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns);
+  wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns,
+                                                          nullptr);
   ASAP_CHECK_LAUNCH("wait_replies_kernel");
   return ASAP_OK;
 }

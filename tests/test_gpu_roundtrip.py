@@ -215,3 +215,46 @@ def test_uneven_six_f_ranks(cuda_ok):
         lb.close()
         for d in per_f:
             d[3].release()
+
+
+def test_zipf_skew_four_f_ranks_and_timestamps(cuda_ok):
+    """Routing skew (config 5's shape, scaled down): Zipf(s=1.2) expert popularity over a seeded permutation of 32
+    experts, top-8 without replacement, 4 F ranks of 8 -- the most popular expert takes most tokens (a segment of
+    several 128-row tiles), some experts none.  Per-F row counts announced by the dispatch, per-expert counts
+    (bit-exact) and the output (rel L2) against the oracle; the device timestamps are ordered."""
+    rng = np.random.default_rng(11)
+    T, H, I, k, E_, n_f = 700, 256, 128, 8, 32, 4
+    per_f = [{0: Mxfp4Experts.random(8, H, I, expert_base=8 * f, seed=30 + f)} for f in range(n_f)]
+    bounds = [0, 8, 16, 24, 32]
+    lb = Loopback(Geometry(1, 1, 2, T, H, k, n_f), per_f, timeout_s=5.0)
+    lb.install()
+    try:
+        ow = [experts_to_oracle(d[0]) for d in per_f]
+        logp = np.empty(E_)
+        logp[rng.permutation(E_)] = -1.2 * np.log(np.arange(1, E_ + 1))
+        scores = logp[None, :] - np.log(-np.log(rng.uniform(1e-12, 1.0, (T, E_))))
+        ids = np.argsort(-scores, axis=1)[:, :k].astype(np.int32)
+        w = 1.0 / (1.0 + np.exp(-rng.standard_normal((T, k))))
+        w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+        x = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        got = run_layer(lb, 0, x, ids, w)
+        ref = moe.round_trip(x, ids, w, bounds, ow)
+        assert moe.rel_l2(got, ref) < TOL
+        tables = moe.f_rank_tables(ids, bounds)[0]
+        stream = torch.cuda.current_stream().cuda_stream
+        info = lb.channel.dispatch_info(0, stream)
+        assert info["counts"] == [int((tables[f] >= 0).sum()) for f in range(n_f)]
+        top = np.bincount(ids.ravel(), minlength=E_).max()
+        assert top > 3 * 128  # the skew really spans several tiles of one expert
+        for f in range(n_f):
+            sel = tables[f] >= 0
+            c = lb.scheds[f].debug_tensors()["expert_counts"].cpu().numpy()
+            np.testing.assert_array_equal(c, moe.expert_counts(ids[sel], bounds[f], 8))
+        jobs = [sc.job_info(stream) for sc in lb.scheds]
+        assert 0 < info["t_ring_ns"] <= jobs[0]["t_seen_ns"]
+        for j in jobs:
+            assert j["t_seen_ns"] <= j["t_reply_ns"] <= info["t_replies_ns"]
+    finally:
+        lb.close()
+        for d in per_f:
+            d[0].release()
