@@ -33,6 +33,18 @@ sys.path.insert(0, ROOT)
 
 METRIC = "MoE layer tokens/s A->F->A (DeepSeek-V3-shape MXFP4 layer, T=16384 per A replica)"
 H, I, E, K_TOP, T_DEFAULT = 7168, 2048, 256, 8, 16384
+ROUTING, KIND, SHARED = "sigmoid", "mxfp4", True
+LAYERS = {
+    # config 2: DeepSeek-V3 shape, MXFP4 experts, top-8 sigmoid, one bf16 shared expert on the A side
+    "layer": dict(H=7168, I=2048, E=256, K_TOP=8, T_DEFAULT=16384, ROUTING="sigmoid", KIND="mxfp4", SHARED=True,
+                  METRIC=METRIC),
+    # config 4: FP8 E4M3 experts with fp32 128x128 block scales, H=8192, I=3584, 64 experts, top-6 softmax
+    "fp8-layer": dict(H=8192, I=3584, E=64, K_TOP=6, T_DEFAULT=8192, ROUTING="softmax", KIND="fp8", SHARED=False,
+                      METRIC="MoE layer tokens/s A->F->A (FP8 block-scaled layer: H=8192, 64 experts, top-6, I=3584, "
+                             "T=8192 per A replica)"),
+}
+DTYPE = {"mxfp4": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport",
+         "fp8": "e4m3 x e4m3 (fp32 block-scale promotion per 128-deep K block), bf16 transport"}
 SWEEP_T = [256, 1024, 4096, 16384]
 ZIPF_S = 1.2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -103,11 +115,13 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------------------------ workload
 def make_routing(T, seed, device):
+    """Top-k of N(0,1) router logits: sigmoid scores (config 2) or softmax probabilities (config 4), the selected
+    weights renormalised to sum 1."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
     logits = torch.randn(T, E, device=device, generator=g)
-    scores = torch.sigmoid(logits)
+    scores = torch.sigmoid(logits) if ROUTING == "sigmoid" else torch.softmax(logits, dim=1)
     w, ids = torch.topk(scores, K_TOP, dim=1)
     w = w / w.sum(1, keepdim=True)
     return ids.to(torch.int32).contiguous(), w.float().contiguous()
@@ -129,6 +143,17 @@ def zipf_routing(T, seed, device, s=ZIPF_S, perm_seed=1234):
     w = torch.sigmoid(torch.randn(T, K_TOP, device=device, generator=g))
     w = w / w.sum(1, keepdim=True)
     return ids.to(torch.int32).contiguous(), w.float().contiguous()
+
+
+def make_experts(P, expert_base, seed, device="cuda"):
+    """Seeded synthetic routed experts of the selected layer: MXFP4 (uniform E2M1 codes, E8M0 scales 2^-10..2^-7)
+    or FP8 (N(0, 0.02) weights block-quantised to E4M3 with fp32 128x128 scales)."""
+    from asap_b200.experts import Fp8Experts, Mxfp4Experts
+
+    if KIND == "fp8":
+        return Fp8Experts.random(P, H, I, expert_base=expert_base, seed=seed, device=device)
+    return Mxfp4Experts.random(P, H, I, expert_base=expert_base, seed=seed, scale_lo=117, scale_hi=120,
+                               device=device)
 
 
 def topology(name, world):
@@ -241,10 +266,10 @@ def run_single(args):
     dev = "cuda:0"
     torch.cuda.set_device(0)
     T = args.tokens
-    experts = Mxfp4Experts.random(E, H, I, seed=1, scale_lo=117, scale_hi=120)
+    experts = make_experts(E, 0, 1, dev)
     lb = Loopback(Geometry(1, 1, 2, T, H, K_TOP, 1), {0: experts}, timeout_s=30.0)
     lb.install()
-    shared = SharedExpert(dev)
+    shared = SharedExpert(dev) if SHARED else (lambda _x: None)
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
     ids, w = make_routing(T, 3, dev)
@@ -325,25 +350,31 @@ def run_single(args):
     g1_flops, g2_flops = gemm_flops(pairs)
     fp8_peak = 2.0 * peaks["bf16_tflops_sustained"]  # kind::f8f6f4 runs at twice the bf16 rate
     achieved = g1_flops / (kernel_ms["gemm1"] * 1e-3) / 1e12
-    traffic = load_traffic("gemm1", pairs)
+    traffic = load_traffic("gemm1" if KIND == "mxfp4" else "gemm1_fp8", pairs)
     cpu = cpu_baseline(args.cpu_experts) if not args.no_cpu else None
     clk = clocks.summary()
     nvlink_bytes_dispatch = T * (2 * H + 8 * K_TOP)
+    workload = (f"1 GPU loopback A+F: config 2 layer (T={T}, H=7168, {E} experts, top-8 sigmoid, I=2048, MXFP4 "
+                "weights, 1 bf16 shared expert)" if KIND == "mxfp4" else
+                f"1 GPU loopback A+F: config 4 layer (T={T}, H={H}, {E} experts, top-{K_TOP} softmax, I={I}, FP8 E4M3 "
+                "weights with fp32 128x128 block scales, no shared expert)")
     line = {
         "metric": METRIC, "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport", "data": "synthetic",
-        "config": {"workload": f"1 GPU loopback A+F: config 2 layer (T={T}, H=7168, {E} experts, top-8 sigmoid, "
-                               "I=2048, MXFP4 weights, 1 bf16 shared expert)", "tokens_per_replica": T,
+        "vs_baseline": None, "dtype": DTYPE[KIND], "data": "synthetic",
+        "config": {"workload": workload, "tokens_per_replica": T,
                    "a_replicas": 1, "f_ranks": 1, "parallelism": "1A1F loopback",
-                   "l2": "inputs larger than L2 (x 235 MB, weights 6.0 GB), no flush"},
+                   "l2": f"inputs larger than L2 (x {T * H * 2 / 1e6:.0f} MB, weights {experts.nbytes / 1e9:.1f} GB), "
+                         "no flush"},
         "e2e": e2e,
         "gpu_launches": args.steps * 12,
-        "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)", "bound": "tensor",
+        "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)" if KIND == "mxfp4" else
+                     "moe_gemm_fp8_kernel<0> (GEMM1, block-scale promotion + SwiGLU + FP8 requant)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / fp8_peak, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained x 2 (FP8-rate tensor kind)",
-                     "frac_of_fp4_dense_nominal": round(achieved / 9000.0, 4)},
+                     "frac_of_fp4_dense_nominal" if KIND == "mxfp4" else "frac_of_fp8_dense_nominal":
+                         round(achieved / (9000.0 if KIND == "mxfp4" else 4500.0), 4)},
         "kernels_ms": {k: round(v, 4) for k, v in kernel_ms.items()},
         "dispatch_ms": round(statistics.median(dsp), 4), "combine_ms": round(statistics.median(cmb), 4),
         "dispatch_gbs_algorithmic": round(nvlink_bytes_dispatch / (statistics.median(dsp) * 1e-3) / 1e9, 1),
@@ -369,9 +400,10 @@ def load_traffic(kernel, pairs):
 
 # ------------------------------------------------------------------------------------------ CPU baseline
 def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0):
-    """The oracle (the reference's torch semantics restated in numpy, with the same MXFP8 activation rounding)
-    on the host cores: every (token, slot) pair of the T=16384 layer that routes to experts [0, n_experts),
-    dequantised MXFP4 weights (dequantisation not timed).  tokens/s counts pairs / top-k."""
+    """The oracle (the reference's torch semantics restated in numpy, with the same activation rounding as the
+    GPU path: MXFP8 for config 2, E4M3 per 1x128 for config 4) on the host cores: every (token, slot) pair of the
+    layer that routes to experts [0, n_experts), dequantised weights (dequantisation not timed).  tokens/s counts
+    pairs / top-k."""
     import numpy as np
 
     from oracle import moe, mx
@@ -380,28 +412,40 @@ def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0):
     rng = np.random.default_rng(seed)
     T = T_DEFAULT
     logits = rng.standard_normal((T, E))
-    ids, w = moe.topk_routing(logits, K_TOP, "sigmoid")
+    ids, w = moe.topk_routing(logits, K_TOP, ROUTING)
     sel = np.any(ids < n_experts, axis=1)
     x = mx.bf16_round(rng.standard_normal((int(sel.sum()), H)).astype(np.float32))
     P = n_experts
-    codes13 = rng.integers(0, 256, (P, 2 * I, H // 2), dtype=np.uint8)
-    sf13 = rng.integers(117, 121, (P, 2 * I * H // 32), dtype=np.uint8)
-    codes2 = rng.integers(0, 256, (P, H, I // 2), dtype=np.uint8)
-    sf2 = rng.integers(117, 121, (P, H * I // 32), dtype=np.uint8)
-    gate, up = moe.dequant_w13(codes13, sf13, P, H, I)
-    w2 = moe.dequant_w2(codes2, sf2, P, H, I)
+    if KIND == "fp8":
+        # E4M3 codes with magnitudes 2^-1 .. 2^3 and random signs, one scale per 128x128 block
+        q13 = (rng.integers(0x30, 0x50, (P, 2 * I, H), dtype=np.uint8) | (rng.integers(0, 2, (P, 2 * I, H),
+                                                                                       dtype=np.uint8) << 7))
+        q2 = rng.integers(0x30, 0x50, (P, H, I), dtype=np.uint8) | (rng.integers(0, 2, (P, H, I), dtype=np.uint8) << 7)
+        s13 = rng.uniform(0.002, 0.01, (P, 2 * I // 128, H // 128)).astype(np.float32)
+        s2 = rng.uniform(0.002, 0.01, (P, H // 128, I // 128)).astype(np.float32)
+        gate, up, w2 = moe.dequant_fp8(q13, s13, q2, s2)
+        act = "fp8"
+    else:
+        codes13 = rng.integers(0, 256, (P, 2 * I, H // 2), dtype=np.uint8)
+        sf13 = rng.integers(117, 121, (P, 2 * I * H // 32), dtype=np.uint8)
+        codes2 = rng.integers(0, 256, (P, H, I // 2), dtype=np.uint8)
+        sf2 = rng.integers(117, 121, (P, H * I // 32), dtype=np.uint8)
+        gate, up = moe.dequant_w13(codes13, sf13, P, H, I)
+        w2 = moe.dequant_w2(codes2, sf2, P, H, I)
+        act = True
     pairs = int(np.sum(ids[sel] < n_experts))
     times = []
     for i in range(warmup + steps):
         t = time.perf_counter()
-        moe.ffn_rank(x, ids[sel], w[sel], gate, up, w2, 0, P, act_quant=True)
+        moe.ffn_rank(x, ids[sel], w[sel], gate, up, w2, 0, P, act_quant=act)
         if i >= warmup:
             times.append(time.perf_counter() - t)
     dt = statistics.median(times)
+    cfg = "config-2" if KIND == "mxfp4" else "config-4"
     return {"value": round(pairs / K_TOP / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"all {pairs} (token, expert) pairs of the T=16384 config-2 layer that route to experts "
-                      f"0..{n_experts - 1} (numpy oracle, MXFP8 activation emulation, {cores} host threads); "
-                      f"tokens = pairs / top-k; {dt:.2f} s per sample"}
+            "sample": f"all {pairs} (token, expert) pairs of the T={T} {cfg} layer that route to experts "
+                      f"0..{n_experts - 1} (numpy oracle, {'FP8 1x128' if act == 'fp8' else 'MXFP8'} activation "
+                      f"emulation, {cores} host threads); tokens = pairs / top-k; {dt:.2f} s per sample"}
 
 
 def run_reference(args):
@@ -422,7 +466,8 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
             "data": "synthetic",
-            "config": {"workload": "config 2 layer, bounded CPU sample", "tokens_per_replica": T_DEFAULT},
+            "config": {"workload": f"{'config 2' if KIND == 'mxfp4' else 'config 4'} layer, bounded CPU sample",
+                       "tokens_per_replica": T_DEFAULT},
             "cpu_baseline": {**last, "value": v},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -553,8 +598,7 @@ def run_multi(args):
     ep = None
     if not is_a:
         f = rank - n_a
-        experts = Mxfp4Experts.random(bounds[f + 1] - bounds[f], H, I, expert_base=bounds[f], seed=100 + f,
-                                      scale_lo=117, scale_hi=120, device=dev)
+        experts = make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + f, dev)
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
         sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s)
@@ -579,7 +623,7 @@ def run_multi(args):
         feeder = threading.Thread(target=feed, daemon=True)
         feeder.start()
     else:
-        shared = SharedExpert(dev)
+        shared = SharedExpert(dev) if SHARED else None
         gen = torch.Generator(device=dev).manual_seed(rank)
         x_all = torch.randn(T_max, H, device=dev, generator=gen).to(torch.bfloat16)
         send_stream = torch.cuda.Stream(dev)
@@ -617,9 +661,9 @@ def run_multi(args):
             def step(xx=x, ii=ids, ww=w, TT=T):
                 send_stream.wait_stream(stream)
                 t = channel.send(0, 0, xx.data_ptr(), ii.data_ptr(), ww.data_ptr(), TT, send_stream.cuda_stream)
-                s = shared(xx)
+                s = shared(xx) if shared is not None else None
                 out = torch.empty(TT, H, dtype=torch.bfloat16, device=dev)
-                channel.combine(t, out.data_ptr(), stream.cuda_stream, s.data_ptr())
+                channel.combine(t, out.data_ptr(), stream.cuda_stream, s.data_ptr() if s is not None else 0)
                 return out
         with ClockSampler(local) as clocks:
             ms = timed(step if is_a else (lambda: None))
@@ -685,7 +729,7 @@ def run_multi(args):
         base = {
             "metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport", "data": "synthetic",
+            "dtype": DTYPE[KIND], "data": "synthetic",
             "gpu_launches": args.steps * (4 * n_a + 8 * n_a * n_f), "roofline": None, "cpu_baseline": None,
             "clocks": clock_summary,
         }
@@ -696,7 +740,9 @@ def run_multi(args):
             line["config"] = {
                 "workload": (f"{n_a}A{n_f}F: config 2 layer per A replica (T={T}, H=7168, 256 experts, "
                              f"top-8 {'Zipf(s=1.2) popularity' if args.routing == 'zipf' else 'sigmoid'}, I=2048, "
-                             "MXFP4, 1 bf16 shared expert)"),
+                             "MXFP4, 1 bf16 shared expert)") if KIND == "mxfp4" else
+                            (f"{n_a}A{n_f}F: config 4 layer per A replica (T={T}, H={H}, {E} experts, top-{K_TOP} "
+                             f"softmax, I={I}, FP8 E4M3 with fp32 128x128 block scales)"),
                 "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
                 "expert_bounds": bounds, "routing": args.routing, "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
@@ -741,29 +787,34 @@ def run_multi(args):
 
 
 def main():
-    global E
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--tokens", type=int, default=T_DEFAULT)
-    ap.add_argument("--experts", type=int, default=E, help="routed experts (small profiling cases)")
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per A replica (default: the layer's T)")
+    ap.add_argument("--experts", type=int, default=None, help="routed experts (small profiling cases)")
     ap.add_argument("--cpu-experts", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=("layer", "zipf-sweep"), default="layer",
-                    help="zipf-sweep: T in 256/1024/4096/16384 with skewed routing (config 5), one line per T")
+    ap.add_argument("--workload", choices=("layer", "fp8-layer", "zipf-sweep"), default="layer",
+                    help="layer: config 2 (MXFP4); fp8-layer: config 4 (FP8 block-scaled); zipf-sweep: config 5, "
+                         "T in 256/1024/4096/16384 with skewed routing, one line per T")
     ap.add_argument("--routing", choices=("sigmoid", "zipf"), default=None,
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
     args = ap.parse_args()
-    E = args.experts
+    layer = LAYERS["fp8-layer" if args.workload == "fp8-layer" else "layer"]
+    globals().update(layer)
+    if args.tokens is None:
+        args.tokens = T_DEFAULT
+    if args.experts is not None:
+        globals()["E"] = args.experts
     if args.warmup < 3:
         args.warmup = 3
     if args.routing is None:
-        args.routing = "zipf" if args.workload == "zipf-sweep" else "sigmoid"
+        args.routing = "zipf" if args.workload == "zipf-sweep" else ROUTING
     if args.impl == "reference":
         run_reference(args)
     elif int(os.environ.get("WORLD_SIZE", "1")) > 1:

@@ -176,7 +176,8 @@ int asap_wait_replies(const asap_geometry_t* g, int32_t slot, uint32_t seq, uint
  *  w13     [num_local][2*inter][hidden/2] bytes: E2M1 pairs, low nibble first. Rows are the gate (W1) and
  *          up (W3) projections interleaved in blocks of 128: rows [256b, 256b+128) = gate[128b, 128b+128),
  *          rows [256b+128, 256b+256) = up[128b, 128b+128).
- *  w13_sf  [num_local][hidden/128][2*inter/128][512] E8M0 scale atoms (see DESIGN: scale-factor atom)
+ *  w13_sf  [num_local][hidden/128][2*inter/128][512] E8M0 scale atoms: one 512-byte atom per 128 rows x 4
+ *          32-wide K blocks, byte (r % 32) * 16 + ((r / 32) % 4) * 4 + kb % 4 for row r, block kb
  *  w2      [num_local][hidden][inter/2] bytes
  *  w2_sf   [num_local][inter/128][hidden/128][512]
  * hidden % 256 == 0, inter % 128 == 0. */
@@ -188,6 +189,23 @@ typedef struct {
 /* Build the TMA descriptors of a layer's weights once; *handle names them in asap_ffn_job. */
 int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle);
 int asap_experts_release(uint64_t handle);
+
+/* Routed experts of one layer on one F rank, FP8 E4M3 with fp32 scales per 128 x 128 block -- the layout of
+ * SGLang's block-quantised FusedMoE (w13_weight / w13_weight_scale_inv, w2_weight / w2_weight_scale_inv of a
+ * DeepSeek-style FP8 checkpoint, weight = e4m3 * scale), unchanged:
+ *  w13        [num_local][2*inter][hidden] E4M3: gate (W1) rows [0, inter), up (W3) rows [inter, 2*inter)
+ *  w13_scale  [num_local][2*inter/128][hidden/128] fp32
+ *  w2         [num_local][hidden][inter] E4M3
+ *  w2_scale   [num_local][hidden/128][inter/128] fp32
+ * Activations are quantised to E4M3 per 1 x 128 with an fp32 scale amax / 448 (as SGLang's per-token-group
+ * FP8 quantisation).  hidden % 256 == 0, inter % 128 == 0.  The handle is used with asap_ffn_job like an MXFP4
+ * one; asap_experts_release frees either kind. */
+typedef struct {
+  int32_t num_local, expert_base, hidden, inter;
+  uint64_t w13, w13_scale, w2, w2_scale;
+} asap_fp8_experts_t;
+
+int asap_experts_register_fp8(const asap_fp8_experts_t* e, uint64_t* handle);
 
 /* F-rank job workspace for up to n_max tokens of top-k `topk` (device memory, owned by the caller).
  * Size from asap_ffn_ws_bytes; asap_ffn_ws_register builds its TMA descriptors. */

@@ -109,15 +109,31 @@ def dequant_w2(w2: np.ndarray, w2_sf: np.ndarray, P: int, H: int, I: int):
     return out
 
 
+def dequant_fp8(w13_codes, w13_scale, w2_codes, w2_scale):
+    """FP8 block-scaled experts (checkpoint layout: w13 [P, 2I, H] gate rows then up rows, scales per 128 x 128)
+    -> (gate [P, I, H], up [P, I, H], w2 [P, H, I]) fp32."""
+    w13 = mx.fp8_block_dequantize(np.asarray(w13_codes), w13_scale)
+    I = w13.shape[1] // 2
+    return w13[:, :I], w13[:, I:], mx.fp8_block_dequantize(np.asarray(w2_codes), w2_scale)
+
+
 # ---------------------------------------------------------------- F side
 def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
+def _act_roundtrip(v, act_quant):
+    if act_quant == "fp8":
+        return mx.fp8_act_roundtrip(v)
+    return mx.mx_roundtrip(v) if act_quant else v
+
+
 def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, swiglu_limit=None):
     """One F rank's reply for one message: bf16 values as fp32 [n_f, H].
 
-    x_f: bf16 values (fp32 array) [n_f, H]; ids_f/w_f: [n_f, k]; gate/up [P, I, H]; w2 [P, H, I]."""
+    x_f: bf16 values (fp32 array) [n_f, H]; ids_f/w_f: [n_f, k]; gate/up [P, I, H]; w2 [P, H, I].
+    act_quant: True = MXFP8 (E8M0 scale per 32) activations, "fp8" = E4M3 with an fp32 scale per 1 x 128,
+    False = none."""
     x_f = np.asarray(x_f, np.float32)
     ids_f = np.asarray(ids_f, np.int64)
     w_f = np.asarray(w_f, np.float32)
@@ -129,17 +145,13 @@ def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, 
         tt, jj = np.nonzero(ids_f == e0 + e)
         if tt.size == 0:
             continue
-        xa = x_f[tt]
-        if act_quant:
-            xa = mx.mx_roundtrip(xa)
+        xa = _act_roundtrip(x_f[tt], act_quant)
         g = xa @ gate[e].T
         u = xa @ up[e].T
         if swiglu_limit:
             g = np.minimum(g, swiglu_limit)
             u = np.clip(u, -swiglu_limit, swiglu_limit)
-        h = (silu(g) * u).astype(np.float32)
-        if act_quant:
-            h = mx.mx_roundtrip(h)
+        h = _act_roundtrip((silu(g) * u).astype(np.float32), act_quant)
         y = h @ w2[e].T
         y2[tt, jj] = mx.bf16_round(y * w_f[tt, jj][:, None])
         used[tt, jj] = True

@@ -160,3 +160,37 @@ def sf_from_kmajor_atoms(atoms: np.ndarray, n: int, kblocks: int) -> np.ndarray:
     r, kb = np.meshgrid(np.arange(n), np.arange(kblocks), indexing="ij")
     off = ((kb >> 2) * (n >> 7) + (r >> 7)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (kb & 3)
     return atoms.reshape(-1)[off].astype(np.uint8)
+
+
+# ---------------------------------------------------------------- FP8 per 1 x 128 (fp32 scale)
+FP8_MAX = np.float32(448.0)
+
+
+def fp8_act_quantize(v: np.ndarray):
+    """[..., K] fp32 (K % 128 == 0) -> (E4M3 codes [..., K], fp32 scales [..., K/128]).  SGLang's per-token-group
+    FP8 quantisation (group 128): amax clamped to 1e-10, scale = amax / 448, codes = e4m3(v * (448 / amax)),
+    every operation one fp32 rounding (as libasap's quant_tok_fp8 and FP8 GEMM1 epilogue compute it)."""
+    v = np.asarray(v, dtype=np.float32)
+    blocks = v.reshape(*v.shape[:-1], v.shape[-1] // 128, 128)
+    amax = np.maximum(np.max(np.abs(blocks), axis=-1), np.float32(1e-10)).astype(np.float32)
+    scale = (amax / FP8_MAX).astype(np.float32)
+    inv = (FP8_MAX / amax).astype(np.float32)
+    q = e4m3_encode((blocks * inv[..., None]).astype(np.float32))
+    return q.reshape(v.shape), scale
+
+
+def fp8_act_dequantize(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    vals = e4m3_decode(q).reshape(*q.shape[:-1], q.shape[-1] // 128, 128)
+    return (vals * scale[..., None]).reshape(q.shape).astype(np.float32)
+
+
+def fp8_act_roundtrip(v: np.ndarray) -> np.ndarray:
+    return fp8_act_dequantize(*fp8_act_quantize(v))
+
+
+def fp8_block_dequantize(codes: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """E4M3 weights [..., N, K] with fp32 scales [..., N/128, K/128] -> fp32 (weight = e4m3 * scale)."""
+    vals = e4m3_decode(codes)
+    *lead, n, k = vals.shape
+    b = vals.reshape(*lead, n // 128, 128, k // 128, 128) * np.asarray(scale, np.float32)[..., :, None, :, None]
+    return b.reshape(*lead, n, k).astype(np.float32)

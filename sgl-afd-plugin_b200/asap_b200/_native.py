@@ -43,6 +43,11 @@ class Mxfp4Experts_t(ctypes.Structure):
                 ("w13", c_uint64), ("w13_sf", c_uint64), ("w2", c_uint64), ("w2_sf", c_uint64)]
 
 
+class Fp8Experts_t(ctypes.Structure):
+    _fields_ = [("num_local", c_int32), ("expert_base", c_int32), ("hidden", c_int32), ("inter", c_int32),
+                ("w13", c_uint64), ("w13_scale", c_uint64), ("w2", c_uint64), ("w2_scale", c_uint64)]
+
+
 # name -> (restype, argtypes); every int-returning call is checked
 _SIGS = {
     "asap_last_error_string": (c_char_p, []),
@@ -74,6 +79,7 @@ _SIGS = {
     "asap_wait_replies": (c_int32, [POINTER(Geometry_t), c_int32, c_uint32, c_uint64, c_uint64, c_uint64,
                                     c_void_p]),
     "asap_experts_register": (c_int32, [POINTER(Mxfp4Experts_t), POINTER(c_uint64)]),
+    "asap_experts_register_fp8": (c_int32, [POINTER(Fp8Experts_t), POINTER(c_uint64)]),
     "asap_experts_release": (c_int32, [c_uint64]),
     "asap_ffn_ws_bytes": (c_uint64, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "asap_ffn_ws_register": (c_int32, [c_uint64, c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_uint64)]),

@@ -13,6 +13,10 @@ asap_mxfp4_experts_t):
 
 ``from_logical`` builds that layout from plain [P, rows, K] codes and [P, rows, K/32] scale bytes (the
 checkpoint layout after SGLang's loader, W13 = [W1; W3]); ``random`` makes seeded synthetic weights.
+
+FP8 (``Fp8Experts``): E4M3 weights with one fp32 scale per 128 x 128 block, in the checkpoint's own layout
+(include/asap.h, asap_fp8_experts_t): w13 [P, 2I, H] (gate rows then up rows), w13_scale [P, 2I/128, H/128],
+w2 [P, H, I], w2_scale [P, H/128, I/128].
 """
 
 from __future__ import annotations
@@ -102,6 +106,74 @@ class Mxfp4Experts:
 
         return cls(dev(packed13), dev(atoms13), dev(packed2), dev(atoms2), num_local=P, expert_base=expert_base,
                    hidden=H, inter=I)
+
+
+class Fp8Experts:
+    """FP8 block-scaled routed experts of one layer on one F rank (used with FfnScheduler like Mxfp4Experts)."""
+
+    def __init__(self, w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor, *,
+                 num_local: int, expert_base: int, hidden: int, inter: int):
+        self.num_local, self.expert_base, self.hidden, self.inter = num_local, expert_base, hidden, inter
+        P, H, I = num_local, hidden, inter
+        if H % 256 or I % 128:
+            raise ValueError("FP8 experts need hidden % 256 == 0 and inter % 128 == 0")
+        w13, w2 = (t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t for t in (w13, w2))
+        expect = {"w13": (torch.uint8, P * 2 * I * H), "w13_scale": (torch.float32, P * (2 * I // 128) * (H // 128)),
+                  "w2": (torch.uint8, P * H * I), "w2_scale": (torch.float32, P * (H // 128) * (I // 128))}
+        for name, t in (("w13", w13), ("w13_scale", w13_scale), ("w2", w2), ("w2_scale", w2_scale)):
+            dt, n = expect[name]
+            if t.dtype != dt or not t.is_cuda or not t.is_contiguous() or t.numel() != n:
+                raise ValueError(f"{name}: need a contiguous CUDA {dt} tensor of {n} elements")
+        self.w13, self.w13_scale, self.w2, self.w2_scale = w13, w13_scale, w2, w2_scale
+        desc = N.Fp8Experts_t(P, expert_base, H, I, w13.data_ptr(), w13_scale.data_ptr(), w2.data_ptr(),
+                              w2_scale.data_ptr())
+        h = ctypes.c_uint64()
+        N.call("asap_experts_register_fp8", ctypes.byref(desc), ctypes.byref(h))
+        self.handle = h.value
+
+    kind = "fp8"
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.w13, self.w13_scale, self.w2, self.w2_scale))
+
+    def release(self) -> None:
+        if self.handle:
+            N.call("asap_experts_release", self.handle)
+            self.handle = 0
+
+    @classmethod
+    def from_float(cls, w13, w2, *, expert_base: int = 0, device="cuda") -> "Fp8Experts":
+        """Dense w13 [P, 2I, H] (gate rows then up rows) and w2 [P, H, I] -> block-quantised FP8 on ``device``."""
+        from .quant import fp8_block_quantize
+
+        w13 = torch.as_tensor(w13, device=device)
+        w2 = torch.as_tensor(w2, device=device)
+        P, two_i, H = w13.shape
+        q13, s13, q2, s2 = [], [], [], []
+        for e in range(P):  # one expert at a time: bounded fp32 temporaries
+            a, b = fp8_block_quantize(w13[e])
+            c, d = fp8_block_quantize(w2[e])
+            q13.append(a), s13.append(b), q2.append(c), s2.append(d)
+        return cls(torch.stack(q13).contiguous(), torch.stack(s13).contiguous(), torch.stack(q2).contiguous(),
+                   torch.stack(s2).contiguous(), num_local=P, expert_base=expert_base, hidden=H, inter=two_i // 2)
+
+    @classmethod
+    def random(cls, num_local: int, hidden: int, inter: int, *, expert_base: int = 0, device="cuda", seed: int = 0,
+               std: float = 0.02) -> "Fp8Experts":
+        """N(0, std) weights generated on the device, block-quantised one expert at a time."""
+        from .quant import fp8_block_quantize
+
+        P, H, I = num_local, hidden, inter
+        gen = torch.Generator(device=device).manual_seed(seed)
+        w13 = torch.empty(P, 2 * I, H, dtype=torch.uint8, device=device)
+        s13 = torch.empty(P, 2 * I // 128, H // 128, dtype=torch.float32, device=device)
+        w2 = torch.empty(P, H, I, dtype=torch.uint8, device=device)
+        s2 = torch.empty(P, H // 128, I // 128, dtype=torch.float32, device=device)
+        for e in range(P):
+            w13[e], s13[e] = fp8_block_quantize(torch.randn(2 * I, H, device=device, generator=gen) * std)
+            w2[e], s2[e] = fp8_block_quantize(torch.randn(H, I, device=device, generator=gen) * std)
+        return cls(w13, s13, w2, s2, num_local=P, expert_base=expert_base, hidden=H, inter=I)
 
 
 def _kmajor_atoms(sf: np.ndarray) -> np.ndarray:

@@ -1,4 +1,8 @@
-"""Host-side weight quantisation to MXFP4 (weight ingest of dense fp32/bf16 expert weights).
+"""Host-side weight quantisation (weight ingest of dense fp32/bf16 expert weights): MXFP4, and FP8 E4M3 with one
+fp32 scale per 128 x 128 block.
+
+FP8 block quantisation (the DeepSeek-V3 / SGLang block-FP8 checkpoint format, weight = e4m3 * scale_inv): per
+128 x 128 block, scale = amax / 448 and codes = e4m3(w / scale), round to nearest even.
 
 OCP Microscaling Formats v1.0, section 6.3, for E2M1 elements: per block of 32 values along K, shared exponent
 X = floor(log2(amax)) - 2 (emax of E2M1), stored as E8M0 byte X + 127 (clamped to [0, 254]); elements are
@@ -32,3 +36,17 @@ def mxfp4_quantize(w: np.ndarray):
     scaled = blocks.astype(np.float64) / np.ldexp(1.0, sb.astype(np.int64) - 127)[..., None]
     codes = e2m1_round_codes(np.abs(scaled)) | (np.signbit(scaled).astype(np.uint8) << 3)
     return codes.reshape(w.shape), sb
+
+
+def fp8_block_quantize(w):
+    """[..., N, K] float (N, K multiples of 128) -> (E4M3 codes as uint8 [..., N, K], fp32 scales
+    [..., N/128, K/128]); a torch tensor in, torch tensors out on its device."""
+    import torch
+
+    w = torch.as_tensor(w).float()
+    *lead, n, k = w.shape
+    b = w.reshape(*lead, n // 128, 128, k // 128, 128)
+    amax = b.abs().amax(dim=(-3, -1))
+    scale = torch.clamp(amax, min=1e-12) / 448.0
+    q = (b / scale[..., :, None, :, None]).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8).reshape(*lead, n, k).contiguous(), scale.contiguous()

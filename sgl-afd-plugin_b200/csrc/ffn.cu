@@ -639,6 +639,8 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
 }
 }  // namespace gemm
 
+#include "gemm_fp8.cuh"
+
 // ------------------------------------------------------------------ K5b: weighted reduce + reply
 struct FinalArgs {
   const JobDesc* desc;
@@ -763,8 +765,11 @@ static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
   return ASAP_OK;
 }
 
+enum ExpertsKind { kMxfp4 = 0, kFp8Block = 1 };
 struct ExpertsHandle {
-  asap_mxfp4_experts_t e;
+  ExpertsKind kind;
+  asap_mxfp4_experts_t e;   // kMxfp4 (num_local/expert_base/hidden/inter filled for both kinds)
+  asap_fp8_experts_t f8;    // kFp8Block
   CUtensorMap w13_map, w2_map;
 };
 constexpr int kTimedKernels = 5;  // routing (count+scan+place), quantise+permute, gemm1, gemm2, finalize_reply
@@ -802,7 +807,30 @@ static int ensure_gemm_attrs() {
                                  gemm::SMEM_BYTES));
   ASAP_CUDA(cudaFuncSetAttribute(gemm::moe_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  gemm::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemm8::moe_gemm_fp8_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm8::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemm8::moe_gemm_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm8::SMEM_BYTES));
   gemm_attr_set = true;
+  return ASAP_OK;
+}
+
+// K5b launch shared by both weight kinds; `mark` records the job's last timing event.
+template <class Mark>
+static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_t* B, uint64_t reply_seg,
+                    uint64_t reply_done, cudaStream_t st, int sms, Mark& mark) {
+  FinalArgs fa{};
+  fa.desc = desc;
+  fa.topk = L.topk;
+  fa.H = L.H;
+  fa.pair_pos = pa.pair_pos;
+  fa.y2 = (const __nv_bfloat16*)(B + L.y2);
+  fa.reply_seg = (__nv_bfloat16*)reply_seg;
+  fa.reply_done = (uint32_t*)reply_done;
+  fa.desc_rw = desc;
+  finalize_reply_kernel<<<sms * 4, 256, 0, st>>>(fa);
+  ASAP_CHECK_LAUNCH("finalize_reply_kernel");
+  mark(5);
   return ASAP_OK;
 }
 
@@ -829,6 +857,7 @@ int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
     return ASAP_EINVAL;
   }
   ExpertsHandle* h = new ExpertsHandle;
+  h->kind = kMxfp4;
   h->e = *e;
   const uint64_t P = e->num_local, H = e->hidden, I = e->inter;
   int rc = make_tmap_2d(&h->w13_map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w13, H, P * 2 * I, H / 2,
@@ -836,6 +865,47 @@ int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
   if (!rc)
     rc = make_tmap_2d(&h->w2_map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2, gemm::BK,
                       gemm::BN, "w2");
+  if (rc) {
+    delete h;
+    return rc;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  *handle = g_next++;
+  g_experts[*handle] = h;
+  return ASAP_OK;
+}
+
+int asap_experts_register_fp8(const asap_fp8_experts_t* e, uint64_t* handle) {
+  if (!e || !handle) {
+    set_error("asap_experts_register_fp8: NULL argument");
+    return ASAP_EINVAL;
+  }
+  if (e->num_local < 1 || e->num_local > ASAP_MAX_LOCAL_EXPERTS || e->hidden % 256 || e->inter % 128 ||
+      e->hidden <= 0 || e->inter <= 0 || e->expert_base < 0) {
+    set_error("asap_experts_register_fp8: need 1 <= num_local <= %d, hidden %% 256 == 0, inter %% 128 == 0 "
+              "(got %d, %d, %d)",
+              ASAP_MAX_LOCAL_EXPERTS, e->num_local, e->hidden, e->inter);
+    return ASAP_EINVAL;
+  }
+  if ((e->w13 & 15) || (e->w2 & 15) || (e->w13_scale & 3) || (e->w2_scale & 3) || !e->w13 || !e->w2 ||
+      !e->w13_scale || !e->w2_scale) {
+    set_error("asap_experts_register_fp8: weights must be 16-byte and scales 4-byte aligned, non-NULL");
+    return ASAP_EINVAL;
+  }
+  ExpertsHandle* h = new ExpertsHandle;
+  h->kind = kFp8Block;
+  h->f8 = *e;
+  memset(&h->e, 0, sizeof(h->e));
+  h->e.num_local = e->num_local;
+  h->e.expert_base = e->expert_base;
+  h->e.hidden = e->hidden;
+  h->e.inter = e->inter;
+  const uint64_t P = e->num_local, H = e->hidden, I = e->inter;
+  int rc = make_tmap_2d(&h->w13_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, (const void*)e->w13, H, P * 2 * I, H, gemm8::BK,
+                        128, "w13 fp8");
+  if (!rc)
+    rc = make_tmap_2d(&h->w2_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, (const void*)e->w2, I, P * H, I, gemm8::BK, 128,
+                      "w2 fp8");
   if (rc) {
     delete h;
     return rc;
@@ -1007,6 +1077,49 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   qa.xtok_sf = B + L.xtok_sf;
   qa.xq = B + L.xq;
   qa.xq_sf = B + L.xq_sf;
+  if (eh->kind == kFp8Block) {
+    quant_tok_fp8_kernel<<<sms * 4, 256, 0, st>>>(qa);
+    ASAP_CHECK_LAUNCH("quant_tok_fp8_kernel");
+    permute_copy_fp8_kernel<<<sms * 4, 256, 0, st>>>(qa, L.m_cap);
+    ASAP_CHECK_LAUNCH("permute_copy_fp8_kernel");
+    mark(2);
+    gemm8::Params g1;
+    memset(&g1, 0, sizeof(g1));
+    g1.tmap_a = wh->xq_map;
+    g1.tmap_b = eh->w13_map;
+    g1.sa = (const float*)(B + L.xq_sf);
+    g1.sb = (const float*)eh->f8.w13_scale;
+    g1.m_cap = L.m_cap;
+    g1.desc = desc;
+    g1.mstart = pa.mstart;
+    g1.row_tok = pa.row_tok;
+    g1.row_w = pa.row_w;
+    g1.out_q = B + L.hq;
+    g1.out_sa = (float*)(B + L.hq_sf);
+    g1.P = L.P;
+    g1.N = 2 * L.I;
+    g1.K = L.H;
+    g1.swiglu_limit = swiglu_limit;
+    g1.status = status;
+    g1.timeout_ns = timeout_ns;
+    gemm8::moe_gemm_fp8_kernel<0><<<sms, gemm8::THREADS, gemm8::SMEM_BYTES, st>>>(g1);
+    ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<0>");
+    mark(3);
+    gemm8::Params g2 = g1;
+    g2.tmap_a = wh->hq_map;
+    g2.tmap_b = eh->w2_map;
+    g2.sa = (const float*)(B + L.hq_sf);
+    g2.sb = (const float*)eh->f8.w2_scale;
+    g2.out_q = nullptr;
+    g2.out_sa = nullptr;
+    g2.out_bf = (__nv_bfloat16*)(B + L.y2);
+    g2.N = L.H;
+    g2.K = L.I;
+    gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
+    ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<1>");
+    mark(4);
+    return finalize(desc, L, pa, B, reply_seg, reply_done, st, sms, mark);
+  }
   quant_tok_kernel<<<sms * 4, 256, 0, st>>>(qa);
   ASAP_CHECK_LAUNCH("quant_tok_kernel");
   permute_copy_kernel<<<sms * 4, 256, 0, st>>>(qa);
@@ -1051,19 +1164,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
   mark(4);
 
-  FinalArgs fa{};
-  fa.desc = desc;
-  fa.topk = L.topk;
-  fa.H = L.H;
-  fa.pair_pos = pa.pair_pos;
-  fa.y2 = (const __nv_bfloat16*)(B + L.y2);
-  fa.reply_seg = (__nv_bfloat16*)reply_seg;
-  fa.reply_done = (uint32_t*)reply_done;
-  fa.desc_rw = desc;
-  finalize_reply_kernel<<<sms * 4, 256, 0, st>>>(fa);
-  ASAP_CHECK_LAUNCH("finalize_reply_kernel");
-  mark(5);
-  return ASAP_OK;
+  return finalize(desc, L, pa, B, reply_seg, reply_done, st, sms, mark);
 }
 
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable) {

@@ -1,0 +1,372 @@
+// FP8 E4M3 experts with fp32 scales per 128 x 128 weight block (SGLang's block-quantised FusedMoE format,
+// python/sgl_asap_plugin/srt/managers/scheduler.py:410-412 -> FusedMoE with a DeepSeek-style FP8 checkpoint):
+// per-token 1 x 128 activation quantisation, the expert-major copy, and the two grouped GEMMs on tcgen05
+// kind::f8f6f4.  Included by ffn.cu (same translation unit: JobDesc, QuantArgs, gemm::decode_tile).
+//
+// Block scales are not powers of two, so they cannot ride in the MMA: every 128-deep K block is accumulated
+// on its own into one of two TMEM buffers (ping-pong), and the epilogue warps fold it into fp32 registers,
+//     acc[r][c] += partial_kb[r][c] * (sa[r][kb] * sb[c / 128][kb]),
+// while the tensor core already runs the next K block into the other buffer.
+
+namespace gemm8 {
+constexpr int BM = 128, BN = 256, BK = 128;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;  // E4M3 activations, 128 rows x 128 bytes
+constexpr int B_BYTES = BN * BK;  // E4M3 weights, 256 rows x 128 bytes (two 128-row boxes)
+constexpr int B_HALF = B_BYTES / 2;
+constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int THREADS = 32 * (2 + NUM_EPI_WARPS);
+constexpr uint32_t TMEM_COLS = 512;  // two 256-column partial accumulators
+constexpr int CTRL_BYTES = 4096;     // barriers, TMEM slot, expert starts, row amax exchange
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + CTRL_BYTES;
+static_assert(256 + 4 * (ASAP_MAX_LOCAL_EXPERTS + 1) <= 2048, "expert starts overlap the amax exchange");
+constexpr float kE4M3Max = 448.f;
+
+// tcgen05 instruction descriptor, kind::f8f6f4: D fp32, A = B = E4M3, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f8f6f4(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+struct Params {
+  CUtensorMap tmap_a;  // activations [m_cap, K] E4M3
+  CUtensorMap tmap_b;  // weights [P * N, K] E4M3, the checkpoint's row order
+  const float* sa;     // activation scales, K-block-major [K/128][m_cap]
+  const float* sb;     // weight block scales [P][N/128][K/128]
+  int64_t m_cap;
+  const JobDesc* desc;
+  const int32_t* mstart;   // [P + 1] in 128-row blocks
+  const int32_t* row_tok;  // [m_cap]
+  const float* row_w;      // [m_cap]
+  uint8_t* out_q;          // GEMM1: [m_cap, N/2] E4M3
+  float* out_sa;           // GEMM1: [(N/2)/128][m_cap] fp32
+  __nv_bfloat16* out_bf;   // GEMM2: [m_cap, N]
+  int32_t P, N, K;
+  float swiglu_limit;
+  uint64_t status, timeout_ns;
+};
+
+// E4M3 codes of 4 values (scaled by inv) packed little-endian into one word.
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d, float inv) {
+  return cvt_e4m3x2(a * inv, b * inv) | (cvt_e4m3x2(c * inv, d * inv) << 16);
+}
+
+// EPI 0 (GEMM1, N = 2I): tile n covers gate rows [128n, 128n+128) and up rows I + [128n, 128n+128); epilogue
+// h = silu(gate) * up, requantised to E4M3 per 1 x 128 (the tile's 128 h columns are one K block of GEMM2).
+// EPI 1 (GEMM2, N = H): tile n covers rows [256n, 256n+256); epilogue bf16(acc * w[row]).
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* ctrl = sB + STAGES * B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* mma_done = acc_empty + 2;
+  uint64_t* amax_bar = mma_done + 1;    // [4 lane quarters][2 tile parities]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 196);
+  int32_t* s_mstart = reinterpret_cast<int32_t*>(ctrl + 256);
+  float* s_amax = reinterpret_cast<float*>(ctrl + 2048);  // [2 tile parities][2 halves][128 rows]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = p.P;
+  const bool valid_job = p.desc->valid != 0;
+  for (int i = threadIdx.x; i <= P; i += THREADS) s_mstart[i] = valid_job ? p.mstart[i] : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], NUM_EPI_WARPS);
+    }
+    mbar_init(mma_done, 1);
+    for (int b = 0; b < 8; ++b) mbar_init(&amax_bar[b], 64);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tmap_a);
+    prefetch_tmap(&p.tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int NT = p.N / BN, KT = p.K / BK;
+  const int num_tiles = s_mstart[P] * NT;
+  const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int e, m_blk, n_t;
+        gemm::decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
+        const int a_row = m_blk * BM;
+        int b0, b1;
+        if constexpr (EPI == 0) {
+          b0 = e * p.N + n_t * 128;
+          b1 = e * p.N + p.N / 2 + n_t * 128;
+        } else {
+          b0 = e * p.N + n_t * BN;
+          b1 = b0 + 128;
+        }
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, deadline, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_TX);
+          tma_load_2d(sA + stage * A_BYTES, &p.tmap_a, kt * BK, a_row, &full[stage]);
+          tma_load_2d(sB + stage * B_BYTES, &p.tmap_b, kt * BK, b0, &full[stage]);
+          tma_load_2d(sB + stage * B_BYTES + B_HALF, &p.tmap_b, kt * BK, b1, &full[stage]);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the copies of the last armed stages must land before this CTA may exit.
+      const uint64_t drain_deadline = globaltimer_ns() + 200000000ull;
+      const int n_drain = issued < STAGES ? issued : STAGES;
+      volatile int no_abort = 0;
+      for (int i = 0; i < n_drain; ++i) {
+        int s = stage - 1 - i;
+        uint32_t ph = phase;
+        if (s < 0) {
+          s += STAGES;
+          ph ^= 1u;
+        }
+        mbar_wait(&full[s], ph, drain_deadline, &no_abort);
+      }
+      if (!ok) report(p.status, status_word(ASAP_ST_PIPELINE_TIMEOUT, 0, 0, 8 + EPI));
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: one K block per TMEM buffer, alternating
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t it = 0;
+      const uint32_t idesc = idesc_f8f6f4(BM, BN);
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const uint32_t buf = it & 1u;
+          if (!mbar_wait(&acc_empty[buf], ((it >> 1) & 1u) ^ 1u, deadline, abort_flag) ||
+              !mbar_wait(&full[stage], phase, deadline, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = gemm::sdesc_sw128(sA + stage * A_BYTES);
+          const uint64_t bdesc = gemm::sdesc_sw128(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            tc_mma_f8f6f4(tmem_base + buf * BN, adesc + 2ull * k, bdesc + 2ull * k, idesc, k != 0);
+          tc_commit(&empty[stage]);
+          tc_commit(&acc_full[buf]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // every MMA this thread issued has completed before TMEM is released
+      tc_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, globaltimer_ns() + 200000000ull, &no_abort);
+    }
+  } else {
+    // ---------------- epilogue warps: promotion of every K block, then the tile's epilogue
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
+    const int NB = p.N / 128;  // 128-row weight blocks per expert
+    // this thread's two 64-column groups inside the 256-column accumulator
+    const int col0 = EPI == 0 ? 64 * half : 128 * half;
+    const int col1 = EPI == 0 ? 128 + 64 * half : 128 * half + 64;
+    uint32_t it = 0, tcount = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
+      int e, m_blk, n_t;
+      gemm::decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
+      const int64_t row = (int64_t)m_blk * BM + row_in_tile;
+      const bool valid = p.row_tok[row] >= 0;
+      const int nb0 = EPI == 0 ? n_t : 2 * n_t + half;
+      const int nb1 = EPI == 0 ? NB / 2 + n_t : 2 * n_t + half;
+      const float* sb0 = p.sb + ((int64_t)e * NB + nb0) * KT;
+      const float* sb1 = p.sb + ((int64_t)e * NB + nb1) * KT;
+      float acc0[64], acc1[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        acc0[i] = 0.f;
+        acc1[i] = 0.f;
+      }
+      float sa_next = p.sa[row];
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const float sa = sa_next;
+        if (kt + 1 < KT) sa_next = p.sa[(int64_t)(kt + 1) * p.m_cap + row];
+        const float f0 = sa * __ldg(sb0 + kt), f1 = sa * __ldg(sb1 + kt);
+        const uint32_t buf = it & 1u;
+        if (!mbar_wait(&acc_full[buf], (it >> 1) & 1u, deadline, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tb = t_lane + buf * BN;
+        uint32_t v[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld_32x32b_x32(tb + col0 + 32 * c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc0[32 * c + i] = fmaf(__uint_as_float(v[i]), f0, acc0[32 * c + i]);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld_32x32b_x32(tb + col1 + 32 * c, v);
+          tmem_wait_ld();
+          if (c == 1) {  // this warp's reads of the buffer are complete: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc1[32 * c + i] = fmaf(__uint_as_float(v[i]), f1, acc1[32 * c + i]);
+        }
+      }
+      if (!ok) break;
+      if constexpr (EPI == 0) {
+        const int I = p.N / 2;
+        const float lim = p.swiglu_limit;
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float gv = acc0[i], uv = acc1[i];
+          if (lim > 0.f) {
+            gv = fminf(gv, lim);
+            uv = fminf(fmaxf(uv, -lim), lim);
+          }
+          acc0[i] = gemm::silu_f(gv) * uv;
+          amax = fmaxf(amax, fabsf(acc0[i]));
+        }
+        // the row's other 64 h values live in the partner warp (same lane quarter, other half)
+        const uint32_t par = tcount & 1u;
+        s_amax[(par * 2 + half) * 128 + row_in_tile] = amax;
+        mbar_arrive(&amax_bar[q * 2 + par]);
+        if (!mbar_wait(&amax_bar[q * 2 + par], (tcount >> 1) & 1u, deadline, abort_flag)) break;
+        amax = fmaxf(amax, s_amax[(par * 2 + (half ^ 1)) * 128 + row_in_tile]);
+        if (valid) {
+          const float amax_c = fmaxf(amax, 1e-10f);
+          const float scale = amax_c / kE4M3Max, inv = kE4M3Max / amax_c;
+          uint4* dst = reinterpret_cast<uint4*>(p.out_q + row * I + n_t * 128 + half * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float* h = acc0 + 16 * j;
+            dst[j] = make_uint4(e4m3x4(h[0], h[1], h[2], h[3], inv), e4m3x4(h[4], h[5], h[6], h[7], inv),
+                                e4m3x4(h[8], h[9], h[10], h[11], inv), e4m3x4(h[12], h[13], h[14], h[15], inv));
+          }
+          if (half == 0) p.out_sa[(int64_t)n_t * p.m_cap + row] = scale;
+        }
+      } else {
+        if (!valid) continue;
+        const float wr = p.row_w[row];
+        uint4* dst = reinterpret_cast<uint4*>(p.out_bf + row * p.N + (int64_t)n_t * BN + half * 128);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float* a = j < 8 ? acc0 + 8 * j : acc1 + 8 * (j - 8);
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[2 * i] * wr, a[2 * i + 1] * wr);
+            o[i] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+}  // namespace gemm8
+
+// ------------------------------------------------------------------ FP8 activation quantisation + copy
+// Every token once: bf16 row -> E4M3 row + one fp32 scale per 128 values (scale = amax / 448, values
+// multiplied by 448 / amax before the round-to-nearest-even, saturating conversion).  One warp per token;
+// each pass covers 256 values, a half-warp per 128-value block.
+__global__ void __launch_bounds__(256) quant_tok_fp8_kernel(const __grid_constant__ QuantArgs p) {
+  if (!p.desc->valid) return;
+  const int n = p.desc->n;
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int H = p.H;
+  float* sf = reinterpret_cast<float*>(p.xtok_sf);
+  for (int64_t t = gwarp; t < n; t += nwarps) {
+    const __nv_bfloat16* src = p.x + t * H;
+    for (int base = 0; base < H; base += 256) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + base + lane * 8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float amax_c = fmaxf(amax, 1e-10f);
+      const float inv = gemm8::kE4M3Max / amax_c;
+      *reinterpret_cast<uint2*>(p.xtok + t * H + base + lane * 8) =
+          make_uint2(gemm8::e4m3x4(v[0], v[1], v[2], v[3], inv), gemm8::e4m3x4(v[4], v[5], v[6], v[7], inv));
+      if ((lane & 15) == 0) sf[t * (H / 128) + base / 128 + (lane >> 4)] = amax_c / gemm8::kE4M3Max;
+    }
+  }
+}
+
+// Expert-major copy: permuted row r <- token row_tok[r]; scales to the K-block-major [H/128][m_cap] layout the
+// GEMM epilogue reads (one coalesced 4-byte load per thread and K block).
+__global__ void __launch_bounds__(256) permute_copy_fp8_kernel(const __grid_constant__ QuantArgs p, int64_t m_cap) {
+  if (!p.desc->valid) return;
+  const int64_t rows = (int64_t)p.mstart[p.P] * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int H = p.H, kblocks = H / 128, nvec = H / 16;
+  const float* sf = reinterpret_cast<const float*>(p.xtok_sf);
+  float* dsf = reinterpret_cast<float*>(p.xq_sf);
+  for (int64_t r = gwarp; r < rows; r += nwarps) {
+    const int32_t t = p.row_tok[r];
+    if (t < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xtok + (int64_t)t * H);
+    uint4* dst = reinterpret_cast<uint4*>(p.xq + r * H);
+    for (int c = lane; c < nvec; c += 32) dst[c] = src[c];
+    for (int kb = lane; kb < kblocks; kb += 32) dsf[(int64_t)kb * m_cap + r] = sf[(int64_t)t * kblocks + kb];
+  }
+}

@@ -3,7 +3,7 @@
 Run where the reference tree is available (it is not needed afterwards):
     python tests/golden/make_golden.py --reference /path/to/sgl-afd-plugin
 The reference module is loaded by file path (it imports nothing outside the standard library), so neither
-sglang nor libcuda is needed.  The JSON holds, for a set of geometries covering every BASELINE config and edge
+sglang nor libcuda is needed.  The JSON holds, for a set of geometries covering every benchmark config and edge
 cases, every offset the transport uses, plus doorbell known-answer vectors (including the seq wrap and the
 out-of-range fields that must raise) and the invalid geometries the reference rejects.
 """

@@ -25,8 +25,11 @@ def device_bytes(ptr: int, nbytes: int) -> np.ndarray:
     return _raw_bytes(ptr, nbytes, torch.cuda.current_device()).cpu().numpy()
 
 
-def experts_to_oracle(e: Mxfp4Experts):
-    """Dequantised (gate, up, w2) of device-layout experts, read back from the GPU."""
+def experts_to_oracle(e):
+    """Dequantised (gate, up, w2) of device-layout experts (MXFP4 or FP8 block-scaled), read back from the GPU."""
+    if getattr(e, "kind", "mxfp4") == "fp8":
+        return moe.dequant_fp8(e.w13.cpu().numpy(), e.w13_scale.cpu().numpy(), e.w2.cpu().numpy(),
+                               e.w2_scale.cpu().numpy())
     P, H, I = e.num_local, e.hidden, e.inter
     gate, up = moe.dequant_w13(e.w13.cpu().numpy(), e.w13_sf.cpu().numpy(), P, H, I)
     w2 = moe.dequant_w2(e.w2.cpu().numpy(), e.w2_sf.cpu().numpy(), P, H, I)

@@ -92,7 +92,7 @@ def test_ffn_chain_random_weights(cuda_ok, n, k, P, H, I, e0):
 
 
 def test_ffn_chain_config1_weights(cuda_ok):
-    """BASELINE config 1's F rank 1 (experts 8..15 of 16, H=1024, I=512, top-2 softmax, T=512): fp32 weights
+    """Benchmark config 1's F rank 1 (experts 8..15 of 16, H=1024, I=512, top-2 softmax, T=512): fp32 weights
     N(0, 0.02) quantised to MXFP4 on the host, through the logical -> device layout packer."""
     rng = np.random.default_rng(0)
     T, H, I, E, k = 512, 1024, 512, 16, 2

@@ -53,7 +53,7 @@ def run_layer(lb, layer_id, x, ids, w, shared=None, micro_batch=None):
 
 
 def test_config1_round_trip(pair):
-    """BASELINE config 1 (T=512, H=1024, 16 experts, top-2 softmax, I=512), plus a bf16 shared expert output."""
+    """Benchmark config 1 (T=512, H=1024, 16 experts, top-2 softmax, I=512), plus a bf16 shared expert output."""
     lb, ow = pair
     rng = np.random.default_rng(1)
     T = 512
@@ -162,7 +162,7 @@ def _from_fp32(rng, E, H, I, base):
 
 
 def test_config1_two_f_ranks(cuda_ok):
-    """BASELINE config 1 exactly: 1 A replica + 2 F ranks with 8 experts each (T=512, H=1024, top-2 softmax over
+    """Benchmark config 1 exactly: 1 A replica + 2 F ranks with 8 experts each (T=512, H=1024, top-2 softmax over
     16 experts, I=512, fp32 N(0, 0.02) weights as MXFP4, x ~ N(0,1) bf16, seed 0)."""
     rng = np.random.default_rng(0)
     T, H, I = 512, 1024, 512
