@@ -59,7 +59,10 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before the timed region to after it.  The
+    sampler starts on entry (nvidia-smi needs a moment to produce its first line); ``mark_start`` / ``mark_end``
+    bracket the timed region and ``summary`` keeps the samples read inside it (or, for a region shorter than the
+    sampling period, the samples nearest to it)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -67,6 +70,7 @@ class ClockSampler:
 
     def __init__(self, gpu: int):
         self.gpu, self.proc, self.lines = gpu, None, []
+        self.t_start = self.t_end = None
 
     def __enter__(self):
         try:
@@ -75,16 +79,29 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            deadline = time.time() + 3.0
+            while not self.lines and time.time() < deadline:  # the first sample, so the region is covered
+                time.sleep(0.01)
         except OSError:
             self.proc = None
+        self.t_start = time.time()
         return self
+
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
     def __exit__(self, *exc):
+        if self.t_end is None:
+            self.t_end = time.time()
         if self.proc is not None:
+            time.sleep(0.1)  # the sample that covers the end of the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -93,9 +110,15 @@ class ClockSampler:
             self.t.join(timeout=2)
 
     def summary(self):
+        lines = [(t, l) for t, l in self.lines if self.t_start - 0.01 <= t <= self.t_end + 0.06]
+        window = "timed region"
+        if not lines and self.lines:  # region shorter than the sampling period: the nearest samples
+            mid = (self.t_start + self.t_end) / 2
+            lines = sorted(self.lines, key=lambda tl: abs(tl[0] - mid))[:2]
+            window = "nearest samples (timed region shorter than the 50 ms period)"
         sm, mx, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        for _, line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -110,7 +133,7 @@ class ClockSampler:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 # ------------------------------------------------------------------------------------------ workload
@@ -442,10 +465,39 @@ def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0):
             times.append(time.perf_counter() - t)
     dt = statistics.median(times)
     cfg = "config-2" if KIND == "mxfp4" else "config-4"
+    c1 = cpu_config1()
     return {"value": round(pairs / K_TOP / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"all {pairs} (token, expert) pairs of the T={T} {cfg} layer that route to experts "
                       f"0..{n_experts - 1} (numpy oracle, {'FP8 1x128' if act == 'fp8' else 'MXFP8'} activation "
-                      f"emulation, {cores} host threads); tokens = pairs / top-k; {dt:.2f} s per sample"}
+                      f"emulation, {cores} host threads); tokens = pairs / top-k; {dt:.2f} s per sample",
+            "config1": c1}
+
+
+def cpu_config1(reps=3):
+    """Config 1 on the host cores, the benchmark's own CPU case: the oracle's round trip (1 A replica, 2 F ranks
+    x 8 experts, T=512, H=1024, top-2 softmax over N(0,1) logits, I=512, fp32 N(0, 0.02) weights, x bf16 N(0,1),
+    seed 0, fp32 arithmetic with no activation quantisation)."""
+    import numpy as np
+
+    from oracle import moe, mx
+
+    rng = np.random.default_rng(0)
+    T1, H1, I1, E1 = 512, 1024, 512, 16
+    experts = []
+    for _ in range(2):
+        w13 = rng.standard_normal((8, 2 * I1, H1)).astype(np.float32) * 0.02
+        w2 = rng.standard_normal((8, H1, I1)).astype(np.float32) * 0.02
+        experts.append((w13[:, :I1], w13[:, I1:], w2))
+    x = mx.bf16_round(rng.standard_normal((T1, H1)).astype(np.float32))
+    ids, w = moe.topk_routing(rng.standard_normal((T1, E1)), 2, "softmax")
+    times = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        moe.round_trip(x, ids, w, [0, 8, 16], experts, act_quant=False)
+        times.append(time.perf_counter() - t)
+    dt = statistics.median(times)
+    return {"value": round(T1 / dt, 1), "unit": "tokens/s", "ms_per_layer": round(dt * 1e3, 2),
+            "sample": "config 1: one layer, T=512, H=1024, 16 experts over 2 F ranks, top-2 softmax, I=512, fp32"}
 
 
 def run_reference(args):
@@ -482,6 +534,9 @@ def run_sweep(args):
     busy time."""
     import torch
 
+    import ctypes
+
+    from asap_b200 import _native as N
     from asap_b200.dispatcher import AsapDispatcher
     from asap_b200.experts import Mxfp4Experts
     from asap_b200.loopback import Loopback
@@ -514,6 +569,7 @@ def run_sweep(args):
             step()
         torch.cuda.synchronize()
         lb.check()
+        N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 1)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(0) as clocks:
             torch.cuda.synchronize()
@@ -524,6 +580,11 @@ def run_sweep(args):
             torch.cuda.synchronize()
         lb.check()
         ms = t0.elapsed_time(t1) / args.steps
+        kms = (ctypes.c_float * 5)()
+        N.call("asap_ffn_last_timing", lb.scheds[0].ws_handle, kms, 5)
+        N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 0)
+        f0_ms = dict(zip(("routing", "quantise_permute", "gemm1", "gemm2", "reduce_reply"),
+                         [round(v, 4) for v in kms]))
         lat, busy, rows = [], [], None
         for _ in range(max(args.latency_iters, 1)):
             _, ticket = step()
@@ -547,7 +608,7 @@ def run_sweep(args):
             "f_rows": rows, "f_imbalance": round(max(rows) / mean_f, 4),
             "doorbell_to_f_start_us_p50": round(statistics.median(lat), 2),
             "f_rows_per_s": round(sum(rows) / statistics.median(busy), 1),
-            "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4),
+            "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4), "f0_kernels_ms": f0_ms,
             "weights_gb_read_per_step": round(E * (2 * I * H + H * I) * (0.5 + 1 / 32) / 1e9, 3),
             "e2e": None, "gpu_launches": args.steps * (4 + 8 * n_f), "roofline": None, "cpu_baseline": None,
             "clocks": clocks.summary(),
@@ -556,6 +617,173 @@ def run_sweep(args):
     lb.close()
     for d in per_f:
         d[0].release()
+
+
+# ------------------------------------------------------------------------------------------ config 3: layer stack
+N_LAYERS = 8
+
+
+def run_stack(args):
+    """Config 3: a stack of N_LAYERS config-2 layers, each A replica's T tokens as two micro-batches of T/2 on
+    slots 0 and 1 (two-batch overlap): per layer dispatch(mb0), shared(mb0), dispatch(mb1), shared(mb1),
+    combine(mb0), combine(mb1) through the public API (AsapDispatcher per layer), so each micro-batch's shared
+    expert runs while its routed experts are away and the F ranks always hold the other slot's job.  The output of
+    layer l, RMS-normalised, is the input of layer l+1.  N = 1: loopback (one F rank with all experts of all layers); N > 1: the
+    --topology split (2a4f on 6 GPUs is the benchmark's), F jobs enqueued by a feeder thread.  value = tokens of
+    all A replicas per second through the whole stack."""
+    from datetime import timedelta
+
+    import torch
+
+    from asap_b200.dispatcher import AsapBuffer, AsapDispatcher
+    from asap_b200.sglang_shim import StandardTopKOutput
+    from asap_b200.transport.layout import Geometry
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    T = args.tokens
+    Tmb = T // 2
+    L = N_LAYERS
+    steps_total = args.warmup + args.steps
+    if world == 1:
+        from asap_b200.loopback import Loopback
+
+        n_a, n_f, is_a = 1, 1, True
+        layers = {l: make_experts(E, 0, 1 + l, dev) for l in range(L)}
+        lb = Loopback(Geometry(1, 1, 2, Tmb, H, K_TOP, 1), layers, timeout_s=60.0)
+        lb.install()
+        bounds = [0, E]
+    else:
+        import torch.distributed as dist
+
+        from asap_b200.scheduler import FfnScheduler
+        from asap_b200.transport.channel import AttnChannel
+        from asap_b200.transport.server import FfnServer
+
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+        n_a, n_f = topology(args.topology, world)
+        g = Geometry(n_a, 1, 2, Tmb, H, K_TOP, n_f)
+        bounds = expert_bounds(n_f)
+        is_a = rank < n_a
+        ep = None
+        if not is_a:
+            f = rank - n_a
+            layers = {l: make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + 10 * l + f, dev) for l in range(L)}
+            server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
+                               host="127.0.0.1", port=0).start()
+            sched = FfnScheduler(server, layers, timeout_s=120.0)
+            ep = ("127.0.0.1", server.port)
+        eps = [None] * world
+        dist.all_gather_object(eps, ep)
+        endpoints = [e for e in eps if e is not None]
+        if is_a:
+            channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=120.0).connect()
+            AsapBuffer.connect(channel, local)
+        dist.barrier()
+        feeder = None
+        if not is_a:
+            fstream = torch.cuda.Stream(dev)
+
+            def feed():
+                torch.cuda.set_device(local)
+                for step in range(steps_total):
+                    for l in range(L):
+                        for mb in range(2):
+                            for a in range(n_a):
+                                sched.run_device_wait(a, mb, step * L + l + 1, l, fstream.cuda_stream)
+
+            feeder = threading.Thread(target=feed, daemon=True)
+            feeder.start()
+    ms = 0.0
+    clocks_summary = None
+    if is_a:
+        shared = SharedExpert(dev)
+        gen = torch.Generator(device=dev).manual_seed(rank)
+        x_in = [torch.randn(Tmb, H, device=dev, generator=gen).to(torch.bfloat16) for _ in range(2)]
+        topk = [[StandardTopKOutput(*reversed(make_routing(Tmb, 1000 * rank + 10 * l + mb, dev))) for mb in range(2)]
+                for l in range(L)]
+        disps = [AsapDispatcher(l) for l in range(L)]
+
+        def norm(t):  # the RMSNorm in front of every DeepSeek MoE block (keeps the stack's activations bounded)
+            return torch.nn.functional.rms_norm(t, (H,))
+
+        def step():
+            xs = x_in
+            for l in range(L):
+                d0 = disps[l].dispatch(xs[0], topk[l][0], micro_batch=0)
+                s0 = shared(xs[0])
+                d1 = disps[l].dispatch(xs[1], topk[l][1], micro_batch=1)
+                s1 = shared(xs[1])
+                xs = [norm(disps[l].combine(d0, shared=s0)), norm(disps[l].combine(d1, shared=s1))]
+            return xs
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if is_a:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            t0.record()
+            for _ in range(args.steps):
+                out = step()
+            t1.record()
+            torch.cuda.synchronize()
+        clocks_summary = clocks.summary()
+        ms = t0.elapsed_time(t1) / args.steps
+        finite = bool(torch.isfinite(out[0]).all().item() and torch.isfinite(out[1]).all().item())
+    if world > 1:
+        mt = torch.tensor([ms])
+        dist.all_reduce(mt, op=dist.ReduceOp.MAX)
+        ms = float(mt.item())
+        if feeder is not None:
+            feeder.join()
+        torch.cuda.synchronize()
+        (sched if not is_a else channel).check()
+        dist.barrier()
+    else:
+        lb.check()
+    if rank == 0:
+        line = {
+            "metric": "MoE layer-stack tokens/s A->F->A (8 DeepSeek-V3-shape MXFP4 layers, 2 micro-batches)",
+            "value": round(n_a * T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": DTYPE[KIND], "data": "synthetic", "workload_mode": "stack",
+            "config": {"workload": f"config 3: {L} stacked config-2 layers, {n_a}A{n_f}F, T={T} per A replica as "
+                                   f"2 micro-batches of {Tmb} on slots 0/1, shared expert between dispatch and "
+                                   "combine, uniform (sigmoid top-8) routing", "tokens_per_replica": T,
+                       "a_replicas": n_a, "f_ranks": n_f, "layers": L, "parallelism": f"{n_a}A{n_f}F",
+                       "expert_bounds": bounds},
+            "layer_tokens_per_s": round(n_a * T * L / (ms * 1e-3), 1), "output_finite": finite,
+            "e2e": None, "gpu_launches": args.steps * L * 2 * (4 + 8 * n_f) * n_a,
+            "roofline": None, "cpu_baseline": None, "clocks": clocks_summary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        if is_a:
+            channel.unmap_peers()
+        else:
+            server.unmap_peers()
+        dist.barrier()
+        if is_a:
+            AsapBuffer.install(None)
+            channel.close()
+        else:
+            sched.close()
+            server.close()
+            for e in layers.values():
+                e.release()
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        lb.close()
+        for e in layers.values():
+            e.release()
 
 
 # ------------------------------------------------------------------------------------------ N GPUs
@@ -629,13 +857,15 @@ def run_multi(args):
         send_stream = torch.cuda.Stream(dev)
         stream = torch.cuda.current_stream()
 
-    def timed(fn, finish=None):
+    def timed(fn, finish=None, clocks=None):
         for _ in range(args.warmup):
             fn()
         if is_a:
             torch.cuda.synchronize()
         dist.barrier()
         ms = 0.0
+        if clocks is not None:
+            clocks.mark_start()
         if is_a:
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record()
@@ -646,6 +876,8 @@ def run_multi(args):
             t1.record()
             torch.cuda.synchronize()
             ms = t0.elapsed_time(t1) / args.steps
+        if clocks is not None:
+            clocks.mark_end()
         mt = torch.tensor([ms])
         dist.all_reduce(mt, op=dist.ReduceOp.MAX)
         dist.barrier()
@@ -666,7 +898,7 @@ def run_multi(args):
                 channel.combine(t, out.data_ptr(), stream.cuda_stream, s.data_ptr() if s is not None else 0)
                 return out
         with ClockSampler(local) as clocks:
-            ms = timed(step if is_a else (lambda: None))
+            ms = timed(step if is_a else (lambda: None), clocks=clocks)
         clock_summary = clocks.summary()
         res = {"T": T, "ms": ms}
         if is_a:
@@ -717,8 +949,7 @@ def run_multi(args):
             fi = [i for i in infos[n_a:]]
             busy = [(i["t_reply_ns"] - i["t_seen_ns"]) * 1e-3 for i in fi]
             rt = (a0["t_replies_ns"] - a0["t_ring_ns"]) * 1e-3
-            lat.append({"round_trip_us": rt, "f_busy_us": busy, "signal_us": rt - max(busy),
-                        "ring_to_seen_cross_clock_us": [(i["t_seen_ns"] - a0["t_ring_ns"]) * 1e-3 for i in fi]})
+            lat.append({"round_trip_us": rt, "f_busy_us": busy, "signal_us": rt - max(busy)})
     if is_a:
         channel.check()
     else:
@@ -764,8 +995,6 @@ def run_multi(args):
                               "round_trip_us_p50": round(statistics.median(l["round_trip_us"] for l in lat), 2),
                               "signal_us_p50": round(statistics.median(l["signal_us"] for l in lat), 2),
                               "f_busy_us_p50": round(statistics.median(max(l["f_busy_us"]) for l in lat), 2),
-                              "ring_to_seen_cross_clock_us_p50": round(statistics.median(
-                                  min(l["ring_to_seen_cross_clock_us"]) for l in lat), 2),
                               "note": "signal = A round trip (doorbell release -> combine saw every done flag, A "
                                       "clock) - slowest F's busy time (doorbell seen -> done flag released, F clock): "
                                       "one doorbell plus one done-flag hop; no cross-GPU clock needed"}), flush=True)
@@ -797,9 +1026,10 @@ def main():
     ap.add_argument("--cpu-experts", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=("layer", "fp8-layer", "zipf-sweep"), default="layer",
+    ap.add_argument("--workload", choices=("layer", "fp8-layer", "zipf-sweep", "stack"), default="layer",
                     help="layer: config 2 (MXFP4); fp8-layer: config 4 (FP8 block-scaled); zipf-sweep: config 5, "
-                         "T in 256/1024/4096/16384 with skewed routing, one line per T")
+                         "T in 256/1024/4096/16384 with skewed routing, one line per T; stack: config 3, 8 layers "
+                         "x 2 micro-batches")
     ap.add_argument("--routing", choices=("sigmoid", "zipf"), default=None,
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
@@ -817,6 +1047,8 @@ def main():
         args.routing = "zipf" if args.workload == "zipf-sweep" else ROUTING
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "stack":
+        run_stack(args)
     elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_multi(args)
     elif args.workload == "zipf-sweep":
