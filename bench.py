@@ -829,7 +829,7 @@ def run_multi(args):
         experts = make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + f, dev)
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
-        sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s)
+        sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s, join=n_a if args.join_replicas else 1)
         ep = ("127.0.0.1", server.port)
     eps = [None] * world
     dist.all_gather_object(eps, ep)
@@ -845,6 +845,9 @@ def run_multi(args):
         def feed():
             torch.cuda.set_device(local)
             for s in range(queued):
+                if args.join_replicas:  # one job answers every replica's message of this step
+                    sched.run_device_wait_rows([(a, 0, s + 1) for a in range(n_a)], 0, stream.cuda_stream)
+                    continue
                 for a in range(n_a):
                     sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
 
@@ -961,7 +964,8 @@ def run_multi(args):
             "metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE[KIND], "data": "synthetic",
-            "gpu_launches": args.steps * (4 * n_a + 8 * n_a * n_f), "roofline": None, "cpu_baseline": None,
+            "gpu_launches": args.steps * (4 * n_a + (9 if args.join_replicas else 8 * n_a) * n_f), "roofline": None,
+            "cpu_baseline": None,
             "clocks": clock_summary,
         }
         for res in results:
@@ -975,7 +979,9 @@ def run_multi(args):
                             (f"{n_a}A{n_f}F: config 4 layer per A replica (T={T}, H={H}, {E} experts, top-{K_TOP} "
                              f"softmax, I={I}, FP8 E4M3 with fp32 128x128 block scales)"),
                 "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
-                "expert_bounds": bounds, "routing": args.routing, "l2": "inputs larger than L2, no flush"
+                "expert_bounds": bounds, "routing": args.routing,
+                "f_jobs": "one joined job per step (all replicas' messages)" if args.join_replicas else
+                          "one job per message", "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
             line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
@@ -1034,6 +1040,8 @@ def main():
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
+    ap.add_argument("--join-replicas", action="store_true",
+                    help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
     args = ap.parse_args()
     layer = LAYERS["fp8-layer" if args.workload == "fp8-layer" else "layer"]
     globals().update(layer)

@@ -52,6 +52,7 @@ extern "C" {
 
 #define ASAP_MAX_F 16          /* F ranks one A rank can address */
 #define ASAP_MAX_LOCAL_EXPERTS 256
+#define ASAP_MAX_JOB_ROWS 8 /* messages one F job may answer at once (asap_ffn_*_rows) */
 
 /* Transport geometry: the fields of transport/layout.py:115-125 (Geometry), same meaning. */
 typedef struct {
@@ -226,6 +227,18 @@ int asap_ffn_wait(uint64_t ws_handle, uint64_t bell, uint32_t last_seq, int32_t 
 int asap_ffn_post(uint64_t ws_handle, uint32_t seq, int32_t n, int32_t layer_id, int32_t epoch,
                   void* stream);
 
+/* Joined jobs (the reference's Job with several Rows, transport/server.py:322-337 and scheduler.py:387-436, here
+ * also across A replicas): one F job answers `rows` <= ASAP_MAX_JOB_ROWS messages of the same layer at once, the
+ * experts' weights read once for all of them.  asap_ffn_wait_rows waits for every row's doorbell (arrays of
+ * `rows` entries: doorbell address, last seq, expected epoch); asap_ffn_post_rows is its host-side form.  The
+ * workspace must hold the rows' tokens together (asap_ffn_ws_bytes with n_max = the sum).  A mismatch of the rows'
+ * layers or an overflow writes ASAP_ST_BAD_JOB and an invalid descriptor. */
+int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint32_t* last_seqs,
+                       const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
+                       void* stream);
+int asap_ffn_post_rows(uint64_t ws_handle, int32_t rows, const uint32_t* seqs, const int32_t* ns, int32_t layer_id,
+                       const int32_t* epochs, void* stream);
+
 /* One job (replaces scheduler.py:387-436 run_job + FusedMoE + server.py:340-350 reply):
  * x/ids/w are the row's arena views (server.py:309-320 Row pointers); the token count comes from the
  * workspace's job descriptor. Routed experts [expert_base, expert_base+num_local) only, SwiGLU
@@ -235,6 +248,16 @@ int asap_ffn_post(uint64_t ws_handle, uint32_t seq, int32_t n, int32_t layer_id,
 int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64_t ids, uint64_t w,
                  uint64_t reply_seg, uint64_t reply_done, float swiglu_limit, uint64_t status,
                  uint64_t timeout_ns, void* stream);
+
+/* One message's arena views and reply target (asap_ffn_job's x/ids/w/reply_seg/reply_done). */
+typedef struct {
+  uint64_t x, ids, w, reply_seg, reply_done;
+} asap_ffn_row_t;
+
+/* asap_ffn_job over the `rows` messages of a joined job (their tokens numbered in row order); each row's reply goes
+ * to its own segment and done flag (= that row's seq). */
+int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t rows, const asap_ffn_row_t* row_views,
+                      float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream);
 
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
  * stream around its 5 stages (routing, quantise+permute, gemm1, gemm2, reduce+reply); last_timing waits

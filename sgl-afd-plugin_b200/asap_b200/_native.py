@@ -21,6 +21,7 @@ ST_NAMES = {
 }
 MAX_F = 16
 MAX_LOCAL_EXPERTS = 256
+MAX_JOB_ROWS = 8
 
 
 class AsapError(RuntimeError):
@@ -41,6 +42,10 @@ class Offsets_t(ctypes.Structure):
 class Mxfp4Experts_t(ctypes.Structure):
     _fields_ = [("num_local", c_int32), ("expert_base", c_int32), ("hidden", c_int32), ("inter", c_int32),
                 ("w13", c_uint64), ("w13_sf", c_uint64), ("w2", c_uint64), ("w2_sf", c_uint64)]
+
+
+class FfnRow_t(ctypes.Structure):
+    _fields_ = [(n, c_uint64) for n in ("x", "ids", "w", "reply_seg", "reply_done")]
 
 
 class Fp8Experts_t(ctypes.Structure):
@@ -86,6 +91,12 @@ _SIGS = {
     "asap_ffn_ws_release": (c_int32, [c_uint64]),
     "asap_ffn_wait": (c_int32, [c_uint64, c_uint64, c_uint32, c_int32, c_int32, c_uint64, c_uint64, c_void_p]),
     "asap_ffn_post": (c_int32, [c_uint64, c_uint32, c_int32, c_int32, c_int32, c_void_p]),
+    "asap_ffn_wait_rows": (c_int32, [c_uint64, c_int32, POINTER(c_uint64), POINTER(c_uint32), POINTER(c_int32), c_int32,
+                                     c_uint64, c_uint64, c_void_p]),
+    "asap_ffn_post_rows": (c_int32, [c_uint64, c_int32, POINTER(c_uint32), POINTER(c_int32), c_int32,
+                                     POINTER(c_int32), c_void_p]),
+    "asap_ffn_job_rows": (c_int32, [c_uint64, c_uint64, c_int32, POINTER(FfnRow_t), c_float, c_uint64, c_uint64,
+                                    c_void_p]),
     "asap_ffn_job": (c_int32, [c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_float,
                                c_uint64, c_uint64, c_void_p]),
     "asap_ffn_enable_timing": (c_int32, [c_uint64, c_int32]),

@@ -10,6 +10,11 @@ queued) and reply ms (here part of the expert chain, reported as 0).
 
 Everything a job needs on the GPU is derived on the device from the job descriptor (n, seq), so a job can be
 enqueued before its doorbell rings (``run_device_wait``) and the chain can be captured in a CUDA graph.
+
+A job may answer several messages of one layer at once (``join`` > 1): the reference's ``Job`` already carries a
+list of ``Row``s (the A ranks of a group, server.py:322-337, concatenated by ``run_job``, scheduler.py:399-405);
+here the rows may also come from different A replicas (``run_device_wait_rows``), so that small messages share
+one read of the experts' weights.
 """
 
 from __future__ import annotations
@@ -78,7 +83,7 @@ class FfnScheduler:
     """The experts of one F rank (``experts[layer_id]``) answering the jobs of ``server``."""
 
     def __init__(self, server: FfnServer, experts: Dict[int, Mxfp4Experts], *, swiglu_limit: float = 0.0,
-                 timeout_s: float = 60.0, timing: bool = False):
+                 timeout_s: float = 60.0, timing: bool = False, join: int = 1):
         g = server.g
         if g.group != 1:
             raise NotImplementedError("AFD supports attention TP size 1 only (group=1), as the reference's "
@@ -96,10 +101,14 @@ class FfnScheduler:
         self.swiglu_limit = float(swiglu_limit or 0.0)
         self.timeout_ns = int(timeout_s * 1e9)
         self.local = range(first.expert_base, first.expert_base + first.num_local)
-        nbytes = N.lib().asap_ffn_ws_bytes(g.n_max, g.topk, first.num_local, first.hidden, first.inter)
+        if not 1 <= join <= N.MAX_JOB_ROWS:
+            raise ValueError(f"join must be in [1, {N.MAX_JOB_ROWS}]")
+        self.join = join
+        cap = g.n_max * join  # tokens of one (joined) job
+        nbytes = N.lib().asap_ffn_ws_bytes(cap, g.topk, first.num_local, first.hidden, first.inter)
         self._ws_owner, self.ws = _aligned_empty(nbytes, f"cuda:{self.device}")
         h = ctypes.c_uint64()
-        N.call("asap_ffn_ws_register", self.ws.data_ptr(), g.n_max, g.topk, first.num_local, first.hidden,
+        N.call("asap_ffn_ws_register", self.ws.data_ptr(), cap, g.topk, first.num_local, first.hidden,
                first.inter, ctypes.byref(h))
         self.ws_handle = h.value
         self.status = HostWords(1)
@@ -126,22 +135,40 @@ class FfnScheduler:
         N.call("asap_ffn_job", experts.handle, self.ws_handle, row.x_ptr, row.ids_ptr, row.w_ptr, seg, done,
                ctypes.c_float(self.swiglu_limit), self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
 
+    def _launch_rows(self, experts, rows, targets, stream: int) -> None:
+        views = (N.FfnRow_t * len(rows))(*[N.FfnRow_t(r.x_ptr, r.ids_ptr, r.w_ptr, seg, done)
+                                            for r, (seg, done) in zip(rows, targets)])
+        N.call("asap_ffn_job_rows", experts.handle, self.ws_handle, len(rows), views,
+               ctypes.c_float(self.swiglu_limit), self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
+
     def run_job(self, job: Job, stream: Optional[int] = None) -> None:
-        """One expert chain for the row of one replica's micro-batch (host-poll mode); enqueues GPU work only."""
+        """One expert chain for the rows of one job (host-poll mode; the rows' tokens are answered together, as
+        scheduler.py:399-405 concatenates them); enqueues GPU work only."""
         tic, timer = time.perf_counter(), self.job_timer
         started = timer.start() if timer else None
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
-        row = job.rows[0]
-        target = self.server.reply_target(row)
-        if target is None:  # the A rank reconnected since: its reply is dropped (server.py:343-346)
+        live = [(row, self.server.reply_target(row)) for row in job.rows]
+        live = [(row, t) for row, t in live if t is not None]  # reconnected A ranks: dropped (server.py:343-346)
+        if not live:
             return
-        N.call("asap_ffn_post", self.ws_handle, row.seq & SEQ_MASK, row.n_tokens, row.layer_id, row.epoch,
-               ctypes.c_void_p(stream))
-        self._launch(self.experts[job.layer_id], row, target, stream)
+        if len(live) > self.join:
+            raise ValueError(f"a job of {len(live)} rows needs join >= {len(live)} (this scheduler: {self.join})")
+        rows = [r for r, _ in live]
+        if len(rows) == 1:
+            row, target = live[0]
+            N.call("asap_ffn_post", self.ws_handle, row.seq & SEQ_MASK, row.n_tokens, row.layer_id, row.epoch,
+                   ctypes.c_void_p(stream))
+            self._launch(self.experts[job.layer_id], row, target, stream)
+        else:
+            R = len(rows)
+            N.call("asap_ffn_post_rows", self.ws_handle, R, (ctypes.c_uint32 * R)(*[r.seq & SEQ_MASK for r in rows]),
+                   (ctypes.c_int32 * R)(*[r.n_tokens for r in rows]), job.layer_id,
+                   (ctypes.c_int32 * R)(*[r.epoch for r in rows]), ctypes.c_void_p(stream))
+            self._launch_rows(self.experts[job.layer_id], rows, [t for _, t in live], stream)
         self.layer_calls[job.layer_id] += 1
         if timer:
-            timer.add(row.n_tokens, started, time.perf_counter() - tic)
+            timer.add(sum(r.n_tokens for r in rows), started, time.perf_counter() - tic)
 
     def run_device_wait(self, a: int, slot: int, seq: int, layer_id: int, stream: int) -> None:
         """Enqueue a job for the next message of (a, slot) before it arrives: the chain starts with a bounded
@@ -158,6 +185,33 @@ class FfnScheduler:
                self.g.n_max, self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
         self._launch(self.experts[layer_id], row, target, stream)
         server.advance(a, slot, seq)
+        self.layer_calls[layer_id] += 1
+
+    def run_device_wait_rows(self, messages, layer_id: int, stream: int) -> None:
+        """One joined job over the next messages of several (a, slot) pairs, ``messages`` = [(a, slot, seq), ...]
+        (all of layer ``layer_id``), enqueued before they arrive: the chain starts with one bounded device wait for
+        all their doorbells; every row's reply goes to its own A rank."""
+        server = self.server
+        rows, targets = [], []
+        for a, slot, seq in messages:
+            row = server.row_for(a, slot, seq, self.g.n_max, layer_id)
+            target = server.reply_target(row)
+            if target is not None:
+                rows.append(row)
+                targets.append(target)
+        if not rows:
+            return
+        R = len(rows)
+        if R > self.join:
+            raise ValueError(f"a job of {R} rows needs join >= {R} (this scheduler: {self.join})")
+        N.call("asap_ffn_wait_rows", self.ws_handle, R,
+               (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
+               (ctypes.c_uint32 * R)(*[(r.seq - 1) & SEQ_MASK for r in rows]),
+               (ctypes.c_int32 * R)(*[server.peers[r.a].epoch for r in rows]), self.g.n_max, self.status.ptr,
+               self.timeout_ns, ctypes.c_void_p(stream))
+        self._launch_rows(self.experts[layer_id], rows, targets, stream)
+        for r in rows:
+            server.advance(r.a, r.slot, r.seq)
         self.layer_calls[layer_id] += 1
 
     def rows_of(self, row: Row):

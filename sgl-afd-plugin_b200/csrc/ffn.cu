@@ -30,16 +30,42 @@ struct JobDesc {
   uint32_t sync;     // arrive counter of the finalize grid
   uint64_t t_seen;   // globaltimer (ns) when the doorbell wait saw the message (0: posted by the host)
   uint64_t t_reply;  // globaltimer (ns) when the reply's done flag was released
-  uint32_t pad[6];
+  int32_t rows;      // messages joined in this job (RowState entries after the descriptor)
+  uint32_t pad[5];
 };
 static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
+
+// A job answers up to kMaxJobRows messages at once (rows of several A replicas for the same layer and slot, as the
+// reference's Job joins the Rows of a group, transport/server.py:322-337): tokens are numbered across the rows in
+// row order; each row's state follows the descriptor in the workspace.
+constexpr int kMaxJobRows = ASAP_MAX_JOB_ROWS;
+struct RowState {
+  int32_t n, off;  // tokens of this message and its first job-wide token index
+  uint32_t seq;
+  int32_t layer;
+};
+static_assert(sizeof(RowState) == 16, "RowState is 16 bytes");
+__device__ __forceinline__ const RowState* row_states(const JobDesc* d) {
+  return reinterpret_cast<const RowState*>(d + 1);
+}
+// The row holding job-wide token t and t's index inside it.
+__device__ __forceinline__ int row_of_token(const JobDesc* d, int64_t t, int64_t& local) {
+  const RowState* rs = row_states(d);
+  const int rows = d->rows;
+  int r = 0;
+  for (int i = 1; i < rows; ++i)
+    if (t >= rs[i].off) r = i;
+  local = t - rs[r].off;
+  return r;
+}
 
 constexpr int kPermChunks = 128;  // chunks of pairs the permutation is split into (upper bound)
 
 struct WsLayout {
   int32_t n_max, topk, P, H, I;
   int64_t m_cap;  // rows of the expert-major activation buffers (multiple of 128)
-  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, xtok, xtok_sf, xq, xq_sf, hq, hq_sf, y2, total;
+  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, ids_all, w_all, xtok, xtok_sf, xq, xq_sf, hq, hq_sf, y2,
+      total;
 };
 
 static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
@@ -56,13 +82,15 @@ static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
     off = align_up(off + bytes, 1024);
     return at;
   };
-  L.desc = take(sizeof(JobDesc));
+  L.desc = take(sizeof(JobDesc) + sizeof(RowState) * kMaxJobRows);
   L.ecnt = take(4ull * ASAP_MAX_LOCAL_EXPERTS);
   L.mstart = take(4ull * (ASAP_MAX_LOCAL_EXPERTS + 1));
   L.hist = take(4ull * kPermChunks * ASAP_MAX_LOCAL_EXPERTS);
   L.pair_pos = take(4ull * n_max * topk);
   L.row_tok = take(4ull * L.m_cap);
   L.row_w = take(4ull * L.m_cap);
+  L.ids_all = take(4ull * n_max * topk);  // ids / weights of a multi-row job, gathered in token order
+  L.w_all = take(4ull * n_max * topk);
   L.xtok = take((uint64_t)n_max * H);
   L.xtok_sf = take((uint64_t)n_max * (H / 32));
   L.xq = take((uint64_t)L.m_cap * H);
@@ -83,51 +111,125 @@ __host__ __device__ __forceinline__ uint64_t sf_atom_off(int64_t r, int kb, int 
 }
 
 // ------------------------------------------------------------------ K3: doorbell wait / host post
-__global__ void ffn_wait_kernel(JobDesc* d, const uint64_t* bell, uint32_t last_seq, int32_t expect_epoch,
-                                int32_t n_max, uint64_t status, uint64_t timeout_ns) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const uint64_t deadline = globaltimer_ns() + timeout_ns;
-  uint64_t word = 0;
-  for (;;) {
-    word = ld_relaxed_sys_u64(bell);
-    if ((int32_t)((uint32_t)word - last_seq) > 0) break;
-    if (globaltimer_ns() > deadline) {
-      report(status, status_word(ASAP_ST_DOORBELL_TIMEOUT, 0, 0, last_seq + 1u));
-      d->valid = 0;
-      d->n = 0;
-      return;
+struct WaitArgs {
+  JobDesc* d;
+  int32_t rows, n_max, capacity;  // messages to wait for; tokens per message; tokens per job (workspace)
+  const uint64_t* bell[kMaxJobRows];
+  uint32_t last_seq[kMaxJobRows];
+  int32_t epoch[kMaxJobRows];
+  uint64_t status, timeout_ns;
+};
+
+// One warp; lane r spins (bounded) on row r's doorbell until its seq is cyclically ahead of last_seq[r], then
+// decodes it.  The job is valid when every doorbell came, every epoch and size checks, all rows name the same
+// layer and the tokens fit the workspace.
+__global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
+  JobDesc* d = a.d;
+  RowState* rs = reinterpret_cast<RowState*>(d + 1);
+  const int lane = threadIdx.x;
+  int ok = 1, n = 0, layer = 0, epoch = 0;
+  uint32_t seq = 0;
+  if (lane < a.rows) {
+    const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
+    uint64_t word = 0;
+    for (;;) {
+      word = ld_relaxed_sys_u64(a.bell[lane]);
+      if ((int32_t)((uint32_t)word - a.last_seq[lane]) > 0) break;
+      if (globaltimer_ns() > deadline) {
+        report(a.status, status_word(ASAP_ST_DOORBELL_TIMEOUT, lane, 0, a.last_seq[lane] + 1u));
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
     }
-    __nanosleep(64);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    seq = (uint32_t)word;
+    n = (int32_t)((word >> 32) & kMaxTokens);
+    layer = (int32_t)((word >> 49) & kMaxLayer);
+    epoch = (int32_t)(word >> 59);
+    if (ok && (epoch != a.epoch[lane] || n < 1 || n > a.n_max)) {
+      report(a.status, status_word(ASAP_ST_BAD_DOORBELL, lane, 0, seq));
+      ok = 0;
+    }
   }
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  d->t_seen = globaltimer_ns();
-  const uint32_t seq = (uint32_t)word;
-  const int32_t n = (int32_t)((word >> 32) & kMaxTokens);
-  const int32_t layer = (int32_t)((word >> 49) & kMaxLayer);
-  const int32_t epoch = (int32_t)(word >> 59);
-  d->seq = seq;
-  d->layer = layer;
-  d->epoch = epoch;
+  ok = __all_sync(0xffffffffu, ok);
+  const int layer0 = __shfl_sync(0xffffffffu, layer, 0);
+  const bool same_layer = __all_sync(0xffffffffu, lane >= a.rows || layer == layer0);
+  int incl = ok ? n : 0;  // inclusive scan of the row sizes
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  if (lane < a.rows) rs[lane] = RowState{ok ? n : 0, incl - (ok ? n : 0), seq, layer};
+  const uint32_t seq0 = __shfl_sync(0xffffffffu, seq, 0);
+  const int epoch0 = __shfl_sync(0xffffffffu, epoch, 0);
+  if (lane == 0) {
+    d->t_seen = globaltimer_ns();
+    d->t_reply = 0;
+    d->seq = seq0;
+    d->layer = layer0;
+    d->epoch = epoch0;
+    d->sync = 0;
+    d->rows = a.rows;
+    bool valid = ok != 0;
+    if (valid && (!same_layer || total > a.capacity)) {
+      report(a.status, status_word(ASAP_ST_BAD_JOB, 0, 0, seq0));
+      valid = false;
+    }
+    d->n = valid ? total : 0;
+    d->valid = valid ? 1 : 0;
+  }
+}
+
+struct PostArgs {
+  JobDesc* d;
+  int32_t rows, layer;
+  uint32_t seq[kMaxJobRows];
+  int32_t n[kMaxJobRows], epoch[kMaxJobRows];
+};
+
+__global__ void ffn_post_kernel(const __grid_constant__ PostArgs a) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  JobDesc* d = a.d;
+  RowState* rs = reinterpret_cast<RowState*>(d + 1);
+  int off = 0;
+  for (int r = 0; r < a.rows; ++r) {
+    rs[r] = RowState{a.n[r], off, a.seq[r], a.layer};
+    off += a.n[r];
+  }
+  d->seq = a.seq[0];
+  d->n = off;
+  d->layer = a.layer;
+  d->epoch = a.epoch[0];
   d->sync = 0;
-  if (epoch != expect_epoch || n < 1 || n > n_max) {
-    report(status, status_word(ASAP_ST_BAD_DOORBELL, 0, 0, seq));
-    d->valid = 0;
-    d->n = 0;
-    return;
-  }
-  d->n = n;
+  d->t_seen = 0;
+  d->t_reply = 0;
+  d->rows = a.rows;
   d->valid = 1;
 }
 
-__global__ void ffn_post_kernel(JobDesc* d, uint32_t seq, int32_t n, int32_t layer, int32_t epoch) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  d->seq = seq;
-  d->n = n;
-  d->layer = layer;
-  d->epoch = epoch;
-  d->sync = 0;
-  d->t_seen = 0;
-  d->valid = 1;
+// Multi-row jobs: the rows' ids and weights copied into job-wide [n, topk] arrays for the permutation.
+struct GatherArgs {
+  const JobDesc* desc;
+  int32_t topk;
+  const int32_t* ids[kMaxJobRows];
+  const float* w[kMaxJobRows];
+  int32_t* ids_all;
+  float* w_all;
+};
+
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ GatherArgs p) {
+  if (!p.desc->valid) return;
+  const int64_t total = (int64_t)p.desc->n * p.topk;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    int64_t local;
+    const int r = row_of_token(p.desc, q / p.topk, local);
+    const int64_t src = local * p.topk + q % p.topk;
+    p.ids_all[q] = p.ids[r][src];
+    p.w_all[q] = p.w[r][src];
+  }
 }
 
 // ------------------------------------------------------------------ K3b-1: expert-major permutation
@@ -258,7 +360,7 @@ struct QuantArgs {
   const JobDesc* desc;
   const int32_t* mstart;
   int32_t P, H;
-  const __nv_bfloat16* x;  // [n, H] in the RecvArena
+  const __nv_bfloat16* x[kMaxJobRows];  // [n_r, H] per message, in the RecvArena
   const int32_t* row_tok;
   uint8_t* xtok;     // [n_max, H] E4M3, one row per token
   uint8_t* xtok_sf;  // [n_max, H/32] E8M0, row-major
@@ -295,7 +397,9 @@ __global__ void __launch_bounds__(256) quant_tok_kernel(const __grid_constant__ 
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = p.H, kblocks = H / 32;
   for (int64_t t = gwarp; t < n; t += nwarps) {
-    const uint4* src = reinterpret_cast<const uint4*>(p.x + t * H);
+    int64_t local;
+    const int r = row_of_token(p.desc, t, local);
+    const uint4* src = reinterpret_cast<const uint4*>(p.x[r] + local * H);
     for (int kb = lane; kb < kblocks; kb += 32) {
       float v[32];
 #pragma unroll
@@ -647,8 +751,8 @@ struct FinalArgs {
   int32_t topk, H;
   const int32_t* pair_pos;    // [n, topk]
   const __nv_bfloat16* y2;    // [m_cap, H], rows already weighted
-  __nv_bfloat16* reply_seg;   // A's ResultArena seg(f, slot) (peer memory in a multi-GPU deployment)
-  uint32_t* reply_done;       // A's done flag (f, slot); NULL: no flag
+  __nv_bfloat16* reply_seg[kMaxJobRows];  // each message's A ResultArena seg(f, slot) (peer memory across GPUs)
+  uint32_t* reply_done[kMaxJobRows];      // each message's done flag (f, slot); NULL: no flag
   JobDesc* desc_rw;
 };
 
@@ -660,6 +764,9 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = p.H, nvec = H / 8;
   for (int64_t t = gwarp; t < n; t += nwarps) {
+    int64_t local;
+    const int row = row_of_token(p.desc, t, local);
+    __nv_bfloat16* dst = p.reply_seg[row] + local * H;
     // this token's local pairs, in ascending slot order (the summation order)
     const int32_t mine = lane < p.topk ? p.pair_pos[t * p.topk + lane] : -1;
     const uint32_t vmask = __ballot_sync(0xffffffffu, mine >= 0);
@@ -706,7 +813,7 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
       __nv_bfloat162* rh = reinterpret_cast<__nv_bfloat162*>(&r);
 #pragma unroll
       for (int i = 0; i < 4; ++i) rh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-      *reinterpret_cast<uint4*>(p.reply_seg + t * H + (int64_t)c * 8) = r;
+      *reinterpret_cast<uint4*>(dst + (int64_t)c * 8) = r;
     }
   }
   // Reply rows visible to A before its done flag (server.py:347-350 ordering).
@@ -719,10 +826,10 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
   __syncthreads();
   if (last && threadIdx.x == 0) {
     p.desc_rw->t_reply = globaltimer_ns();
-    if (p.reply_done) {
-      __threadfence_system();
-      st_release_sys_u32(p.reply_done, p.desc->seq);
-    }
+    __threadfence_system();
+    const RowState* rs = row_states(p.desc);
+    for (int r = 0; r < p.desc->rows; ++r)
+      if (p.reply_done[r]) st_release_sys_u32(p.reply_done[r], rs[r].seq);
   }
 }
 
@@ -817,16 +924,18 @@ static int ensure_gemm_attrs() {
 
 // K5b launch shared by both weight kinds; `mark` records the job's last timing event.
 template <class Mark>
-static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_t* B, uint64_t reply_seg,
-                    uint64_t reply_done, cudaStream_t st, int sms, Mark& mark) {
+static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_t* B, int R,
+                    const asap_ffn_row_t* rows, cudaStream_t st, int sms, Mark& mark) {
   FinalArgs fa{};
   fa.desc = desc;
   fa.topk = L.topk;
   fa.H = L.H;
   fa.pair_pos = pa.pair_pos;
   fa.y2 = (const __nv_bfloat16*)(B + L.y2);
-  fa.reply_seg = (__nv_bfloat16*)reply_seg;
-  fa.reply_done = (uint32_t*)reply_done;
+  for (int r = 0; r < R; ++r) {
+    fa.reply_seg[r] = (__nv_bfloat16*)rows[r].reply_seg;
+    fa.reply_done[r] = (uint32_t*)rows[r].reply_done;
+  }
   fa.desc_rw = desc;
   finalize_reply_kernel<<<sms * 4, 256, 0, st>>>(fa);
   ASAP_CHECK_LAUNCH("finalize_reply_kernel");
@@ -975,41 +1084,88 @@ int asap_ffn_ws_release(uint64_t handle) {
   return ASAP_OK;
 }
 
-int asap_ffn_wait(uint64_t ws_handle, uint64_t bell, uint32_t last_seq, int32_t expect_epoch, int32_t n_max,
-                  uint64_t status, uint64_t timeout_ns, void* stream) {
+int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint32_t* last_seqs,
+                       const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
+                       void* stream) {
   WsHandle* w = get_ws(ws_handle);
-  if (!w || !bell || (bell & 7)) {
-    set_error("asap_ffn_wait: unknown workspace handle or misaligned doorbell");
+  if (!w || rows < 1 || rows > kMaxJobRows || !bells || !last_seqs || !expect_epochs) {
+    set_error("asap_ffn_wait: unknown workspace handle, NULL arrays or rows %d outside [1, %d]", rows, kMaxJobRows);
     return ASAP_EINVAL;
   }
   if (n_max < 1 || n_max > w->L.n_max) {
     set_error("asap_ffn_wait: n_max %d outside the workspace's %d", n_max, w->L.n_max);
     return ASAP_EINVAL;
   }
-  ffn_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((JobDesc*)(w->base + w->L.desc), (const uint64_t*)bell,
-                                                       last_seq, expect_epoch, n_max, status, timeout_ns);
+  WaitArgs a{};
+  a.d = (JobDesc*)(w->base + w->L.desc);
+  a.rows = rows;
+  a.n_max = n_max;
+  a.capacity = w->L.n_max;
+  for (int r = 0; r < rows; ++r) {
+    if (!bells[r] || (bells[r] & 7)) {
+      set_error("asap_ffn_wait: doorbell %d is NULL or misaligned", r);
+      return ASAP_EINVAL;
+    }
+    a.bell[r] = (const uint64_t*)bells[r];
+    a.last_seq[r] = last_seqs[r];
+    a.epoch[r] = expect_epochs[r];
+  }
+  a.status = status;
+  a.timeout_ns = timeout_ns;
+  ffn_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(a);
   ASAP_CHECK_LAUNCH("ffn_wait_kernel");
   return ASAP_OK;
 }
 
-int asap_ffn_post(uint64_t ws_handle, uint32_t seq, int32_t n, int32_t layer_id, int32_t epoch, void* stream) {
+int asap_ffn_wait(uint64_t ws_handle, uint64_t bell, uint32_t last_seq, int32_t expect_epoch, int32_t n_max,
+                  uint64_t status, uint64_t timeout_ns, void* stream) {
+  return asap_ffn_wait_rows(ws_handle, 1, &bell, &last_seq, &expect_epoch, n_max, status, timeout_ns, stream);
+}
+
+int asap_ffn_post_rows(uint64_t ws_handle, int32_t rows, const uint32_t* seqs, const int32_t* ns, int32_t layer_id,
+                       const int32_t* epochs, void* stream) {
   WsHandle* w = get_ws(ws_handle);
-  if (!w) {
-    set_error("asap_ffn_post: unknown workspace handle");
+  if (!w || rows < 1 || rows > kMaxJobRows || !seqs || !ns || !epochs) {
+    set_error("asap_ffn_post: unknown workspace handle, NULL arrays or rows %d outside [1, %d]", rows, kMaxJobRows);
     return ASAP_EINVAL;
   }
-  if (n < 1 || n > w->L.n_max) {
-    set_error("asap_ffn_post: n_tokens %d outside [1, %d]", n, w->L.n_max);
+  PostArgs a{};
+  a.d = (JobDesc*)(w->base + w->L.desc);
+  a.rows = rows;
+  a.layer = layer_id;
+  int64_t total = 0;
+  for (int r = 0; r < rows; ++r) {
+    if (ns[r] < 1) {
+      set_error("asap_ffn_post: n_tokens %d of row %d below 1", ns[r], r);
+      return ASAP_EINVAL;
+    }
+    total += ns[r];
+    a.seq[r] = seqs[r];
+    a.n[r] = ns[r];
+    a.epoch[r] = epochs[r];
+  }
+  if (total > w->L.n_max) {
+    set_error("asap_ffn_post: %lld tokens exceed the workspace's %d", (long long)total, w->L.n_max);
     return ASAP_EINVAL;
   }
-  ffn_post_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((JobDesc*)(w->base + w->L.desc), seq, n, layer_id, epoch);
+  ffn_post_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(a);
   ASAP_CHECK_LAUNCH("ffn_post_kernel");
   return ASAP_OK;
+}
+
+int asap_ffn_post(uint64_t ws_handle, uint32_t seq, int32_t n, int32_t layer_id, int32_t epoch, void* stream) {
+  return asap_ffn_post_rows(ws_handle, 1, &seq, &n, layer_id, &epoch, stream);
 }
 
 int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64_t ids, uint64_t w,
                  uint64_t reply_seg, uint64_t reply_done, float swiglu_limit, uint64_t status, uint64_t timeout_ns,
                  void* stream) {
+  const asap_ffn_row_t row = {x, ids, w, reply_seg, reply_done};
+  return asap_ffn_job_rows(experts_handle, ws_handle, 1, &row, swiglu_limit, status, timeout_ns, stream);
+}
+
+int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, const asap_ffn_row_t* rows,
+                      float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream) {
   ExpertsHandle* eh = get_experts(experts_handle);
   WsHandle* wh = get_ws(ws_handle);
   if (!eh || !wh) {
@@ -1023,9 +1179,17 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
               E.hidden, E.inter, L.P, L.H, L.I);
     return ASAP_EINVAL;
   }
-  if (!x || !ids || !w || !reply_seg || (x & 15) || (reply_seg & 15) || (reply_done & 3)) {
-    set_error("asap_ffn_job: x/reply_seg must be 16-byte aligned and non-NULL");
+  if (R < 1 || R > kMaxJobRows || !rows) {
+    set_error("asap_ffn_job: rows %d outside [1, %d] or NULL", R, kMaxJobRows);
     return ASAP_EINVAL;
+  }
+  for (int r = 0; r < R; ++r) {
+    const asap_ffn_row_t& q = rows[r];
+    if (!q.x || !q.ids || !q.w || !q.reply_seg || (q.x & 15) || (q.reply_seg & 15) || (q.reply_done & 3) ||
+        (q.ids & 3) || (q.w & 3)) {
+      set_error("asap_ffn_job: row %d: x/reply_seg must be 16-byte aligned and non-NULL", r);
+      return ASAP_EINVAL;
+    }
   }
   int rc = ensure_gemm_attrs();
   if (rc) return rc;
@@ -1036,8 +1200,8 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
 
   PermArgs pa{};
   pa.desc = desc;
-  pa.ids = (const int32_t*)ids;
-  pa.w = (const float*)w;
+  pa.ids = R == 1 ? (const int32_t*)rows[0].ids : (const int32_t*)(B + L.ids_all);
+  pa.w = R == 1 ? (const float*)rows[0].w : (const float*)(B + L.w_all);
   pa.topk = L.topk;
   pa.P = L.P;
   pa.expert_base = E.expert_base;
@@ -1058,6 +1222,19 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
     set_error("asap_ffn_job: internal error, a permutation buffer is unset");
     return ASAP_EINVAL;
   }
+  if (R > 1) {
+    GatherArgs ga{};
+    ga.desc = desc;
+    ga.topk = L.topk;
+    for (int r = 0; r < R; ++r) {
+      ga.ids[r] = (const int32_t*)rows[r].ids;
+      ga.w[r] = (const float*)rows[r].w;
+    }
+    ga.ids_all = (int32_t*)(B + L.ids_all);
+    ga.w_all = (float*)(B + L.w_all);
+    gather_rows_kernel<<<sms * 2, 256, 0, st>>>(ga);
+    ASAP_CHECK_LAUNCH("gather_rows_kernel");
+  }
   route_count_kernel<<<kPermChunks, 256, 0, st>>>(pa);
   ASAP_CHECK_LAUNCH("route_count_kernel");
   route_scan_kernel<<<1, ASAP_MAX_LOCAL_EXPERTS, 0, st>>>(pa);
@@ -1071,7 +1248,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   qa.mstart = pa.mstart;
   qa.P = L.P;
   qa.H = L.H;
-  qa.x = (const __nv_bfloat16*)x;
+  for (int r = 0; r < R; ++r) qa.x[r] = (const __nv_bfloat16*)rows[r].x;
   qa.row_tok = pa.row_tok;
   qa.xtok = B + L.xtok;
   qa.xtok_sf = B + L.xtok_sf;
@@ -1118,7 +1295,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
     gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
     ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<1>");
     mark(4);
-    return finalize(desc, L, pa, B, reply_seg, reply_done, st, sms, mark);
+    return finalize(desc, L, pa, B, R, rows, st, sms, mark);
   }
   quant_tok_kernel<<<sms * 4, 256, 0, st>>>(qa);
   ASAP_CHECK_LAUNCH("quant_tok_kernel");
@@ -1164,7 +1341,7 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
   mark(4);
 
-  return finalize(desc, L, pa, B, reply_seg, reply_done, st, sms, mark);
+  return finalize(desc, L, pa, B, R, rows, st, sms, mark);
 }
 
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable) {

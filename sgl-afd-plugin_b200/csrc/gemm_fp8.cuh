@@ -325,7 +325,9 @@ __global__ void __launch_bounds__(256) quant_tok_fp8_kernel(const __grid_constan
   const int H = p.H;
   float* sf = reinterpret_cast<float*>(p.xtok_sf);
   for (int64_t t = gwarp; t < n; t += nwarps) {
-    const __nv_bfloat16* src = p.x + t * H;
+    int64_t local;
+    const int r = row_of_token(p.desc, t, local);
+    const __nv_bfloat16* src = p.x[r] + local * H;
     for (int base = 0; base < H; base += 256) {
       const uint4 u = *reinterpret_cast<const uint4*>(src + base + lane * 8);
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
