@@ -390,7 +390,7 @@ def run_single(args):
                    "l2": f"inputs larger than L2 (x {T * H * 2 / 1e6:.0f} MB, weights {experts.nbytes / 1e9:.1f} GB), "
                          "no flush"},
         "e2e": e2e,
-        "gpu_launches": args.steps * 12,
+        "gpu_launches": args.steps * 13,  # dispatch 2 + F chain 9 + combine 2 (cuBLAS shared expert not counted)
         "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)" if KIND == "mxfp4" else
                      "moe_gemm_fp8_kernel<0> (GEMM1, block-scale promotion + SwiGLU + FP8 requant)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
@@ -610,7 +610,7 @@ def run_sweep(args):
             "f_rows_per_s": round(sum(rows) / statistics.median(busy), 1),
             "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4), "f0_kernels_ms": f0_ms,
             "weights_gb_read_per_step": round(E * (2 * I * H + H * I) * (0.5 + 1 / 32) / 1e9, 3),
-            "e2e": None, "gpu_launches": args.steps * (4 + 8 * n_f), "roofline": None, "cpu_baseline": None,
+            "e2e": None, "gpu_launches": args.steps * (4 + 9 * n_f), "roofline": None, "cpu_baseline": None,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -759,7 +759,7 @@ def run_stack(args):
                        "a_replicas": n_a, "f_ranks": n_f, "layers": L, "parallelism": f"{n_a}A{n_f}F",
                        "expert_bounds": bounds},
             "layer_tokens_per_s": round(n_a * T * L / (ms * 1e-3), 1), "output_finite": finite,
-            "e2e": None, "gpu_launches": args.steps * L * 2 * (4 + 8 * n_f) * n_a,
+            "e2e": None, "gpu_launches": args.steps * L * 2 * (4 + 9 * n_f) * n_a,
             "roofline": None, "cpu_baseline": None, "clocks": clocks_summary,
         }
         print(json.dumps(line), flush=True)
@@ -964,7 +964,7 @@ def run_multi(args):
             "metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE[KIND], "data": "synthetic",
-            "gpu_launches": args.steps * (4 * n_a + (9 if args.join_replicas else 8 * n_a) * n_f), "roofline": None,
+            "gpu_launches": args.steps * (4 * n_a + (10 if args.join_replicas else 9 * n_a) * n_f), "roofline": None,
             "cpu_baseline": None,
             "clocks": clock_summary,
         }

@@ -1,0 +1,65 @@
+"""Host-side pieces of bench.py on CPU: topologies, expert splits, the routing generators (config 2 sigmoid,
+config 4 softmax, config 5 Zipf), the clock-sample filter and the config-1 CPU timing."""
+
+import time
+
+import numpy as np
+import pytest
+import torch
+
+import bench
+
+
+def test_topology_and_expert_bounds():
+    assert bench.topology("half", 2) == (1, 1)
+    assert bench.topology("half", 8) == (4, 4)
+    assert bench.topology("2a6f", 8) == (2, 6)
+    assert bench.topology("2a4f", 6) == (2, 4)
+    with pytest.raises(SystemExit):
+        bench.topology("2a6f", 6)
+    b = bench.expert_bounds(6)
+    assert b[0] == 0 and b[-1] == 256 and sorted(np.diff(b)) == [42, 42, 43, 43, 43, 43]
+    assert bench.expert_bounds(4) == [0, 64, 128, 192, 256]
+
+
+def test_routing_generators():
+    saved = {k: getattr(bench, k) for k in ("E", "K_TOP", "ROUTING")}
+    try:
+        for routing, E, k in (("sigmoid", 256, 8), ("softmax", 64, 6)):
+            bench.E, bench.K_TOP, bench.ROUTING = E, k, routing
+            ids, w = bench.make_routing(512, 3, "cpu")
+            assert ids.shape == (512, k) and ids.dtype == torch.int32 and w.dtype == torch.float32
+            assert torch.all((ids >= 0) & (ids < E))
+            assert torch.all(torch.tensor([len(set(r.tolist())) == k for r in ids]))  # distinct experts per token
+            assert torch.allclose(w.sum(1), torch.ones(512), atol=1e-5)
+        bench.E, bench.K_TOP = 256, 8
+        ids, w = bench.zipf_routing(20000, 1, "cpu")
+        ids2, _ = bench.zipf_routing(20000, 2, "cpu")
+        c1 = torch.bincount(ids.flatten().long(), minlength=256)
+        c2 = torch.bincount(ids2.flatten().long(), minlength=256)
+        assert int(c1.argmax()) == int(c2.argmax())  # popularity is a property of the model, not of the seed
+        assert c1.max() > 0.8 * 20000  # the top expert of Zipf(1.2) is in most tokens' top-8
+        assert torch.all(torch.tensor([len(set(r.tolist())) == 8 for r in ids[:500]]))
+        assert torch.allclose(w.sum(1), torch.ones(20000), atol=1e-5)
+    finally:
+        for k, v in saved.items():
+            setattr(bench, k, v)
+
+
+def test_clock_sampler_window():
+    c = bench.ClockSampler(0)
+    now = time.time()
+    c.t_start, c.t_end = now, now + 0.2
+    line = "0, {}, 1965, 700.0, 0x0, Not Active, Not Active, Not Active, {}"
+    c.lines = [(now - 1.0, line.format(1000, "Active")), (now + 0.05, line.format(1965, "Not Active")),
+               (now + 0.15, line.format(1950, "Active"))]
+    s = c.summary()
+    assert s["samples"] == 2 and s["sm_mhz"] == pytest.approx(1957.5) and s["reasons"] == ["sw_power_cap"]
+    c.t_start, c.t_end = now + 0.3, now + 0.31  # no sample inside (a region shorter than the period): nearest
+    s = c.summary()
+    assert s["samples"] == 2 and s["window"].startswith("nearest")
+
+
+def test_cpu_config1_runs():
+    r = bench.cpu_config1(reps=1)
+    assert r["value"] > 0 and r["unit"] == "tokens/s"
