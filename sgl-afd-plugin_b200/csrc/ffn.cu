@@ -64,8 +64,7 @@ constexpr int kPermChunks = 128;  // chunks of pairs the permutation is split in
 struct WsLayout {
   int32_t n_max, topk, P, H, I;
   int64_t m_cap;  // rows of the expert-major activation buffers (multiple of 128)
-  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, ids_all, w_all, xtok, xtok_sf, xq, xq_sf, hq, hq_sf, y2,
-      total;
+  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, ids_all, w_all, xq, xq_sf, hq, hq_sf, y2, total;
 };
 
 static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
@@ -91,8 +90,6 @@ static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
   L.row_w = take(4ull * L.m_cap);
   L.ids_all = take(4ull * n_max * topk);  // ids / weights of a multi-row job, gathered in token order
   L.w_all = take(4ull * n_max * topk);
-  L.xtok = take((uint64_t)n_max * H);
-  L.xtok_sf = take((uint64_t)n_max * (H / 32));
   L.xq = take((uint64_t)L.m_cap * H);
   L.xq_sf = take((uint64_t)L.m_cap * (H / 32));
   L.hq = take((uint64_t)L.m_cap * I);
@@ -358,14 +355,12 @@ __global__ void __launch_bounds__(32) route_place_kernel(const __grid_constant__
 // ------------------------------------------------------------------ K3b-2: gather + MXFP8 quantisation
 struct QuantArgs {
   const JobDesc* desc;
-  const int32_t* mstart;
-  int32_t P, H;
+  int32_t H, topk;
+  int64_t m_cap;
   const __nv_bfloat16* x[kMaxJobRows];  // [n_r, H] per message, in the RecvArena
-  const int32_t* row_tok;
-  uint8_t* xtok;     // [n_max, H] E4M3, one row per token
-  uint8_t* xtok_sf;  // [n_max, H/32] E8M0, row-major
-  uint8_t* xq;       // [m_cap, H] E4M3, expert-major
-  uint8_t* xq_sf;    // scale atoms [m_cap/128][H/128][512]
+  const int32_t* pair_pos;              // [n, topk] permuted row of each (token, slot), -1 when not local
+  uint8_t* xq;                          // [m_cap, H] E4M3, expert-major
+  uint8_t* xq_sf;                       // MXFP8: scale atoms [m_cap/128][H/128][512]; FP8: fp32 [H/128][m_cap]
 };
 
 // Quantise 32 consecutive fp32 values to E4M3 with one E8M0 scale; returns the scale byte.
@@ -387,9 +382,10 @@ __device__ __forceinline__ uint32_t mx_quant32(const float (&v)[32], uint4& lo, 
   return sb;
 }
 
-// Every token once: bf16 row -> E4M3 row + E8M0 scale per 32 (OCP MX rule).  One warp per token, a lane per
-// 32-value block.
-__global__ void __launch_bounds__(256) quant_tok_kernel(const __grid_constant__ QuantArgs p) {
+// Every token once: bf16 row -> E4M3 codes + one E8M0 scale per 32 values (OCP MX rule), stored straight into
+// each of the token's local pair rows of the expert-major buffer (rows and scale atoms), so no intermediate
+// per-token copy is written and read back.  One warp per token; lane L quantises the 32-value blocks L, L+32, ...
+__global__ void __launch_bounds__(256) quant_permute_kernel(const __grid_constant__ QuantArgs p) {
   if (!p.desc->valid) return;
   const int n = p.desc->n;
   const int lane = threadIdx.x & 31;
@@ -397,50 +393,46 @@ __global__ void __launch_bounds__(256) quant_tok_kernel(const __grid_constant__ 
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = p.H, kblocks = H / 32;
   for (int64_t t = gwarp; t < n; t += nwarps) {
+    const int32_t mine = lane < p.topk ? p.pair_pos[t * p.topk + lane] : -1;
+    const uint32_t vmask = __ballot_sync(0xffffffffu, mine >= 0);
+    if (!vmask) continue;  // no local expert: nothing to copy
     int64_t local;
     const int r = row_of_token(p.desc, t, local);
     const uint4* src = reinterpret_cast<const uint4*>(p.x[r] + local * H);
-    for (int kb = lane; kb < kblocks; kb += 32) {
-      float v[32];
+    for (int kb0 = 0; kb0 < kblocks; kb0 += 32) {
+      const int kb = kb0 + lane;
+      const bool act = kb < kblocks;
+      uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+      uint32_t sb = 0;
+      if (act) {
+        float v[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 u = src[kb * 4 + c];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        for (int c = 0; c < 4; ++c) {
+          const uint4 u = src[kb * 4 + c];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h[i]);
-          v[c * 8 + 2 * i] = f.x;
-          v[c * 8 + 2 * i + 1] = f.y;
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            v[c * 8 + 2 * i] = f.x;
+            v[c * 8 + 2 * i + 1] = f.y;
+          }
+        }
+        sb = mx_quant32(v, lo, hi);
+      }
+      // the scale bytes of 4 consecutive blocks are 4 consecutive atom bytes: one word, stored by the group's
+      // first lane (kblocks is a multiple of 4, so a group is all active or all inactive)
+      const uint32_t word = sb | (__shfl_down_sync(0xffffffffu, sb, 1) << 8) |
+                            (__shfl_down_sync(0xffffffffu, sb, 2) << 16) | (__shfl_down_sync(0xffffffffu, sb, 3) << 24);
+      for (uint32_t m = vmask; m; m &= m - 1) {
+        const int32_t row = __shfl_sync(0xffffffffu, mine, __ffs(m) - 1);
+        if (act) {
+          uint4* dst = reinterpret_cast<uint4*>(p.xq + (int64_t)row * H + (int64_t)kb * 32);
+          dst[0] = lo;
+          dst[1] = hi;
+          if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(p.xq_sf + sf_atom_off(row, kb, kblocks)) = word;
         }
       }
-      uint4 lo, hi;
-      const uint32_t sb = mx_quant32(v, lo, hi);
-      uint4* dst = reinterpret_cast<uint4*>(p.xtok + t * H + (int64_t)kb * 32);
-      dst[0] = lo;
-      dst[1] = hi;
-      p.xtok_sf[t * kblocks + kb] = (uint8_t)sb;
     }
-  }
-}
-
-// Expert-major copy of the quantised rows: permuted row r <- token row_tok[r] (rows and their scale atoms).
-__global__ void __launch_bounds__(256) permute_copy_kernel(const __grid_constant__ QuantArgs p) {
-  if (!p.desc->valid) return;
-  const int64_t rows = (int64_t)p.mstart[p.P] * 128;
-  const int lane = threadIdx.x & 31;
-  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  const int H = p.H, kblocks = H / 32, nvec = H / 16;
-  for (int64_t r = gwarp; r < rows; r += nwarps) {
-    const int32_t t = p.row_tok[r];
-    if (t < 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(p.xtok + (int64_t)t * H);
-    uint4* dst = reinterpret_cast<uint4*>(p.xq + r * H);
-    for (int c = lane; c < nvec; c += 32) dst[c] = src[c];
-    // the 4 scales of one 128-value chunk are 4 consecutive bytes of the atom: one 32-bit store each
-    const uint32_t* sf = reinterpret_cast<const uint32_t*>(p.xtok_sf + (int64_t)t * kblocks);
-    for (int kc = lane; kc < kblocks / 4; kc += 32)
-      *reinterpret_cast<uint32_t*>(p.xq_sf + sf_atom_off(r, kc * 4, kblocks)) = sf[kc];
   }
 }
 
@@ -460,7 +452,10 @@ constexpr int THREADS = 32 * (2 + NUM_EPI_WARPS);
 constexpr uint32_t TMEM_COLS = 512, TMEM_ACC = 0, TMEM_SFA = 256, TMEM_SFB = TMEM_SFA + 4 * STAGES;
 static_assert(TMEM_SFB + 8 * STAGES <= TMEM_COLS, "scale-factor columns exceed TMEM");
 constexpr int SMEM_TILES = STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES);
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + SMEM_TILES + 1024 /*barriers*/ + 4 * (ASAP_MAX_LOCAL_EXPERTS + 8);
+constexpr int STAGE_OUT_BYTES = NUM_EPI_WARPS * 2048;  // per epilogue warp: 32 rows x 64 B of output in flight
+constexpr int SMEM_BYTES =
+    1024 /*align slack*/ + SMEM_TILES + STAGE_OUT_BYTES + 1024 /*barriers*/ + 4 * (ASAP_MAX_LOCAL_EXPERTS + 8);
+static_assert(SMEM_BYTES <= 232448, "shared memory over the 227 KB per block");
 
 // tcgen05 instruction descriptor, kind::mxf8f6f4 block-scaled: A = E4M3, B = E2M1, both K-major,
 // UE8M0 scales, M x N.  Scale-factor byte ids are OR-ed in per MMA.
@@ -515,6 +510,25 @@ __device__ __forceinline__ void decode_tile(const int32_t* s_mstart, int P, int 
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
 
+// Store a warp's 32 rows x 32 bf16 (lane = row, o = its 32 values packed in pairs) through a 2 KB shared-memory
+// buffer, so that every global store instruction writes 8 rows x 64 contiguous bytes instead of 32 rows x 16 B.
+// 16-byte units are XOR-swizzled by (row >> 1) & 3: both the row-wise writes and the transposed reads touch each
+// group of 4 banks 4 times (the minimum for 512 bytes).  Rows whose bit in `valid` is clear are not stored.
+__device__ __forceinline__ void store_rows_bf16x32(const uint32_t (&o)[16], uint8_t* wb, __nv_bfloat16* out0,
+                                                   int64_t row_stride, uint32_t valid, int lane) {
+  uint4* mine = reinterpret_cast<uint4*>(wb + lane * 64);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) mine[u ^ ((lane >> 1) & 3)] = make_uint4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = i * 8 + (lane >> 2), u = lane & 3;
+    const uint4 val = reinterpret_cast<const uint4*>(wb + row * 64)[u ^ ((row >> 1) & 3)];
+    if ((valid >> row) & 1u) *reinterpret_cast<uint4*>(out0 + row * row_stride + u * 8) = val;
+  }
+  __syncwarp();
+}
+
 // EPI 0: h = silu(gate) * up, quantised to MXFP8 (GEMM1).  EPI 1: bf16(acc * w[row]) (GEMM2).
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_constant__ Params p) {
@@ -524,7 +538,8 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sSFA = sB + STAGES * B_BYTES;
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * SFB_BYTES);
+  uint8_t* sOut = sSFB + STAGES * SFB_BYTES;  // [NUM_EPI_WARPS][2048] output staging
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + STAGE_OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
@@ -689,6 +704,25 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       acc_phase ^= 1u;
+      if constexpr (EPI == 1) {  // warp-cooperative stores: every lane takes part, invalid rows are masked
+        const uint32_t valid_rows = __ballot_sync(0xffffffffu, valid);
+        if (!valid_rows) continue;
+        const float wr = valid ? p.row_w[row] : 0.f;
+        uint8_t* wb = sOut + (warp - 2) * 2048;
+        __nv_bfloat16* out0 = p.out_bf + ((int64_t)m_blk * BM + q * 32) * p.N + (int64_t)n_t * BN + half * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const __nv_bfloat162 b2 =
+                __floats2bfloat162_rn(__uint_as_float(v[c][2 * i]) * wr, __uint_as_float(v[c][2 * i + 1]) * wr);
+            o[i] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          store_rows_bf16x32(o, wb, out0 + c * 32, p.N, valid_rows, lane);
+        }
+        continue;
+      }
       if (!valid) continue;
       if constexpr (EPI == 0) {
         const int I = p.N / 2;
@@ -713,23 +747,6 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
           dst[0] = lo;
           dst[1] = hi;
           p.out_sf[sf_atom_off(row, hcol / 32, kblocks)] = (uint8_t)sb;
-        }
-      } else {
-        const float wr = p.row_w[row];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const __nv_bfloat162 b2 =
-                __floats2bfloat162_rn(__uint_as_float(v[c][2 * i]) * wr, __uint_as_float(v[c][2 * i + 1]) * wr);
-            o[i] = *reinterpret_cast<const uint32_t*>(&b2);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(p.out_bf + row * p.N + (int64_t)n_t * BN + half * 128 + c * 32);
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
-          dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
         }
       }
     }
@@ -1245,20 +1262,16 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
 
   QuantArgs qa{};
   qa.desc = desc;
-  qa.mstart = pa.mstart;
-  qa.P = L.P;
   qa.H = L.H;
+  qa.topk = L.topk;
+  qa.m_cap = L.m_cap;
   for (int r = 0; r < R; ++r) qa.x[r] = (const __nv_bfloat16*)rows[r].x;
-  qa.row_tok = pa.row_tok;
-  qa.xtok = B + L.xtok;
-  qa.xtok_sf = B + L.xtok_sf;
+  qa.pair_pos = pa.pair_pos;
   qa.xq = B + L.xq;
   qa.xq_sf = B + L.xq_sf;
   if (eh->kind == kFp8Block) {
-    quant_tok_fp8_kernel<<<sms * 4, 256, 0, st>>>(qa);
-    ASAP_CHECK_LAUNCH("quant_tok_fp8_kernel");
-    permute_copy_fp8_kernel<<<sms * 4, 256, 0, st>>>(qa, L.m_cap);
-    ASAP_CHECK_LAUNCH("permute_copy_fp8_kernel");
+    quant_permute_fp8_kernel<<<sms * 4, 256, 0, st>>>(qa);
+    ASAP_CHECK_LAUNCH("quant_permute_fp8_kernel");
     mark(2);
     gemm8::Params g1;
     memset(&g1, 0, sizeof(g1));
@@ -1297,10 +1310,8 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     mark(4);
     return finalize(desc, L, pa, B, R, rows, st, sms, mark);
   }
-  quant_tok_kernel<<<sms * 4, 256, 0, st>>>(qa);
-  ASAP_CHECK_LAUNCH("quant_tok_kernel");
-  permute_copy_kernel<<<sms * 4, 256, 0, st>>>(qa);
-  ASAP_CHECK_LAUNCH("permute_copy_kernel");
+  quant_permute_kernel<<<sms * 4, 256, 0, st>>>(qa);
+  ASAP_CHECK_LAUNCH("quant_permute_kernel");
   mark(2);
 
   gemm::Params g1;

@@ -19,7 +19,9 @@ constexpr int NUM_EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + NUM_EPI_WARPS);
 constexpr uint32_t TMEM_COLS = 512;  // two 256-column partial accumulators
 constexpr int CTRL_BYTES = 4096;     // barriers, TMEM slot, expert starts, row amax exchange
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + CTRL_BYTES;
+constexpr int STAGE_OUT_BYTES = NUM_EPI_WARPS * 2048;  // GEMM2 output staging, 32 rows x 64 B per epilogue warp
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_OUT_BYTES + CTRL_BYTES;
+static_assert(SMEM_BYTES <= 232448, "shared memory over the 227 KB per block");
 static_assert(256 + 4 * (ASAP_MAX_LOCAL_EXPERTS + 1) <= 2048, "expert starts overlap the amax exchange");
 constexpr float kE4M3Max = 448.f;
 
@@ -60,7 +62,8 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* ctrl = sB + STAGES * B_BYTES;
+  uint8_t* sOut = sB + STAGES * B_BYTES;
+  uint8_t* ctrl = sOut + STAGE_OUT_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
@@ -285,20 +288,22 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
           }
           if (half == 0) p.out_sa[(int64_t)n_t * p.m_cap + row] = scale;
         }
-      } else {
-        if (!valid) continue;
-        const float wr = p.row_w[row];
-        uint4* dst = reinterpret_cast<uint4*>(p.out_bf + row * p.N + (int64_t)n_t * BN + half * 128);
+      } else {  // warp-cooperative stores through shared memory; every lane takes part, invalid rows masked
+        const uint32_t valid_rows = __ballot_sync(0xffffffffu, valid);
+        if (!valid_rows) continue;
+        const float wr = valid ? p.row_w[row] : 0.f;
+        uint8_t* wb = sOut + (warp - 2) * 2048;
+        __nv_bfloat16* out0 = p.out_bf + ((int64_t)m_blk * BM + q * 32) * p.N + (int64_t)n_t * BN + half * 128;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float* a = j < 8 ? acc0 + 8 * j : acc1 + 8 * (j - 8);
-          uint32_t o[4];
+        for (int c = 0; c < 4; ++c) {
+          const float* a = c < 2 ? acc0 + 32 * c : acc1 + 32 * (c - 2);
+          uint32_t o[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < 16; ++i) {
             const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[2 * i] * wr, a[2 * i + 1] * wr);
             o[i] = *reinterpret_cast<const uint32_t*>(&b2);
           }
-          dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+          gemm::store_rows_bf16x32(o, wb, out0 + c * 32, p.N, valid_rows, lane);
         }
       }
     }
@@ -313,18 +318,22 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
 }  // namespace gemm8
 
 // ------------------------------------------------------------------ FP8 activation quantisation + copy
-// Every token once: bf16 row -> E4M3 row + one fp32 scale per 128 values (scale = amax / 448, values
-// multiplied by 448 / amax before the round-to-nearest-even, saturating conversion).  One warp per token;
-// each pass covers 256 values, a half-warp per 128-value block.
-__global__ void __launch_bounds__(256) quant_tok_fp8_kernel(const __grid_constant__ QuantArgs p) {
+// Every token once: bf16 row -> E4M3 codes + one fp32 scale per 128 values (scale = amax / 448, values multiplied
+// by 448 / amax before the round-to-nearest-even, saturating conversion), stored straight into each of the token's
+// local pair rows; the scales go to the K-block-major [H/128][m_cap] layout the GEMM epilogue reads.  One warp per
+// token; each pass covers 256 values, a half-warp per 128-value block.
+__global__ void __launch_bounds__(256) quant_permute_fp8_kernel(const __grid_constant__ QuantArgs p) {
   if (!p.desc->valid) return;
   const int n = p.desc->n;
   const int lane = threadIdx.x & 31;
   const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = p.H;
-  float* sf = reinterpret_cast<float*>(p.xtok_sf);
+  float* dsf = reinterpret_cast<float*>(p.xq_sf);
   for (int64_t t = gwarp; t < n; t += nwarps) {
+    const int32_t mine = lane < p.topk ? p.pair_pos[t * p.topk + lane] : -1;
+    const uint32_t vmask = __ballot_sync(0xffffffffu, mine >= 0);
+    if (!vmask) continue;
     int64_t local;
     const int r = row_of_token(p.desc, t, local);
     const __nv_bfloat16* src = p.x[r] + local * H;
@@ -344,31 +353,15 @@ __global__ void __launch_bounds__(256) quant_tok_fp8_kernel(const __grid_constan
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float amax_c = fmaxf(amax, 1e-10f);
-      const float inv = gemm8::kE4M3Max / amax_c;
-      *reinterpret_cast<uint2*>(p.xtok + t * H + base + lane * 8) =
-          make_uint2(gemm8::e4m3x4(v[0], v[1], v[2], v[3], inv), gemm8::e4m3x4(v[4], v[5], v[6], v[7], inv));
-      if ((lane & 15) == 0) sf[t * (H / 128) + base / 128 + (lane >> 4)] = amax_c / gemm8::kE4M3Max;
+      const float inv = gemm8::kE4M3Max / amax_c, scale = amax_c / gemm8::kE4M3Max;
+      const uint2 codes = make_uint2(gemm8::e4m3x4(v[0], v[1], v[2], v[3], inv),
+                                     gemm8::e4m3x4(v[4], v[5], v[6], v[7], inv));
+      const int64_t kb = base / 128 + (lane >> 4);
+      for (uint32_t m = vmask; m; m &= m - 1) {
+        const int32_t row = __shfl_sync(0xffffffffu, mine, __ffs(m) - 1);
+        *reinterpret_cast<uint2*>(p.xq + (int64_t)row * H + base + lane * 8) = codes;
+        if ((lane & 15) == 0) dsf[kb * p.m_cap + row] = scale;
+      }
     }
-  }
-}
-
-// Expert-major copy: permuted row r <- token row_tok[r]; scales to the K-block-major [H/128][m_cap] layout the
-// GEMM epilogue reads (one coalesced 4-byte load per thread and K block).
-__global__ void __launch_bounds__(256) permute_copy_fp8_kernel(const __grid_constant__ QuantArgs p, int64_t m_cap) {
-  if (!p.desc->valid) return;
-  const int64_t rows = (int64_t)p.mstart[p.P] * 128;
-  const int lane = threadIdx.x & 31;
-  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  const int H = p.H, kblocks = H / 128, nvec = H / 16;
-  const float* sf = reinterpret_cast<const float*>(p.xtok_sf);
-  float* dsf = reinterpret_cast<float*>(p.xq_sf);
-  for (int64_t r = gwarp; r < rows; r += nwarps) {
-    const int32_t t = p.row_tok[r];
-    if (t < 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(p.xtok + (int64_t)t * H);
-    uint4* dst = reinterpret_cast<uint4*>(p.xq + r * H);
-    for (int c = lane; c < nvec; c += 32) dst[c] = src[c];
-    for (int kb = lane; kb < kblocks; kb += 32) dsf[(int64_t)kb * m_cap + r] = sf[(int64_t)t * kblocks + kb];
   }
 }
