@@ -803,7 +803,7 @@ def run_multi(args):
 
     from asap_b200.experts import Mxfp4Experts
     from asap_b200.scheduler import FfnScheduler
-    from asap_b200.transport.channel import AttnChannel
+    from asap_b200.transport.channel import AttnChannel, serve_order
     from asap_b200.transport.layout import Geometry
     from asap_b200.transport.server import FfnServer
 
@@ -835,7 +835,8 @@ def run_multi(args):
     dist.all_gather_object(eps, ep)
     endpoints = [e for e in eps if e is not None]
     if is_a:
-        channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s).connect()
+        channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s,
+                              staged=args.staged).connect()
     dist.barrier()
     feeder = None
     if not is_a:
@@ -848,7 +849,8 @@ def run_multi(args):
                 if args.join_replicas:  # one job answers every replica's message of this step
                     sched.run_device_wait_rows([(a, 0, s + 1) for a in range(n_a)], 0, stream.cuda_stream)
                     continue
-                for a in range(n_a):
+                # staged dispatch: answer the A ranks in the order their messages complete here
+                for a in (serve_order(f, n_a, n_f) if args.staged else range(n_a)):
                     sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
 
         feeder = threading.Thread(target=feed, daemon=True)
@@ -964,7 +966,8 @@ def run_multi(args):
             "metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE[KIND], "data": "synthetic",
-            "gpu_launches": args.steps * (4 * n_a + (10 if args.join_replicas else 9 * n_a) * n_f), "roofline": None,
+            "gpu_launches": args.steps * ((3 + (n_f if args.staged else 1)) * n_a +
+                                          (10 if args.join_replicas else 9 * n_a) * n_f), "roofline": None,
             "cpu_baseline": None,
             "clocks": clock_summary,
         }
@@ -981,7 +984,8 @@ def run_multi(args):
                 "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
                 "expert_bounds": bounds, "routing": args.routing,
                 "f_jobs": "one joined job per step (all replicas' messages)" if args.join_replicas else
-                          "one job per message", "l2": "inputs larger than L2, no flush"
+                          "one job per message", "dispatch": "staged (one F rank at a time)" if args.staged else
+                          "all F ranks at once", "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
             line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
@@ -1040,6 +1044,8 @@ def main():
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
+    ap.add_argument("--staged", action="store_true",
+                    help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that order")
     ap.add_argument("--join-replicas", action="store_true",
                     help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
     args = ap.parse_args()

@@ -148,6 +148,18 @@ int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n
 int asap_dispatch_info(uint64_t route_ws, int32_t num_f, int32_t* counts, uint64_t* t_ring_ns,
                        uint64_t* t_replies_ns, void* stream);
 
+/* asap_dispatch with the payload sent one F rank at a time (no counterpart in the reference: its AttnChannel.send
+ * copies to every F rank and rings every doorbell in one pass, channel.py:340-355): F rank f_order[i]'s rows are
+ * packed by the i-th grid, which rings that F rank's doorbell as soon as they are out, so an F rank can start on
+ * the message while the next F rank's rows still cross NVLink.  f_order is a permutation of [0, num_f); NULL
+ * rotates by the A rank (F ranks a*num_f/num_a, +1, ...), so that the A replicas start on different F ranks.
+ * Same checks, routing table, arena bytes and doorbell words as asap_dispatch. */
+int asap_dispatch_staged(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                         const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                         int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                         const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
+                         uint64_t status, uint64_t timeout_ns, void* stream, const int32_t* f_order);
+
 /* Allocation-free asap_dispatch (no counterpart in the reference).  Some callers cannot allocate device memory:
  * an attention rank whose free memory SGLang has already handed to the KV-cache pool, or a host that binds this
  * ABI from another language and only holds the transport's mapped arenas.  This entry point needs no routing

@@ -82,7 +82,7 @@ class AttnChannel:
 
     def __init__(self, a: int, geometry: Geometry, endpoints: Sequence[Tuple[str, int]], *, device: int,
                  seq_base: int = 0, timeout_s: float = 60.0, connect_timeout_s: float = 60.0, memory: str = "auto",
-                 hello: Optional[dict] = None, expert_bounds: Optional[Sequence[int]] = None,
+                 hello: Optional[dict] = None, expert_bounds: Optional[Sequence[int]] = None, staged: bool = False,
                  _backpressure: bool = True, _epoch_override: Optional[int] = None, _connector=None):
         if len(endpoints) != geometry.num_f:
             raise ValueError(f"need one endpoint per F rank ({geometry.num_f}), got {len(endpoints)}")
@@ -107,6 +107,9 @@ class AttnChannel:
         self.replies: List[dict] = []
         self.status = None
         self._route_ws: List[torch.Tensor] = []
+        # staged: the payload goes to one F rank at a time, each doorbell rung as soon as its rows are out
+        # (asap_dispatch_staged), in the order staged_order(a, num_a, num_f)
+        self.staged = bool(staged) and geometry.num_f > 1
 
     # ---------------------------------------------------------------- connect / close
     def connect(self) -> "AttnChannel":
@@ -235,10 +238,14 @@ class AttnChannel:
         epochs = self._c_epochs
         if self._epoch_override is not None:
             epochs = (ctypes.c_int32 * g.num_f)(*([self._epoch_override] * g.num_f))
-        N.call("asap_dispatch", ctypes.byref(self._gs), self.a, slot, seq, layer_id, epochs, x_ptr, ids_ptr,
-               int(ids_is_int64), w_ptr, int(w_is_bf16), n_tokens, self._c_bounds, self._c_recv, self._c_bells,
-               self._result, self._ws_ptr(slot), int(self._backpressure), self.status.ptr,
-               int(self.timeout_s * 1e9), ctypes.c_void_p(stream))
+        args = (ctypes.byref(self._gs), self.a, slot, seq, layer_id, epochs, x_ptr, ids_ptr, int(ids_is_int64), w_ptr,
+                int(w_is_bf16), n_tokens, self._c_bounds, self._c_recv, self._c_bells, self._result,
+                self._ws_ptr(slot), int(self._backpressure), self.status.ptr, int(self.timeout_s * 1e9),
+                ctypes.c_void_p(stream))
+        if self.staged:
+            N.call("asap_dispatch_staged", *args, None)
+        else:
+            N.call("asap_dispatch", *args)
         return Ticket(slot, seq, layer_id, n_tokens)
 
     def wait(self, ticket: Ticket, stream: int) -> List[int]:
@@ -257,3 +264,15 @@ class AttnChannel:
         N.call("asap_combine", ctypes.byref(self._gs), ticket.slot, ticket.seq, ticket.n_tokens, self._result,
                self._ws_ptr(ticket.slot), shared_ptr, out_ptr, self.status.ptr,
                int(self.timeout_s * 1e9), ctypes.c_void_p(stream))
+
+
+def staged_order(a: int, num_a: int, num_f: int) -> List[int]:
+    """The F ranks in the order A rank a's staged dispatch sends to them (asap_dispatch_staged's default):
+    rotated by a * num_f // num_a, so that the A ranks start on different F ranks."""
+    off = a * num_f // max(1, num_a)
+    return [(off + i) % num_f for i in range(num_f)]
+
+
+def serve_order(f: int, num_a: int, num_f: int) -> List[int]:
+    """The A ranks in the order their staged messages complete at F rank f (the order f should answer them)."""
+    return sorted(range(num_a), key=lambda a: (staged_order(a, num_a, num_f).index(f), a))

@@ -56,7 +56,7 @@ static int check_geometry(const asap_geometry_t* g) {
 // ------------------------------------------------------------------ routing workspace layout
 // [0, 256)      int32 count[ASAP_MAX_F]  (rows announced to F rank f, >= 1)
 // [256, 320)    int32 pad[ASAP_MAX_F]    (1 when f received no token and gets one row of ids -1)
-// [320, 384)    uint32 arrive counter of the pack grid
+// [320, 384)    uint32 arrive counters of the pack grids: [0] for a pack to every F rank, [f] for F rank f alone
 // [384, 392)    uint64 globaltimer (ns) when the doorbells were released
 // [392, 400)    uint64 globaltimer (ns) when the combine's wait saw every done flag
 // [400, 512)    reserved
@@ -165,11 +165,13 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
     count[tid] = total > 0 ? total : 1;
     pad[tid] = total > 0 ? 0 : 1;
   }
-  if (tid == 0) *reinterpret_cast<uint32_t*>(ws + kWsSync) = 0;
+  if (tid < ASAP_MAX_F) reinterpret_cast<uint32_t*>(ws + kWsSync)[tid] = 0;
 }
 
 // K2: pack every routed token into every F rank that owns one of its experts, then the last CTA to finish
-// releases the doorbells.  One warp per token; 16-byte vector loads and stores.
+// releases the doorbells.  One warp per token; 16-byte vector loads and stores.  With only_f >= 0 the grid packs
+// F rank only_f's rows alone and rings only its doorbell (staged dispatch: one launch per F rank, in an order
+// that lets each F rank start on its first message early).
 struct PackArgs {
   asap_geometry_t g;
   int32_t a, slot, layer_id, n;
@@ -182,6 +184,8 @@ struct PackArgs {
   uint8_t* recv[ASAP_MAX_F];
   uint64_t* bell[ASAP_MAX_F];
   uint32_t epoch[ASAP_MAX_F];
+  int32_t only_f;  // -1: every F rank
+  int32_t stamp;   // record the doorbell release time (the first launch of a dispatch)
 };
 
 __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constant__ PackArgs p) {
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constan
     uint32_t mask = 0;
     for (int f = 0; f < F; ++f) {
       rows[f] = row_of[(int64_t)f * g.n_max + t];
-      if (rows[f] >= 0) mask |= 1u << f;
+      if (rows[f] >= 0 && (p.only_f < 0 || p.only_f == f)) mask |= 1u << f;
     }
     if (!mask) continue;
     const uint4* src = reinterpret_cast<const uint4*>(p.x + (uint64_t)t * row_bytes);
@@ -239,7 +243,7 @@ __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constan
   // F ranks that got no token: one row whose ids name no expert (F's experts skip it, the reply row is 0).
   if (blockIdx.x == 0 && threadIdx.x < 32) {
     for (int f = 0; f < F; ++f) {
-      if (!pad[f]) continue;
+      if (!pad[f] || (p.only_f >= 0 && p.only_f != f)) continue;
       uint8_t* base = p.recv[f] + roff;
       if (lane < g.topk) {
         reinterpret_cast<int32_t*>(base + o.ids_off)[lane] = -1;
@@ -252,14 +256,14 @@ __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constan
   __shared__ uint32_t last;
   if (threadIdx.x == 0) {
     __threadfence_system();
-    uint32_t* sync = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(p.ws) + kWsSync);
+    uint32_t* sync = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(p.ws) + kWsSync) + (p.only_f < 0 ? 0 : p.only_f);
     last = (atomicAdd(sync, 1u) == gridDim.x - 1);
   }
   __syncthreads();
-  if (last && threadIdx.x < F) {
+  const int f = p.only_f < 0 ? (int)threadIdx.x : p.only_f;
+  if (last && (p.only_f < 0 ? (int)threadIdx.x < F : threadIdx.x == 0)) {
     __threadfence_system();
-    const int f = threadIdx.x;
-    if (f == 0) *reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(p.ws) + kWsRing) = globaltimer_ns();
+    if (p.stamp && threadIdx.x == 0) *reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(p.ws) + kWsRing) = globaltimer_ns();
     st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.bell[f]) + bell_off(g, p.a, p.slot)),
                        pack_doorbell(p.seq, (uint32_t)count[f], (uint32_t)p.layer_id, p.epoch[f]));
   }
@@ -528,11 +532,11 @@ uint64_t asap_route_ws_bytes(const asap_geometry_t* g) {
   return kWsRows + (uint64_t)g->num_f * g->n_max * 4;
 }
 
-int asap_dispatch(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
-                  const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
-                  int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
-                  const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
-                  uint64_t status, uint64_t timeout_ns, void* stream) {
+static int dispatch_impl(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                         const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                         int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                         const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
+                         uint64_t status, uint64_t timeout_ns, void* stream, const int32_t* f_order) {
   int rc = check_geometry(g);
   if (rc) return rc;
   if (g->num_f > ASAP_MAX_F || g->topk > 32) {
@@ -599,9 +603,54 @@ int asap_dispatch(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t se
   const int warps = 8;
   int blocks = (n + warps - 1) / warps;
   blocks = std::min(blocks, sm_count() * 4);
-  dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
-  ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
+  if (!f_order) {
+    p.only_f = -1;
+    p.stamp = 1;
+    dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
+    ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
+    return ASAP_OK;
+  }
+  for (int i = 0; i < g->num_f; ++i) {  // one grid per F rank, each ringing its own doorbell when its rows are out
+    p.only_f = f_order[i];
+    p.stamp = i == 0;
+    dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
+    ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
+  }
   return ASAP_OK;
+}
+
+int asap_dispatch(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                  const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                  int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                  const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
+                  uint64_t status, uint64_t timeout_ns, void* stream) {
+  return dispatch_impl(g, a, slot, seq, layer_id, epochs, x, ids, ids_is_int64, w, w_is_bf16, n, expert_bounds, recv,
+                       bells, result, route_ws, backpressure, status, timeout_ns, stream, nullptr);
+}
+
+int asap_dispatch_staged(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
+                         const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
+                         int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
+                         const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
+                         uint64_t status, uint64_t timeout_ns, void* stream, const int32_t* f_order) {
+  int rc = check_geometry(g);
+  if (rc) return rc;
+  if (g->num_f > ASAP_MAX_F) {
+    set_error("asap_dispatch_staged: num_f=%d (max %d) unsupported", g->num_f, ASAP_MAX_F);
+    return ASAP_EINVAL;
+  }
+  int32_t order[ASAP_MAX_F];
+  uint32_t seen = 0;
+  for (int i = 0; i < g->num_f; ++i) {  // default: rotated by the A rank, so the A ranks start on different F ranks
+    order[i] = f_order ? f_order[i] : (int32_t)(((int64_t)a * g->num_f / std::max(1, g->num_a) + i) % g->num_f);
+    if (order[i] < 0 || order[i] >= g->num_f || (seen >> order[i]) & 1u) {
+      set_error("asap_dispatch_staged: f_order must be a permutation of the F ranks");
+      return ASAP_EINVAL;
+    }
+    seen |= 1u << order[i];
+  }
+  return dispatch_impl(g, a, slot, seq, layer_id, epochs, x, ids, ids_is_int64, w, w_is_bf16, n, expert_bounds, recv,
+                       bells, result, route_ws, backpressure, status, timeout_ns, stream, order);
 }
 
 int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n, uint64_t result,

@@ -33,15 +33,22 @@ class FakeDeployment:
         self.status = torch.zeros(1, dtype=torch.int64, device=dev)
 
     def dispatch(self, seq, layer, x, ids, w, epochs=None, backpressure=True, timeout_s=2.0, ids64=False,
-                 wbf16=False):
+                 wbf16=False, staged=None):
+        """staged: None -> asap_dispatch; "default" -> asap_dispatch_staged with its rotated order; a list -> that
+        F order."""
         g, F = self.g, self.g.num_f
         epochs = epochs or [1] * F
-        N.call("asap_dispatch", ctypes.byref(self.gs), self.a, 0, seq, layer, (ctypes.c_int32 * F)(*epochs),
-               x.data_ptr(), ids.data_ptr(), int(ids64), w.data_ptr(), int(wbf16), x.shape[0],
-               (ctypes.c_int32 * (F + 1))(*self.bounds), (ctypes.c_uint64 * F)(*[r.data_ptr() for r in self.recv]),
-               (ctypes.c_uint64 * F)(*[b.data_ptr() for b in self.bells]), self.result.data_ptr(),
-               self.ws.data_ptr(), int(backpressure), self.status.data_ptr(), int(timeout_s * 1e9),
-               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        args = (ctypes.byref(self.gs), self.a, 0, seq, layer, (ctypes.c_int32 * F)(*epochs),
+                x.data_ptr(), ids.data_ptr(), int(ids64), w.data_ptr(), int(wbf16), x.shape[0],
+                (ctypes.c_int32 * (F + 1))(*self.bounds), (ctypes.c_uint64 * F)(*[r.data_ptr() for r in self.recv]),
+                (ctypes.c_uint64 * F)(*[b.data_ptr() for b in self.bells]), self.result.data_ptr(),
+                self.ws.data_ptr(), int(backpressure), self.status.data_ptr(), int(timeout_s * 1e9),
+                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if staged is None:
+            N.call("asap_dispatch", *args)
+        else:
+            order = None if staged == "default" else (ctypes.c_int32 * F)(*staged)
+            N.call("asap_dispatch_staged", *args, order)
 
     def done_flags(self):
         return self.result[: self.g.flags_bytes].view(torch.int32)
@@ -221,3 +228,26 @@ def test_doorbell_wait_runs_out_and_rejects_stale_epoch(cuda_ok):
     assert int(h.status.item()) == 0 and int(h.done[0].item()) == 2
     h.release()
     e.release()
+
+
+@pytest.mark.parametrize("staged", ["default", [2, 0, 1]])
+def test_staged_dispatch_same_bytes(cuda_ok, staged):
+    """asap_dispatch_staged (one grid per F rank, each ringing its own doorbell) leaves the same routing table,
+    arena bytes and doorbell words as asap_dispatch, including an F rank that gets only the padding row."""
+    rng = np.random.default_rng(21)
+    n, H, k, bounds = 300, 512, 4, [0, 10, 10, 24]
+    g = Geometry(2, 1, 2, n, H, k, 3)
+    x = bf16_tensor_from_np(mx.bf16_round(rng.standard_normal((n, H)).astype(np.float32)))
+    ids = torch.from_numpy(np.stack([rng.permutation(26)[:k] - 1 for _ in range(n)]).astype(np.int32)).cuda()
+    w = torch.from_numpy(rng.random((n, k)).astype(np.float32)).cuda()
+    plain, stg = FakeDeployment(g, bounds, a=1), FakeDeployment(g, bounds, a=1)
+    plain.dispatch(1, 9, x, ids, w, epochs=[2, 2, 2])  # seq 1: backpressure needs done >= 0, already true
+    stg.dispatch(1, 9, x, ids, w, epochs=[2, 2, 2], staged=staged)
+    torch.cuda.synchronize()
+    assert int(plain.status.item()) == 0 and int(stg.status.item()) == 0
+    assert torch.equal(plain.ws[:320], stg.ws[:320]) and torch.equal(plain.ws[512:], stg.ws[512:])
+    for f in range(3):
+        assert torch.equal(plain.region(f), stg.region(f)), f
+        assert torch.equal(plain.bells[f], stg.bells[f]), f
+    with pytest.raises(N.AsapError, match="permutation"):
+        stg.dispatch(2, 9, x, ids, w, epochs=[2, 2, 2], staged=[0, 0, 1])
