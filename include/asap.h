@@ -251,6 +251,23 @@ int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, 
 int asap_ffn_post_rows(uint64_t ws_handle, int32_t rows, const uint32_t* seqs, const int32_t* ns, int32_t layer_id,
                        const int32_t* epochs, void* stream);
 
+/* asap_ffn_wait_rows whose last consumed seq per row lives in device memory (seq_states: device addresses of
+ * uint32 words, one per row): the wait reads it and stores the seq it consumed, so the same launch -- or a CUDA
+ * graph captured around it -- waits for the next message each time it runs. */
+int asap_ffn_wait_state(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,
+                        const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
+                        void* stream);
+
+/* CUDA graphs of F chains (the analogue of the reference's FfnCudaGraphRunner, srt/model_executor/runner/
+ * ffn_cuda_graph_runner.py:75-92, here with no host copy into static buffers: the chain sizes itself on the
+ * device).  asap_graph_begin starts capturing `stream` (thread-local mode): the asap_* launches on it until
+ * asap_graph_end are recorded, not run; asap_graph_end instantiates them (*graph names the executable graph);
+ * asap_graph_launch replays it on a stream; asap_graph_release frees it. */
+int asap_graph_begin(void* stream);
+int asap_graph_end(void* stream, uint64_t* graph);
+int asap_graph_launch(uint64_t graph, void* stream);
+int asap_graph_release(uint64_t graph);
+
 /* One job (replaces scheduler.py:387-436 run_job + FusedMoE + server.py:340-350 reply):
  * x/ids/w are the row's arena views (server.py:309-320 Row pointers); the token count comes from the
  * workspace's job descriptor. Routed experts [expert_base, expert_base+num_local) only, SwiGLU

@@ -97,6 +97,12 @@ _SIGS = {
     "asap_ffn_post": (c_int32, [c_uint64, c_uint32, c_int32, c_int32, c_int32, c_void_p]),
     "asap_ffn_wait_rows": (c_int32, [c_uint64, c_int32, POINTER(c_uint64), POINTER(c_uint32), POINTER(c_int32), c_int32,
                                      c_uint64, c_uint64, c_void_p]),
+    "asap_ffn_wait_state": (c_int32, [c_uint64, c_int32, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_int32), c_int32,
+                                      c_uint64, c_uint64, c_void_p]),
+    "asap_graph_begin": (c_int32, [c_void_p]),
+    "asap_graph_end": (c_int32, [c_void_p, POINTER(c_uint64)]),
+    "asap_graph_launch": (c_int32, [c_uint64, c_void_p]),
+    "asap_graph_release": (c_int32, [c_uint64]),
     "asap_ffn_post_rows": (c_int32, [c_uint64, c_int32, POINTER(c_uint32), POINTER(c_int32), c_int32,
                                      POINTER(c_int32), c_void_p]),
     "asap_ffn_job_rows": (c_int32, [c_uint64, c_uint64, c_int32, POINTER(FfnRow_t), c_float, c_uint64, c_uint64,

@@ -28,8 +28,8 @@ class LocalFfn:
     the other on one stream.  That stream has the highest priority: the F chain is the critical path of the step,
     so its kernels take SMs ahead of A-side work queued beside them (the shared expert)."""
 
-    def __init__(self, schedulers: List[FfnScheduler], a: int, slots: int, device: int):
-        self.scheds, self.a, self.device = schedulers, a, device
+    def __init__(self, schedulers: List[FfnScheduler], a: int, slots: int, device: int, graphs: bool = False):
+        self.scheds, self.a, self.device, self.graphs = schedulers, a, device, graphs
         self.stream = torch.cuda.Stream(device, priority=-1)
         self.sent = [torch.cuda.Event() for _ in range(slots)]
         self.done = [torch.cuda.Event() for _ in range(slots)]
@@ -44,7 +44,10 @@ class LocalFfn:
         self.sent[s].record(send_stream)
         self.stream.wait_event(self.sent[s])
         for sched in self.scheds:
-            sched.run_device_wait(self.a, s, ticket.seq, ticket.layer_id, self.stream.cuda_stream)
+            if self.graphs:  # one CUDA-graph replay per F rank
+                sched.run_graph([(self.a, s, ticket.seq)], ticket.layer_id, self.stream.cuda_stream)
+            else:
+                sched.run_device_wait(self.a, s, ticket.seq, ticket.layer_id, self.stream.cuda_stream)
         self.done[s].record(self.stream)
 
     def before_combine(self, ticket, stream: torch.cuda.Stream) -> None:
@@ -54,11 +57,12 @@ class LocalFfn:
 class Loopback:
     """One A rank and ``num_f`` F ranks on ``device``.  ``experts``: for one F rank, ``{layer_id: Mxfp4Experts}``;
     for several, a list of such dicts, F rank f owning its experts' [expert_base, expert_base + num_local) --
-    contiguous, in F order, possibly uneven (the 2A6F split 43/43/43/43/42/42)."""
+    contiguous, in F order, possibly uneven (the 2A6F split 43/43/43/43/42/42).  ``graphs``: every F job is one
+    replay of a CUDA graph of its chain (FfnScheduler.run_graph)."""
 
     def __init__(self, geometry: Geometry, experts: Union[Dict[int, Mxfp4Experts], List[Dict[int, Mxfp4Experts]]],
                  *, device: int = 0, timeout_s: float = 10.0, swiglu_limit: float = 0.0,
-                 run_dir: Optional[str] = None, timing: bool = False):
+                 run_dir: Optional[str] = None, timing: bool = False, graphs: bool = False):
         per_f = [experts] if isinstance(experts, dict) else list(experts)
         if geometry.num_a != 1 or geometry.group != 1 or geometry.num_f != len(per_f):
             raise ValueError("a loopback deployment is one A rank (num_a = group = 1) and num_f F ranks, one experts "
@@ -81,7 +85,7 @@ class Loopback:
         self.scheds = [FfnScheduler(srv, d, swiglu_limit=swiglu_limit, timeout_s=timeout_s, timing=timing)
                        for srv, d in zip(self.servers, per_f)]
         self.sched = self.scheds[0]
-        self.local = LocalFfn(self.scheds, 0, geometry.slots, device)
+        self.local = LocalFfn(self.scheds, 0, geometry.slots, device, graphs=graphs)
         self.buffer = AsapBuffer(self.channel, device, local_ffn=self.local)
 
     def install(self) -> AsapBuffer:

@@ -112,12 +112,22 @@ class FfnScheduler:
                first.inter, ctypes.byref(h))
         self.ws_handle = h.value
         self.status = HostWords(1)
+        # CUDA-graph mode: per (A rank, slot) the last consumed seq lives on the device (asap_ffn_wait_state), so a
+        # chain captured once replays for every message; _dev_seq mirrors what those words will hold
+        self.seq_state = torch.zeros(g.num_a * g.slots, dtype=torch.int32, device=f"cuda:{self.device}")
+        self._dev_seq: Dict[tuple, Optional[int]] = {}
+        self._graphs: Dict[tuple, int] = {}
+        self._capture = None
+        self.graph_replays = 0
         self.layer_calls = collections.Counter()
         self.job_timer = JobTimer() if timing else None
         arena = _raw_bytes(server.recv_base, g.recv_bytes, self.device)
         self.recv_arena = arena
 
     def close(self) -> None:
+        for h in self._graphs.values():
+            N.call("asap_graph_release", h)
+        self._graphs.clear()
         if self.ws_handle:
             N.call("asap_ffn_ws_release", self.ws_handle)
             self.ws_handle = 0
@@ -185,7 +195,59 @@ class FfnScheduler:
                self.g.n_max, self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
         self._launch(self.experts[layer_id], row, target, stream)
         server.advance(a, slot, seq)
+        self._dev_seq[(a, slot)] = None  # the device word was not used: re-sync before the next graph replay
         self.layer_calls[layer_id] += 1
+
+    def run_graph(self, messages, layer_id: int, stream: int) -> None:
+        """``run_device_wait`` / ``run_device_wait_rows`` for ``messages`` = [(a, slot, seq), ...] as one replay of a
+        CUDA graph captured on first use per (their (a, slot) pairs, layer, epochs) -- the device-side doorbell
+        wait (sequence words on the device) and the whole expert chain in one launch."""
+        server = self.server
+        rows, targets = [], []
+        for a, slot, seq in messages:
+            row = server.row_for(a, slot, seq, self.g.n_max, layer_id)
+            target = server.reply_target(row)
+            if target is not None:
+                rows.append(row)
+                targets.append(target)
+        if not rows:
+            return
+        if len(rows) > self.join:
+            raise ValueError(f"a job of {len(rows)} rows needs join >= {len(rows)} (this scheduler: {self.join})")
+        for r in rows:  # the device words must hold the seq before this message
+            if self._dev_seq.get((r.a, r.slot)) != (r.seq - 1) & SEQ_MASK:
+                N.call("asap_write32", self._state_ptr(r.a, r.slot), (r.seq - 1) & SEQ_MASK, ctypes.c_void_p(stream))
+        key = (tuple((r.a, r.slot) for r in rows), layer_id, tuple(server.peers[r.a].epoch for r in rows))
+        graph = self._graphs.get(key)
+        if graph is None:
+            graph = self._graphs[key] = self._capture_chain(rows, targets, layer_id)
+        N.call("asap_graph_launch", graph, ctypes.c_void_p(stream))
+        self.graph_replays += 1
+        for r in rows:
+            server.advance(r.a, r.slot, r.seq)
+            self._dev_seq[(r.a, r.slot)] = r.seq & SEQ_MASK
+        self.layer_calls[layer_id] += 1
+
+    def _state_ptr(self, a: int, slot: int) -> int:
+        return self.seq_state.data_ptr() + 4 * (a * self.g.slots + slot)
+
+    def _capture_chain(self, rows, targets, layer_id: int) -> int:
+        if self._capture is None:
+            self._capture = torch.cuda.Stream(self.device)
+        cap = ctypes.c_void_p(self._capture.cuda_stream)
+        server, R = self.server, len(rows)
+        N.call("asap_graph_begin", cap)
+        h = ctypes.c_uint64()
+        try:
+            N.call("asap_ffn_wait_state", self.ws_handle, R,
+                   (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
+                   (ctypes.c_uint64 * R)(*[self._state_ptr(r.a, r.slot) for r in rows]),
+                   (ctypes.c_int32 * R)(*[server.peers[r.a].epoch for r in rows]), self.g.n_max, self.status.ptr,
+                   self.timeout_ns, cap)
+            self._launch_rows(self.experts[layer_id], rows, targets, cap.value)
+        finally:
+            N.call("asap_graph_end", cap, ctypes.byref(h))
+        return h.value
 
     def run_device_wait_rows(self, messages, layer_id: int, stream: int) -> None:
         """One joined job over the next messages of several (a, slot) pairs, ``messages`` = [(a, slot, seq), ...]

@@ -113,6 +113,7 @@ struct WaitArgs {
   int32_t rows, n_max, capacity;  // messages to wait for; tokens per message; tokens per job (workspace)
   const uint64_t* bell[kMaxJobRows];
   uint32_t last_seq[kMaxJobRows];
+  uint32_t* seq_state[kMaxJobRows];  // device words holding the last consumed seq (used and advanced when set)
   int32_t epoch[kMaxJobRows];
   uint64_t status, timeout_ns;
 };
@@ -128,12 +129,13 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
   uint32_t seq = 0;
   if (lane < a.rows) {
     const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
+    const uint32_t last = a.seq_state[lane] ? *a.seq_state[lane] : a.last_seq[lane];
     uint64_t word = 0;
     for (;;) {
       word = ld_relaxed_sys_u64(a.bell[lane]);
-      if ((int32_t)((uint32_t)word - a.last_seq[lane]) > 0) break;
+      if ((int32_t)((uint32_t)word - last) > 0) break;
       if (globaltimer_ns() > deadline) {
-        report(a.status, status_word(ASAP_ST_DOORBELL_TIMEOUT, lane, 0, a.last_seq[lane] + 1u));
+        report(a.status, status_word(ASAP_ST_DOORBELL_TIMEOUT, lane, 0, last + 1u));
         ok = 0;
         break;
       }
@@ -144,6 +146,7 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
     n = (int32_t)((word >> 32) & kMaxTokens);
     layer = (int32_t)((word >> 49) & kMaxLayer);
     epoch = (int32_t)(word >> 59);
+    if (ok && a.seq_state[lane]) *a.seq_state[lane] = seq;  // consumed (a replayed graph waits for the next one)
     if (ok && (epoch != a.epoch[lane] || n < 1 || n > a.n_max)) {
       report(a.status, status_word(ASAP_ST_BAD_DOORBELL, lane, 0, seq));
       ok = 0;
@@ -1068,6 +1071,10 @@ int asap_ffn_ws_register(uint64_t ws, int32_t n_max, int32_t topk, int32_t num_l
               ASAP_MAX_LOCAL_EXPERTS);
     return ASAP_EINVAL;
   }
+  // kernel attributes and the SM count are settled here, outside any stream capture of the jobs
+  int arc = ensure_gemm_attrs();
+  if (arc) return arc;
+  (void)sm_count();
   WsHandle* h = new WsHandle;
   h->base = (uint8_t*)ws;
   h->L = ws_layout(n_max, topk, num_local, hidden, inter);
@@ -1101,11 +1108,11 @@ int asap_ffn_ws_release(uint64_t handle) {
   return ASAP_OK;
 }
 
-int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint32_t* last_seqs,
-                       const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
-                       void* stream) {
+static int ffn_wait_impl(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint32_t* last_seqs,
+                         const uint64_t* seq_states, const int32_t* expect_epochs, int32_t n_max, uint64_t status,
+                         uint64_t timeout_ns, void* stream) {
   WsHandle* w = get_ws(ws_handle);
-  if (!w || rows < 1 || rows > kMaxJobRows || !bells || !last_seqs || !expect_epochs) {
+  if (!w || rows < 1 || rows > kMaxJobRows || !bells || !(last_seqs || seq_states) || !expect_epochs) {
     set_error("asap_ffn_wait: unknown workspace handle, NULL arrays or rows %d outside [1, %d]", rows, kMaxJobRows);
     return ASAP_EINVAL;
   }
@@ -1123,8 +1130,13 @@ int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, 
       set_error("asap_ffn_wait: doorbell %d is NULL or misaligned", r);
       return ASAP_EINVAL;
     }
+    if (seq_states && (!seq_states[r] || (seq_states[r] & 3))) {
+      set_error("asap_ffn_wait: sequence state word %d is NULL or misaligned", r);
+      return ASAP_EINVAL;
+    }
     a.bell[r] = (const uint64_t*)bells[r];
-    a.last_seq[r] = last_seqs[r];
+    a.last_seq[r] = last_seqs ? last_seqs[r] : 0u;
+    a.seq_state[r] = seq_states ? (uint32_t*)seq_states[r] : nullptr;
     a.epoch[r] = expect_epochs[r];
   }
   a.status = status;
@@ -1134,9 +1146,67 @@ int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, 
   return ASAP_OK;
 }
 
+int asap_ffn_wait_rows(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint32_t* last_seqs,
+                       const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
+                       void* stream) {
+  if (!last_seqs) {
+    set_error("asap_ffn_wait: NULL last_seqs");
+    return ASAP_EINVAL;
+  }
+  return ffn_wait_impl(ws_handle, rows, bells, last_seqs, nullptr, expect_epochs, n_max, status, timeout_ns, stream);
+}
+
+int asap_ffn_wait_state(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,
+                        const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
+                        void* stream) {
+  if (!seq_states) {
+    set_error("asap_ffn_wait_state: NULL seq_states");
+    return ASAP_EINVAL;
+  }
+  return ffn_wait_impl(ws_handle, rows, bells, nullptr, seq_states, expect_epochs, n_max, status, timeout_ns, stream);
+}
+
 int asap_ffn_wait(uint64_t ws_handle, uint64_t bell, uint32_t last_seq, int32_t expect_epoch, int32_t n_max,
                   uint64_t status, uint64_t timeout_ns, void* stream) {
   return asap_ffn_wait_rows(ws_handle, 1, &bell, &last_seq, &expect_epoch, n_max, status, timeout_ns, stream);
+}
+
+// ---------------------------------------------------------------- CUDA graphs of F chains
+int asap_graph_begin(void* stream) {
+  ASAP_CUDA(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal));
+  return ASAP_OK;
+}
+
+int asap_graph_end(void* stream, uint64_t* graph) {
+  if (!graph) {
+    set_error("asap_graph_end: NULL graph");
+    return ASAP_EINVAL;
+  }
+  cudaGraph_t g = nullptr;
+  ASAP_CUDA(cudaStreamEndCapture((cudaStream_t)stream, &g));
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    set_error("cudaGraphInstantiate failed: %d %s", (int)e, cudaGetErrorString(e));
+    return ASAP_ECUDA;
+  }
+  *graph = (uint64_t)exec;
+  return ASAP_OK;
+}
+
+int asap_graph_launch(uint64_t graph, void* stream) {
+  if (!graph) {
+    set_error("asap_graph_launch: NULL graph");
+    return ASAP_EINVAL;
+  }
+  ASAP_CUDA(cudaGraphLaunch((cudaGraphExec_t)graph, (cudaStream_t)stream));
+  return ASAP_OK;
+}
+
+int asap_graph_release(uint64_t graph) {
+  if (graph) ASAP_CUDA(cudaGraphExecDestroy((cudaGraphExec_t)graph));
+  return ASAP_OK;
 }
 
 int asap_ffn_post_rows(uint64_t ws_handle, int32_t rows, const uint32_t* seqs, const int32_t* ns, int32_t layer_id,
