@@ -550,7 +550,7 @@ def run_sweep(args):
     per_f = [{0: Mxfp4Experts.random(bounds[f + 1] - bounds[f], H, I, expert_base=bounds[f], seed=100 + f,
                                      scale_lo=117, scale_hi=120)} for f in range(n_f)]
     T_max = max(SWEEP_T)
-    lb = Loopback(Geometry(1, 1, 2, T_max, H, K_TOP, n_f), per_f, timeout_s=30.0)
+    lb = Loopback(Geometry(1, 1, 2, T_max, H, K_TOP, n_f), per_f, timeout_s=30.0, graphs=args.graphs)
     lb.install()
     shared = SharedExpert(dev)
     x_all = torch.randn(T_max, H, device=dev, generator=torch.Generator(device=dev).manual_seed(0)).to(torch.bfloat16)
@@ -569,7 +569,8 @@ def run_sweep(args):
             step()
         torch.cuda.synchronize()
         lb.check()
-        N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 1)
+        if not args.graphs:  # per-stage events are host-side marks: not inside captured graphs
+            N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 1)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(0) as clocks:
             torch.cuda.synchronize()
@@ -580,11 +581,13 @@ def run_sweep(args):
             torch.cuda.synchronize()
         lb.check()
         ms = t0.elapsed_time(t1) / args.steps
-        kms = (ctypes.c_float * 5)()
-        N.call("asap_ffn_last_timing", lb.scheds[0].ws_handle, kms, 5)
-        N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 0)
-        f0_ms = dict(zip(("routing", "quantise_permute", "gemm1", "gemm2", "reduce_reply"),
-                         [round(v, 4) for v in kms]))
+        f0_ms = None
+        if not args.graphs:
+            kms = (ctypes.c_float * 5)()
+            N.call("asap_ffn_last_timing", lb.scheds[0].ws_handle, kms, 5)
+            N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 0)
+            f0_ms = dict(zip(("routing", "quantise_permute", "gemm1", "gemm2", "reduce_reply"),
+                             [round(v, 4) for v in kms]))
         lat, busy, rows = [], [], None
         for _ in range(max(args.latency_iters, 1)):
             _, ticket = step()
@@ -604,7 +607,8 @@ def run_sweep(args):
             "config": {"workload": f"1 GPU loopback 1A{n_f}F: config 2 layer, T={T}, top-8 "
                                    f"{'Zipf(s=1.2) popularity over a seeded expert permutation' if args.routing == 'zipf' else 'sigmoid'}",
                        "tokens_per_replica": T, "a_replicas": 1, "f_ranks": n_f, "expert_bounds": bounds,
-                       "parallelism": f"1A{n_f}F loopback", "routing": args.routing},
+                       "parallelism": f"1A{n_f}F loopback", "routing": args.routing,
+                       "f_jobs": "CUDA-graph replays" if args.graphs else "eager launches"},
             "f_rows": rows, "f_imbalance": round(max(rows) / mean_f, 4),
             "doorbell_to_f_start_us_p50": round(statistics.median(lat), 2),
             "f_rows_per_s": round(sum(rows) / statistics.median(busy), 1),
@@ -847,11 +851,18 @@ def run_multi(args):
             torch.cuda.set_device(local)
             for s in range(queued):
                 if args.join_replicas:  # one job answers every replica's message of this step
-                    sched.run_device_wait_rows([(a, 0, s + 1) for a in range(n_a)], 0, stream.cuda_stream)
+                    msgs = [(a, 0, s + 1) for a in range(n_a)]
+                    if args.graphs:
+                        sched.run_graph(msgs, 0, stream.cuda_stream)
+                    else:
+                        sched.run_device_wait_rows(msgs, 0, stream.cuda_stream)
                     continue
                 # staged dispatch: answer the A ranks in the order their messages complete here
                 for a in (serve_order(f, n_a, n_f) if args.staged else range(n_a)):
-                    sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
+                    if args.graphs:
+                        sched.run_graph([(a, 0, s + 1)], 0, stream.cuda_stream)
+                    else:
+                        sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
 
         feeder = threading.Thread(target=feed, daemon=True)
         feeder.start()
@@ -983,8 +994,8 @@ def run_multi(args):
                              f"softmax, I={I}, FP8 E4M3 with fp32 128x128 block scales)"),
                 "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
                 "expert_bounds": bounds, "routing": args.routing,
-                "f_jobs": "one joined job per step (all replicas' messages)" if args.join_replicas else
-                          "one job per message", "dispatch": "staged (one F rank at a time)" if args.staged else
+                "f_jobs": ("one joined job per step (all replicas' messages)" if args.join_replicas else
+                           "one job per message") + (", CUDA-graph replays" if args.graphs else ""), "dispatch": "staged (one F rank at a time)" if args.staged else
                           "all F ranks at once", "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
@@ -1046,6 +1057,8 @@ def main():
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
     ap.add_argument("--staged", action="store_true",
                     help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that order")
+    ap.add_argument("--graphs", action="store_true",
+                    help="F jobs as CUDA-graph replays (FfnScheduler.run_graph; zipf-sweep and N>1)")
     ap.add_argument("--join-replicas", action="store_true",
                     help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
     args = ap.parse_args()
