@@ -179,6 +179,27 @@ def make_experts(P, expert_base, seed, device="cuda"):
                                device=device)
 
 
+def bind_numa(gpu: int) -> dict:
+    """Run this process on the host cores local to its GPU (from the GPU's PCI device in sysfs), so that the pinned
+    host buffers of the e2e leg are allocated on that NUMA node and copied over the GPU's own host link."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(gpu)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as fh:
+            spec = fh.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= set(os.sched_getaffinity(0)) or cpus
+        os.sched_setaffinity(0, cpus)
+        return {"gpu_pci": bus, "cpus": len(cpus)}
+    except (OSError, AttributeError, ValueError) as exc:
+        return {"unbound": f"{type(exc).__name__}: {exc}"}
+
+
 def topology(name, world):
     """(A replicas, F ranks) of a ``world``-GPU run: 'half' = world/2 each (1A1F, 2A2F, 4A4F), '2a6f' on 8 GPUs,
     '2a4f' on 6."""
@@ -816,6 +837,7 @@ def run_multi(args):
     dist.init_process_group("gloo", timeout=timedelta(seconds=90))
     torch.cuda.set_device(local)
     dev = f"cuda:{local}"
+    binding = bind_numa(local) if not args.no_numa_bind else {"unbound": "--no-numa-bind"}
     n_a, n_f = topology(args.topology, world)
     sweep = args.workload == "zipf-sweep"
     t_list = SWEEP_T if sweep else [args.tokens]
@@ -856,6 +878,11 @@ def run_multi(args):
                         sched.run_graph(msgs, 0, stream.cuda_stream)
                     else:
                         sched.run_device_wait_rows(msgs, 0, stream.cuda_stream)
+                    continue
+                if args.any_order:  # each job answers whichever replica's message is ready first (round robin)
+                    for _ in range(n_a):
+                        sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream,
+                                                  graph=args.graphs)
                     continue
                 # staged dispatch: answer the A ranks in the order their messages complete here
                 for a in (serve_order(f, n_a, n_f) if args.staged else range(n_a)):
@@ -995,7 +1022,9 @@ def run_multi(args):
                 "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
                 "expert_bounds": bounds, "routing": args.routing,
                 "f_jobs": ("one joined job per step (all replicas' messages)" if args.join_replicas else
-                           "one job per message") + (", CUDA-graph replays" if args.graphs else ""), "dispatch": "staged (one F rank at a time)" if args.staged else
+                           "one job per message" + (", first ready replica first (round robin on the device)"
+                                                    if args.any_order else ""))
+                          + (", CUDA-graph replays" if args.graphs else ""), "host_binding": binding, "dispatch": "staged (one F rank at a time)" if args.staged else
                           "all F ranks at once", "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
@@ -1059,6 +1088,10 @@ def main():
                     help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that order")
     ap.add_argument("--graphs", action="store_true",
                     help="F jobs as CUDA-graph replays (FfnScheduler.run_graph; zipf-sweep and N>1)")
+    ap.add_argument("--fixed-order", action="store_true",
+                    help="N>1: F ranks answer the replicas in a fixed order (default: each F job answers the first "
+                         "ready replica's message, round robin, asap_ffn_wait_any -- the reference's poll order)")
+    ap.add_argument("--no-numa-bind", action="store_true", help="N>1: do not bind ranks to their GPU's NUMA node")
     ap.add_argument("--join-replicas", action="store_true",
                     help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
     args = ap.parse_args()
@@ -1072,6 +1105,7 @@ def main():
         args.warmup = 3
     if args.routing is None:
         args.routing = "zipf" if args.workload == "zipf-sweep" else ROUTING
+    args.any_order = not args.fixed_order and not args.staged
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "stack":

@@ -258,6 +258,14 @@ int asap_ffn_wait_state(uint64_t ws_handle, int32_t rows, const uint64_t* bells,
                         const int32_t* expect_epochs, int32_t n_max, uint64_t status, uint64_t timeout_ns,
                         void* stream);
 
+/* Answer ONE message: the first ready one among `rows` doorbells, in round-robin order after the row answered last
+ * (int32 device word rr_state) -- the reference's FfnServer.poll order over ready doorbells (server.py:270-275) on
+ * the device.  Sequence words as in asap_ffn_wait_state.  The job descriptor then holds one row whose view is the
+ * picked index: pass asap_ffn_job_rows all `rows` views (same order); it answers the picked message only. */
+int asap_ffn_wait_any(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,
+                      const int32_t* expect_epochs, int32_t n_max, uint64_t rr_state, uint64_t status,
+                      uint64_t timeout_ns, void* stream);
+
 /* CUDA graphs of F chains (the analogue of the reference's FfnCudaGraphRunner, srt/model_executor/runner/
  * ffn_cuda_graph_runner.py:75-92, here with no host copy into static buffers: the chain sizes itself on the
  * device).  asap_graph_begin starts capturing `stream` (thread-local mode): the asap_* launches on it until

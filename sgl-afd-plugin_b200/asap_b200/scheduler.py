@@ -115,7 +115,9 @@ class FfnScheduler:
         # CUDA-graph mode: per (A rank, slot) the last consumed seq lives on the device (asap_ffn_wait_state), so a
         # chain captured once replays for every message; _dev_seq mirrors what those words will hold
         self.seq_state = torch.zeros(g.num_a * g.slots, dtype=torch.int32, device=f"cuda:{self.device}")
+        self.rr_state = torch.full((1,), -1, dtype=torch.int32, device=f"cuda:{self.device}")
         self._dev_seq: Dict[tuple, Optional[int]] = {}
+        self._dev_owned = set()  # (a, slot) whose last seq only the device knows (after round-robin jobs)
         self._graphs: Dict[tuple, int] = {}
         self._capture = None
         self.graph_replays = 0
@@ -196,6 +198,7 @@ class FfnScheduler:
         self._launch(self.experts[layer_id], row, target, stream)
         server.advance(a, slot, seq)
         self._dev_seq[(a, slot)] = None  # the device word was not used: re-sync before the next graph replay
+        self._dev_owned.discard((a, slot))
         self.layer_calls[layer_id] += 1
 
     def run_graph(self, messages, layer_id: int, stream: int) -> None:
@@ -217,6 +220,7 @@ class FfnScheduler:
         for r in rows:  # the device words must hold the seq before this message
             if self._dev_seq.get((r.a, r.slot)) != (r.seq - 1) & SEQ_MASK:
                 N.call("asap_write32", self._state_ptr(r.a, r.slot), (r.seq - 1) & SEQ_MASK, ctypes.c_void_p(stream))
+            self._dev_owned.discard((r.a, r.slot))
         key = (tuple((r.a, r.slot) for r in rows), layer_id, tuple(server.peers[r.a].epoch for r in rows))
         graph = self._graphs.get(key)
         if graph is None:
@@ -226,6 +230,60 @@ class FfnScheduler:
         for r in rows:
             server.advance(r.a, r.slot, r.seq)
             self._dev_seq[(r.a, r.slot)] = r.seq & SEQ_MASK
+        self.layer_calls[layer_id] += 1
+
+    def run_device_wait_any(self, sources, layer_id: int, stream: int, graph: bool = False) -> None:
+        """One job answering ONE message of layer ``layer_id``: the first of ``sources`` = [(a, slot), ...] with a new
+        message, in round-robin order after the source answered last -- the reference's poll order over ready
+        doorbells (server.py:270-275), decided on the device (asap_ffn_wait_any), so one slow replica does not
+        hold up the others' answers.  Enqueue one such job per expected message.  With ``graph`` the wait and the
+        chain are one CUDA-graph replay (captured once per sources, layer and epochs)."""
+        server = self.server
+        rows, targets = [], []
+        for a, slot in sources:
+            row = server.row_for(a, slot, 0, self.g.n_max, layer_id)
+            target = server.reply_target(row)
+            if target is None:
+                raise RuntimeError(f"A rank {a} is not connected to F rank {self.f}")
+            rows.append(row)
+            targets.append(target)
+            if (a, slot) not in self._dev_owned:  # the device word takes over from the host's bookkeeping
+                with server._lock:
+                    last = server._last[a * self.g.slots + slot]
+                N.call("asap_write32", self._state_ptr(a, slot), last & SEQ_MASK, ctypes.c_void_p(stream))
+                self._dev_owned.add((a, slot))
+                self._dev_seq[(a, slot)] = None
+        R = len(rows)
+        if R > N.MAX_JOB_ROWS:
+            raise ValueError(f"at most {N.MAX_JOB_ROWS} sources")
+        epochs = [server.peers[r.a].epoch for r in rows]
+
+        def enqueue(st: int) -> None:
+            N.call("asap_ffn_wait_any", self.ws_handle, R,
+                   (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
+                   (ctypes.c_uint64 * R)(*[self._state_ptr(r.a, r.slot) for r in rows]),
+                   (ctypes.c_int32 * R)(*epochs), self.g.n_max, self.rr_state.data_ptr(), self.status.ptr,
+                   self.timeout_ns, ctypes.c_void_p(st))
+            self._launch_rows(self.experts[layer_id], rows, targets, st)
+
+        if graph:
+            key = ("any", tuple(sources), layer_id, tuple(epochs))
+            h = self._graphs.get(key)
+            if h is None:
+                if self._capture is None:
+                    self._capture = torch.cuda.Stream(self.device)
+                cap = self._capture.cuda_stream
+                N.call("asap_graph_begin", ctypes.c_void_p(cap))
+                out = ctypes.c_uint64()
+                try:
+                    enqueue(cap)
+                finally:
+                    N.call("asap_graph_end", ctypes.c_void_p(cap), ctypes.byref(out))
+                h = self._graphs[key] = out.value
+            N.call("asap_graph_launch", h, ctypes.c_void_p(stream))
+            self.graph_replays += 1
+        else:
+            enqueue(stream)
         self.layer_calls[layer_id] += 1
 
     def _state_ptr(self, a: int, slot: int) -> int:
@@ -274,6 +332,8 @@ class FfnScheduler:
         self._launch_rows(self.experts[layer_id], rows, targets, stream)
         for r in rows:
             server.advance(r.a, r.slot, r.seq)
+            self._dev_seq[(r.a, r.slot)] = None
+            self._dev_owned.discard((r.a, r.slot))
         self.layer_calls[layer_id] += 1
 
     def rows_of(self, row: Row):

@@ -43,12 +43,14 @@ struct RowState {
   int32_t n, off;  // tokens of this message and its first job-wide token index
   uint32_t seq;
   int32_t layer;
+  int32_t view;    // which of the job's row views (x / ids / w / reply target) holds this message
+  int32_t pad[3];
 };
-static_assert(sizeof(RowState) == 16, "RowState is 16 bytes");
+static_assert(sizeof(RowState) == 32, "RowState is 32 bytes");
 __device__ __forceinline__ const RowState* row_states(const JobDesc* d) {
   return reinterpret_cast<const RowState*>(d + 1);
 }
-// The row holding job-wide token t and t's index inside it.
+// The row view holding job-wide token t, and t's index inside that message.
 __device__ __forceinline__ int row_of_token(const JobDesc* d, int64_t t, int64_t& local) {
   const RowState* rs = row_states(d);
   const int rows = d->rows;
@@ -56,7 +58,7 @@ __device__ __forceinline__ int row_of_token(const JobDesc* d, int64_t t, int64_t
   for (int i = 1; i < rows; ++i)
     if (t >= rs[i].off) r = i;
   local = t - rs[r].off;
-  return r;
+  return rs[r].view;
 }
 
 constexpr int kPermChunks = 128;  // chunks of pairs the permutation is split into (upper bound)
@@ -115,6 +117,7 @@ struct WaitArgs {
   uint32_t last_seq[kMaxJobRows];
   uint32_t* seq_state[kMaxJobRows];  // device words holding the last consumed seq (used and advanced when set)
   int32_t epoch[kMaxJobRows];
+  int32_t* any;  // non-NULL: answer ONE message, the first ready in round-robin order after *any (then updated)
   uint64_t status, timeout_ns;
 };
 
@@ -162,7 +165,7 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
     if (lane >= o) incl += u;
   }
   const int total = __shfl_sync(0xffffffffu, incl, 31);
-  if (lane < a.rows) rs[lane] = RowState{ok ? n : 0, incl - (ok ? n : 0), seq, layer};
+  if (lane < a.rows) rs[lane] = RowState{ok ? n : 0, incl - (ok ? n : 0), seq, layer, lane, {0, 0, 0}};
   const uint32_t seq0 = __shfl_sync(0xffffffffu, seq, 0);
   const int epoch0 = __shfl_sync(0xffffffffu, epoch, 0);
   if (lane == 0) {
@@ -183,6 +186,70 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
   }
 }
 
+// Round-robin form (the reference's FfnServer.poll order over ready doorbells, transport/server.py:270-275): lane
+// r polls row r's doorbell; the first ready row after the last answered one (*a.any) is taken, consumed through
+// its sequence word and described as the job's only row.  Bounded like the all-rows wait.
+__global__ void ffn_wait_any_kernel(const __grid_constant__ WaitArgs a) {
+  JobDesc* d = a.d;
+  RowState* rs = reinterpret_cast<RowState*>(d + 1);
+  const int lane = threadIdx.x;
+  const int rows = a.rows;
+  const uint32_t last = lane < rows ? *a.seq_state[lane] : 0u;
+  const int start = (*a.any + 1) % rows;
+  const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
+  uint64_t word = 0;
+  int pick = -1;
+  for (;;) {
+    bool ready = false;
+    if (lane < rows) {
+      word = ld_relaxed_sys_u64(a.bell[lane]);
+      ready = (int32_t)((uint32_t)word - last) > 0;
+    }
+    const uint32_t mask = __ballot_sync(0xffffffffu, ready);
+    if (mask) {  // rotate so that bit 0 is row `start`, take the lowest set bit
+      const uint32_t full = rows >= 32 ? 0xffffffffu : ((1u << rows) - 1u);
+      const uint32_t rot = ((mask >> start) | (mask << ((rows - start) & 31))) & full;
+      pick = (start + __ffs(rot) - 1) % rows;
+      break;
+    }
+    // lane 0's clock decides, so that the whole warp leaves the loop together (the ballot above needs all lanes)
+    if (__shfl_sync(0xffffffffu, (int)(globaltimer_ns() > deadline), 0)) break;
+    __nanosleep(64);
+  }
+  if (lane == 0) {
+    d->t_seen = globaltimer_ns();
+    d->t_reply = 0;
+    d->sync = 0;
+    d->rows = 1;
+  }
+  if (pick < 0) {
+    if (lane == 0) {
+      report(a.status, status_word(ASAP_ST_DOORBELL_TIMEOUT, 0, 0, 0));
+      d->valid = 0;
+      d->n = 0;
+    }
+    return;
+  }
+  if (lane == pick) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    const uint32_t seq = (uint32_t)word;
+    const int32_t n = (int32_t)((word >> 32) & kMaxTokens);
+    const int32_t layer = (int32_t)((word >> 49) & kMaxLayer);
+    const int32_t epoch = (int32_t)(word >> 59);
+    *a.seq_state[lane] = seq;
+    *a.any = lane;
+    const bool valid = epoch == a.epoch[lane] && n >= 1 && n <= a.n_max && n <= a.capacity;
+    if (!valid) report(a.status, status_word(ASAP_ST_BAD_DOORBELL, lane, 0, seq));
+    rs[0] = RowState{valid ? n : 0, 0, seq, layer, lane, {0, 0, 0}};
+    d->seq = seq;
+    d->layer = layer;
+    d->epoch = epoch;
+    d->n = valid ? n : 0;
+    __threadfence_block();
+    d->valid = valid ? 1 : 0;
+  }
+}
+
 struct PostArgs {
   JobDesc* d;
   int32_t rows, layer;
@@ -196,7 +263,7 @@ __global__ void ffn_post_kernel(const __grid_constant__ PostArgs a) {
   RowState* rs = reinterpret_cast<RowState*>(d + 1);
   int off = 0;
   for (int r = 0; r < a.rows; ++r) {
-    rs[r] = RowState{a.n[r], off, a.seq[r], a.layer};
+    rs[r] = RowState{a.n[r], off, a.seq[r], a.layer, r, {0, 0, 0}};
     off += a.n[r];
   }
   d->seq = a.seq[0];
@@ -848,8 +915,10 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
     p.desc_rw->t_reply = globaltimer_ns();
     __threadfence_system();
     const RowState* rs = row_states(p.desc);
-    for (int r = 0; r < p.desc->rows; ++r)
-      if (p.reply_done[r]) st_release_sys_u32(p.reply_done[r], rs[r].seq);
+    for (int r = 0; r < p.desc->rows; ++r) {
+      const int v = rs[r].view;
+      if (p.reply_done[v]) st_release_sys_u32(p.reply_done[v], rs[r].seq);
+    }
   }
 }
 
@@ -1164,6 +1233,42 @@ int asap_ffn_wait_state(uint64_t ws_handle, int32_t rows, const uint64_t* bells,
     return ASAP_EINVAL;
   }
   return ffn_wait_impl(ws_handle, rows, bells, nullptr, seq_states, expect_epochs, n_max, status, timeout_ns, stream);
+}
+
+int asap_ffn_wait_any(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,
+                      const int32_t* expect_epochs, int32_t n_max, uint64_t rr_state, uint64_t status,
+                      uint64_t timeout_ns, void* stream) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w || rows < 1 || rows > kMaxJobRows || !bells || !seq_states || !expect_epochs || !rr_state ||
+      (rr_state & 3)) {
+    set_error("asap_ffn_wait_any: unknown workspace handle, NULL arrays / round-robin word or rows %d outside "
+              "[1, %d]", rows, kMaxJobRows);
+    return ASAP_EINVAL;
+  }
+  if (n_max < 1 || n_max > w->L.n_max) {
+    set_error("asap_ffn_wait_any: n_max %d outside the workspace's %d", n_max, w->L.n_max);
+    return ASAP_EINVAL;
+  }
+  WaitArgs a{};
+  a.d = (JobDesc*)(w->base + w->L.desc);
+  a.rows = rows;
+  a.n_max = n_max;
+  a.capacity = w->L.n_max;
+  for (int r = 0; r < rows; ++r) {
+    if (!bells[r] || (bells[r] & 7) || !seq_states[r] || (seq_states[r] & 3)) {
+      set_error("asap_ffn_wait_any: doorbell or sequence word %d is NULL or misaligned", r);
+      return ASAP_EINVAL;
+    }
+    a.bell[r] = (const uint64_t*)bells[r];
+    a.seq_state[r] = (uint32_t*)seq_states[r];
+    a.epoch[r] = expect_epochs[r];
+  }
+  a.any = (int32_t*)rr_state;
+  a.status = status;
+  a.timeout_ns = timeout_ns;
+  ffn_wait_any_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(a);
+  ASAP_CHECK_LAUNCH("ffn_wait_any_kernel");
+  return ASAP_OK;
 }
 
 int asap_ffn_wait(uint64_t ws_handle, uint64_t bell, uint32_t last_seq, int32_t expect_epoch, int32_t n_max,

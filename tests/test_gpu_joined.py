@@ -181,3 +181,77 @@ def test_two_replicas_one_joined_job(cuda_ok):
             ch.close()
         srv.close()
         experts.release()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_round_robin_any_ready_message(cuda_ok, graph):
+    """asap_ffn_wait_any: each job answers the first ready message among the sources, in round-robin order after
+    the source answered last.  Only A rank 1 has sent -> the job answers A1 (A0's flag untouched); then A0 sends ->
+    the next job answers A0; then both send -> A1 first (round robin after A0), then A0."""
+    import os
+    import tempfile
+
+    run_dir = tempfile.mkdtemp(dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else None)
+    rng = np.random.default_rng(12)
+    T, H, I, k, E = 64, 256, 128, 2, 8
+    g = Geometry(2, 1, 2, T, H, k, 1)
+    experts = Mxfp4Experts.random(E, H, I, seed=7)
+    srv = FfnServer(0, g, device=0, run_dir=run_dir, listen=False).start()
+    chans = [AttnChannel(a, g, [("in-process", 0)], device=0, timeout_s=5.0, expert_bounds=[0, E],
+                         _connector=lambda f, hello: srv.handshake(hello)).connect() for a in range(2)]
+    sched = FfnScheduler(srv, {0: experts}, timeout_s=5.0)
+    gate, up, w2 = experts_to_oracle(experts)
+    f_stream = torch.cuda.Stream()
+    stream = torch.cuda.current_stream()
+    sources = [(0, 0), (1, 0)]
+    keep = []
+
+    def send(a):
+        x, ids, w = random_inputs(rng, T - 3 * a, H, k, 0, E)
+        dev = (bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+        keep.append(dev)
+        t = chans[a].send(0, 0, dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), dev[0].shape[0],
+                          stream.cuda_stream)
+        return t, (x, ids, w)
+
+    def answer():  # one round-robin job, ordered after everything sent so far (no cross-kernel spin)
+        f_stream.wait_stream(stream)
+        sched.run_device_wait_any(sources, 0, f_stream.cuda_stream, graph=graph)
+        torch.cuda.synchronize()
+        sched.check()
+
+    def check(a, t, msg):
+        out = torch.empty(msg[0].shape, dtype=torch.bfloat16, device="cuda")
+        chans[a].combine(t, out.data_ptr(), stream.cuda_stream)
+        torch.cuda.synchronize()
+        chans[a].check()
+        ref = moe.round_trip(*msg, [0, E], [(gate, up, w2)])
+        assert moe.rel_l2(np_from_bf16(out), ref) < TOL
+
+    try:
+        t1, m1 = send(1)
+        answer()
+        info = sched.job_info()
+        assert info["n"] == T - 3 and info["seq"] == 1  # A rank 1's message
+        check(1, t1, m1)
+        t0, m0 = send(0)
+        answer()
+        assert sched.job_info()["n"] == T
+        check(0, t0, m0)
+        t0, m0 = send(0)
+        t1, m1 = send(1)
+        answer()
+        assert sched.job_info()["n"] == T - 3  # round robin: A1 after A0
+        answer()
+        assert sched.job_info()["n"] == T
+        check(0, t0, m0)
+        check(1, t1, m1)
+        if graph:
+            assert sched.graph_replays == 4 and len(sched._graphs) == 1
+    finally:
+        torch.cuda.synchronize()
+        sched.close()
+        for ch in chans:
+            ch.close()
+        srv.close()
+        experts.release()
