@@ -31,7 +31,8 @@ struct JobDesc {
   uint64_t t_seen;   // globaltimer (ns) when the doorbell wait saw the message (0: posted by the host)
   uint64_t t_reply;  // globaltimer (ns) when the reply's done flag was released
   int32_t rows;      // messages joined in this job (RowState entries after the descriptor)
-  uint32_t pad[5];
+  int32_t small;     // 1: the GEMMs run weights-as-M (gemmT), for jobs whose 128-row blocks are mostly padding
+  uint32_t pad[4];
 };
 static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
 
@@ -315,6 +316,7 @@ struct PermArgs {
   int32_t* row_tok;   // [m_cap]
   float* row_w;       // [m_cap]
   int32_t* hist;      // [kPermChunks][ASAP_MAX_LOCAL_EXPERTS] chunk histograms, then chunk bases
+  int32_t small_mode;  // -1: choose per job (blocks under half full on average); 0 / 1: never / always
 };
 
 __device__ __forceinline__ void perm_chunking(const PermArgs& p, int64_t& total, int64_t& chunk, int& chunks) {
@@ -344,6 +346,8 @@ __global__ void __launch_bounds__(256) route_count_kernel(const __grid_constant_
 
 __global__ void __launch_bounds__(ASAP_MAX_LOCAL_EXPERTS) route_scan_kernel(const __grid_constant__ PermArgs p) {
   __shared__ int32_t wsum[ASAP_MAX_LOCAL_EXPERTS / 32];
+  __shared__ int32_t pairs_total;
+  if (threadIdx.x == 0) pairs_total = 0;
   int64_t total, chunk;
   int chunks;
   perm_chunking(p, total, chunk, chunks);
@@ -385,6 +389,13 @@ __global__ void __launch_bounds__(ASAP_MAX_LOCAL_EXPERTS) route_scan_kernel(cons
     }
   }
   if (e == p.P - 1) p.mstart[p.P] = mst + tiles;
+  if (e < p.P && c) atomicAdd(&pairs_total, c);
+  __syncthreads();
+  if (e == p.P - 1) {  // GEMM variant of this job (both are launched; the other exits at once)
+    const int64_t blocks = mst + tiles;
+    JobDesc* d = const_cast<JobDesc*>(p.desc);
+    d->small = p.small_mode >= 0 ? p.small_mode : (2ll * pairs_total < blocks * 128 ? 1 : 0);
+  }
 }
 
 __global__ void __launch_bounds__(32) route_place_kernel(const __grid_constant__ PermArgs p) {
@@ -602,6 +613,7 @@ __device__ __forceinline__ void store_rows_bf16x32(const uint32_t (&o)[16], uint
 // EPI 0: h = silu(gate) * up, quantised to MXFP8 (GEMM1).  EPI 1: bf16(acc * w[row]) (GEMM2).
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_constant__ Params p) {
+  if (p.desc->valid && p.desc->small) return;  // the weights-as-M kernel (gemmT) runs this job
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -831,6 +843,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
 }  // namespace gemm
 
 #include "gemm_fp8.cuh"
+#include "gemm_small.cuh"
 
 // ------------------------------------------------------------------ K5b: weighted reduce + reply
 struct FinalArgs {
@@ -967,6 +980,7 @@ struct ExpertsHandle {
   asap_mxfp4_experts_t e;   // kMxfp4 (num_local/expert_base/hidden/inter filled for both kinds)
   asap_fp8_experts_t f8;    // kFp8Block
   CUtensorMap w13_map, w2_map;
+  CUtensorMap w13_map_t, w2_map_t;  // kMxfp4: 128-row boxes for the weights-as-M kernels
 };
 constexpr int kTimedKernels = 5;  // routing (count+scan+place), quantise+permute, gemm1, gemm2, finalize_reply
 constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
@@ -975,6 +989,7 @@ struct WsHandle {
   WsLayout L;
   CUtensorMap xq_map, hq_map;
   bool timing = false;
+  int small_mode = 0;  // PermArgs::small_mode (the weights-as-M kernels measured slower: opt-in)
   int jobs = 0;  // jobs recorded since enable
   cudaEvent_t ev[kTimedJobs][kTimedKernels + 1] = {};
 };
@@ -1007,6 +1022,10 @@ static int ensure_gemm_attrs() {
                                  gemm8::SMEM_BYTES));
   ASAP_CUDA(cudaFuncSetAttribute(gemm8::moe_gemm_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  gemm8::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemmT::moe_gemm_t_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemmT::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemmT::moe_gemm_t_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemmT::SMEM_BYTES));
   gemm_attr_set = true;
   return ASAP_OK;
 }
@@ -1063,6 +1082,12 @@ int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
   if (!rc)
     rc = make_tmap_2d(&h->w2_map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2, gemm::BK,
                       gemm::BN, "w2");
+  if (!rc)
+    rc = make_tmap_2d(&h->w13_map_t, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w13, H, P * 2 * I, H / 2,
+                      gemmT::BK, gemmT::BW, "w13 (128-row boxes)");
+  if (!rc)
+    rc = make_tmap_2d(&h->w2_map_t, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2,
+                      gemmT::BK, gemmT::BW, "w2 (128-row boxes)");
   if (rc) {
     delete h;
     return rc;
@@ -1403,6 +1428,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   pa.row_tok = (int32_t*)(B + L.row_tok);
   pa.row_w = (float*)(B + L.row_w);
   pa.hist = (int32_t*)(B + L.hist);
+  pa.small_mode = eh->kind == kMxfp4 ? wh->small_mode : 0;
   const int slot_ev = wh->jobs % kTimedJobs;
   if (wh->timing) ++wh->jobs;
   auto mark = [&](int i) {
@@ -1510,6 +1536,28 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g1.timeout_ns = timeout_ns;
   gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
+  gemmT::Params t1;
+  memset(&t1, 0, sizeof(t1));
+  t1.tmap_w = eh->w13_map_t;
+  t1.tmap_x = wh->xq_map;
+  t1.sfw = g1.sfb;
+  t1.sfw_expert_stride = g1.sfb_expert_stride;
+  t1.sfx = g1.sfa;
+  t1.desc = desc;
+  t1.mstart = pa.mstart;
+  t1.ecnt = pa.ecnt;
+  t1.row_tok = pa.row_tok;
+  t1.row_w = pa.row_w;
+  t1.out_q = g1.out_q;
+  t1.out_sf = g1.out_sf;
+  t1.P = L.P;
+  t1.N = 2 * L.I;
+  t1.K = L.H;
+  t1.swiglu_limit = swiglu_limit;
+  t1.status = status;
+  t1.timeout_ns = timeout_ns;
+  gemmT::moe_gemm_t_kernel<0><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t1);
+  ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<0>");
   mark(3);
 
   gemm::Params g2 = g1;
@@ -1525,9 +1573,32 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.K = L.I;
   gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
+  gemmT::Params t2 = t1;
+  t2.tmap_w = eh->w2_map_t;
+  t2.tmap_x = wh->hq_map;
+  t2.sfw = g2.sfb;
+  t2.sfw_expert_stride = g2.sfb_expert_stride;
+  t2.sfx = g2.sfa;
+  t2.out_q = nullptr;
+  t2.out_sf = nullptr;
+  t2.out_bf = g2.out_bf;
+  t2.N = L.H;
+  t2.K = L.I;
+  gemmT::moe_gemm_t_kernel<1><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t2);
+  ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<1>");
   mark(4);
 
   return finalize(desc, L, pa, B, R, rows, st, sms, mark);
+}
+
+int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w || mode < -1 || mode > 1) {
+    set_error("asap_ffn_set_small_mode: unknown workspace handle or mode %d outside {-1, 0, 1}", mode);
+    return ASAP_EINVAL;
+  }
+  w->small_mode = mode;
+  return ASAP_OK;
 }
 
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable) {
