@@ -279,7 +279,8 @@ int asap_graph_release(uint64_t graph);
 /* One job (replaces scheduler.py:387-436 run_job + FusedMoE + server.py:340-350 reply):
  * x/ids/w are the row's arena views (server.py:309-320 Row pointers); the token count comes from the
  * workspace's job descriptor. Routed experts [expert_base, expert_base+num_local) only, SwiGLU
- * h = silu(x W1^T) * (x W3^T) (clamped to +-swiglu_limit when swiglu_limit > 0), MXFP8 activations,
+ * h = silu(x W1^T) * (x W3^T) (clamped to +-swiglu_limit when swiglu_limit > 0), MXFP8 activations for MXFP4
+ * experts and E4M3 activations with fp32 scales per 1 x 128 for FP8 experts (asap_experts_register_fp8),
  * out[t] = sum_j w[t,j] * (h W2^T), bf16, written to reply_seg row t; then done flag = seq (release, system
  * scope) at reply_done. reply_done == 0 skips the flag. */
 int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64_t ids, uint64_t w,

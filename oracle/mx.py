@@ -169,7 +169,7 @@ FP8_MAX = np.float32(448.0)
 def fp8_act_quantize(v: np.ndarray):
     """[..., K] fp32 (K % 128 == 0) -> (E4M3 codes [..., K], fp32 scales [..., K/128]).  SGLang's per-token-group
     FP8 quantisation (group 128): amax clamped to 1e-10, scale = amax / 448, codes = e4m3(v * (448 / amax)),
-    every operation one fp32 rounding (as libasap's quant_tok_fp8 and FP8 GEMM1 epilogue compute it)."""
+    every operation one fp32 rounding (as libasap's quant_permute_fp8 kernel and FP8 GEMM1 epilogue compute it)."""
     v = np.asarray(v, dtype=np.float32)
     blocks = v.reshape(*v.shape[:-1], v.shape[-1] // 128, 128)
     amax = np.maximum(np.max(np.abs(blocks), axis=-1), np.float32(1e-10)).astype(np.float32)

@@ -1,14 +1,16 @@
-// libasap F side: doorbell wait, expert-major permutation, MXFP8 activation quantisation, the two tcgen05
-// block-scaled grouped GEMMs (MXFP8 activations x MXFP4 weights) with fused epilogues, and the weighted
-// reduce that writes the reply straight into the A rank's ResultArena.
+// libasap F side: doorbell waits (one message, several joined messages, or the first ready one), the expert-major
+// permutation, activation quantisation (MXFP8, or FP8 per 1x128 for block-FP8 experts), the tcgen05 grouped GEMMs
+// with fused epilogues (MXFP8 x MXFP4 block-scaled here; FP8 x FP8 with block-scale promotion in gemm_fp8.cuh;
+// the weights-as-M variant in gemm_small.cuh), the weighted reduce that writes the replies straight into the A
+// ranks' ResultArenas, and the CUDA-graph capture of whole jobs.
 //
 // Reference behaviour replaced here (python/sgl_asap_plugin/):
 //   transport/server.py:262-320     FfnServer.poll/_row        -> ffn_wait_kernel (device-side doorbell spin)
 //   srt/managers/scheduler.py:387-450 run_job / rows_of        -> asap_ffn_job (launch chain, arena views)
 //   SGLang FusedMoE -> FlashInfer trtllm_fp4_block_scale_routed_moe (scheduler.py:410-412;
 //   srt/layers/quantization/mxfp4_flashinfer_trtllm_moe.py:68-99)
-//                                                              -> route_count/scan/place, quant_tok, permute_copy, moe_gemm<0,1>,
-//                                                                 finalize_reply kernels
+//                                                              -> route_count/scan/place, quant_permute, moe_gemm<0,1>
+//                                                                 (FP8: moe_gemm_fp8<0,1>), finalize_reply kernels
 //   transport/server.py:340-350     FfnServer.reply            -> finalize_reply epilogue (P2P rows + done flag)
 #include <cuda.h>
 #include <string.h>

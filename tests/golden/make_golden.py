@@ -62,7 +62,8 @@ def load_layout(ref_root: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ASAP_REFERENCE_DIR"), required="ASAP_REFERENCE_DIR" not in os.environ,
+                    help="the reference checkout (or set ASAP_REFERENCE_DIR)")
     ap.add_argument("--out", default=os.path.join(os.path.dirname(os.path.abspath(__file__)), "layout_golden.json"))
     args = ap.parse_args()
     L = load_layout(args.reference)
