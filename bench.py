@@ -200,6 +200,17 @@ def bind_numa(gpu: int) -> dict:
         return {"unbound": f"{type(exc).__name__}: {exc}"}
 
 
+def placement(world, n_a, how):
+    """(A ranks, F ranks) of a run: 'block' puts the A replicas on ranks [0, n_a); 'interleave' spreads them evenly
+    over the box (ranks round(i * world / n_a)), so that their host copies (the e2e leg) use different host links
+    and NUMA nodes.  NVLink through NVSwitch is the same between any two GPUs, so the data path does not care.
+    Rank 0 is always an A replica (it prints the result line)."""
+    a_ranks = list(range(n_a)) if how == "block" else sorted({round(i * world / n_a) for i in range(n_a)})
+    if len(a_ranks) != n_a:
+        raise SystemExit(f"placement {how} cannot place {n_a} A replicas on {world} GPUs")
+    return a_ranks, [r for r in range(world) if r not in a_ranks]
+
+
 def topology(name, world):
     """(A replicas, F ranks) of a ``world``-GPU run: 'half' = world/2 each (1A1F, 2A2F, 4A4F), '2a6f' on 8 GPUs,
     '2a4f' on 6."""
@@ -690,12 +701,13 @@ def run_stack(args):
 
         dist.init_process_group("gloo", timeout=timedelta(seconds=120))
         n_a, n_f = topology(args.topology, world)
+        a_ranks, f_ranks = placement(world, n_a, args.placement)
         g = Geometry(n_a, 1, 2, Tmb, H, K_TOP, n_f)
         bounds = expert_bounds(n_f)
-        is_a = rank < n_a
+        is_a = rank in a_ranks
         ep = None
         if not is_a:
-            f = rank - n_a
+            f = f_ranks.index(rank)
             layers = {l: make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + 10 * l + f, dev) for l in range(L)}
             server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                                host="127.0.0.1", port=0).start()
@@ -705,7 +717,8 @@ def run_stack(args):
         dist.all_gather_object(eps, ep)
         endpoints = [e for e in eps if e is not None]
         if is_a:
-            channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=120.0).connect()
+            channel = AttnChannel(a_ranks.index(rank), g, endpoints, device=local, expert_bounds=bounds,
+                                  timeout_s=120.0).connect()
             AsapBuffer.connect(channel, local)
         dist.barrier()
         feeder = None
@@ -725,10 +738,11 @@ def run_stack(args):
     ms = 0.0
     clocks_summary = None
     if is_a:
+        a_index = 0 if world == 1 else a_ranks.index(rank)
         shared = SharedExpert(dev)
-        gen = torch.Generator(device=dev).manual_seed(rank)
+        gen = torch.Generator(device=dev).manual_seed(a_index)
         x_in = [torch.randn(Tmb, H, device=dev, generator=gen).to(torch.bfloat16) for _ in range(2)]
-        topk = [[StandardTopKOutput(*reversed(make_routing(Tmb, 1000 * rank + 10 * l + mb, dev))) for mb in range(2)]
+        topk = [[StandardTopKOutput(*reversed(make_routing(Tmb, 1000 * a_index + 10 * l + mb, dev))) for mb in range(2)]
                 for l in range(L)]
         disps = [AsapDispatcher(l) for l in range(L)]
 
@@ -844,14 +858,16 @@ def run_multi(args):
     T_max = max(t_list)
     g = Geometry(n_a, 1, 2, T_max, H, K_TOP, n_f)
     bounds = expert_bounds(n_f)
-    is_a = rank < n_a
+    a_ranks, f_ranks = placement(world, n_a, args.placement)
+    is_a = rank in a_ranks
+    a_idx = a_ranks.index(rank) if is_a else -1
     lat_iters = args.latency_iters if sweep else 0
     phases = len(t_list) * (1 if sweep else 2)  # timed (+ e2e) per token count
     steps_per_phase = args.warmup + args.steps
     timeout_s = 120.0
     ep = None
     if not is_a:
-        f = rank - n_a
+        f = f_ranks.index(rank)
         experts = make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + f, dev)
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
@@ -861,7 +877,7 @@ def run_multi(args):
     dist.all_gather_object(eps, ep)
     endpoints = [e for e in eps if e is not None]
     if is_a:
-        channel = AttnChannel(rank, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s,
+        channel = AttnChannel(a_idx, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s,
                               staged=args.staged).connect()
     dist.barrier()
     feeder = None
@@ -895,7 +911,7 @@ def run_multi(args):
         feeder.start()
     else:
         shared = SharedExpert(dev) if SHARED else None
-        gen = torch.Generator(device=dev).manual_seed(rank)
+        gen = torch.Generator(device=dev).manual_seed(a_idx)
         x_all = torch.randn(T_max, H, device=dev, generator=gen).to(torch.bfloat16)
         send_stream = torch.cuda.Stream(dev)
         stream = torch.cuda.current_stream()
@@ -931,7 +947,8 @@ def run_multi(args):
     for T in t_list:
         if is_a:
             x = x_all[:T]
-            ids, w = (zipf_routing(T, 10 + rank, dev) if args.routing == "zipf" else make_routing(T, 10 + rank, dev))
+            ids, w = (zipf_routing(T, 10 + a_idx, dev) if args.routing == "zipf" else
+                      make_routing(T, 10 + a_idx, dev))
 
             def step(xx=x, ii=ids, ww=w, TT=T):
                 send_stream.wait_stream(stream)
@@ -951,7 +968,7 @@ def run_multi(args):
             counts = None
         allc = [None] * world
         dist.all_gather_object(allc, counts)
-        per_f = [sum(c[f] for c in allc[:n_a]) for f in range(n_f)]
+        per_f = [sum(allc[r][f] for r in a_ranks) for f in range(n_f)]
         res["f_rows"] = per_f
         if not sweep:
             if is_a:
@@ -989,7 +1006,7 @@ def run_multi(args):
         dist.all_gather_object(infos, info)
         if rank == 0:
             a0 = infos[0]
-            fi = [i for i in infos[n_a:]]
+            fi = [infos[r] for r in f_ranks]
             busy = [(i["t_reply_ns"] - i["t_seen_ns"]) * 1e-3 for i in fi]
             rt = (a0["t_replies_ns"] - a0["t_ring_ns"]) * 1e-3
             lat.append({"round_trip_us": rt, "f_busy_us": busy, "signal_us": rt - max(busy)})
@@ -1021,6 +1038,7 @@ def run_multi(args):
                              f"softmax, I={I}, FP8 E4M3 with fp32 128x128 block scales)"),
                 "tokens_per_replica": T, "a_replicas": n_a, "f_ranks": n_f, "parallelism": f"{n_a}A{n_f}F",
                 "expert_bounds": bounds, "routing": args.routing,
+                "placement": args.placement, "a_ranks": a_ranks,
                 "f_jobs": ("one joined job per step (all replicas' messages)" if args.join_replicas else
                            "one job per message" + (", first ready replica first (round robin on the device)"
                                                     if args.any_order else ""))
@@ -1088,6 +1106,9 @@ def main():
                     help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that order")
     ap.add_argument("--graphs", action="store_true",
                     help="F jobs as CUDA-graph replays (FfnScheduler.run_graph; zipf-sweep and N>1)")
+    ap.add_argument("--placement", choices=("block", "interleave"), default="interleave",
+                    help="N>1: which ranks are A replicas: interleave (default) = spread over the box, so that their "
+                         "host copies use different host links; block = the first N_A")
     ap.add_argument("--fixed-order", action="store_true",
                     help="N>1: F ranks answer the replicas in a fixed order (default: each F job answers the first "
                          "ready replica's message, round robin, asap_ffn_wait_any -- the reference's poll order)")

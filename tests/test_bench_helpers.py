@@ -63,3 +63,13 @@ def test_clock_sampler_window():
 def test_cpu_config1_runs():
     r = bench.cpu_config1(reps=1)
     assert r["value"] > 0 and r["unit"] == "tokens/s"
+
+
+def test_placement():
+    assert bench.placement(8, 4, "block") == ([0, 1, 2, 3], [4, 5, 6, 7])
+    assert bench.placement(8, 4, "interleave") == ([0, 2, 4, 6], [1, 3, 5, 7])
+    assert bench.placement(8, 2, "interleave") == ([0, 4], [1, 2, 3, 5, 6, 7])
+    for world, n_a in ((2, 1), (4, 2), (6, 2), (8, 2), (8, 4)):
+        for how in ("block", "interleave"):
+            a, f = bench.placement(world, n_a, how)
+            assert a[0] == 0 and len(a) == n_a and sorted(a + f) == list(range(world))
