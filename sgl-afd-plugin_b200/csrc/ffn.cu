@@ -1495,7 +1495,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     g1.swiglu_limit = swiglu_limit;
     g1.status = status;
     g1.timeout_ns = timeout_ns;
-    gemm8::moe_gemm_fp8_kernel<0><<<sms, gemm8::THREADS, gemm8::SMEM_BYTES, st>>>(g1);
+    gemm8::moe_gemm_fp8_kernel<0><<<sms, gemm8::Cfg<0>::THREADS, gemm8::SMEM_BYTES, st>>>(g1);
     ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<0>");
     mark(3);
     gemm8::Params g2 = g1;
@@ -1508,7 +1508,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     g2.out_bf = (__nv_bfloat16*)(B + L.y2);
     g2.N = L.H;
     g2.K = L.I;
-    gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
+    gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::Cfg<1>::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
     ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<1>");
     mark(4);
     return finalize(desc, L, pa, B, R, rows, st, sms, mark);

@@ -16,7 +16,15 @@ constexpr int B_BYTES = BN * BK;  // E4M3 weights, 256 rows x 128 bytes (two 128
 constexpr int B_HALF = B_BYTES / 2;
 constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
 constexpr int NUM_EPI_WARPS = 8;
-constexpr int THREADS = 32 * (2 + NUM_EPI_WARPS);
+// GEMM1 runs 12 warps: warpgroup 0 (TMA producer, MMA issuer, two idle warps) gives registers up with setmaxnreg
+// (48 each) so the two epilogue warpgroups can hold 224 (the fp32 promotion accumulators plus two TMEM loads in
+// flight): 128 x 48 + 256 x 224 = 63488 <= 384 x 168 registers at launch.  GEMM2 keeps 10 warps (no split: it
+// measured slower with it).
+template <int EPI>
+struct Cfg {
+  static constexpr int EPI_BASE = EPI == 0 ? 4 : 2;  // first epilogue warp
+  static constexpr int THREADS = 32 * (EPI_BASE + NUM_EPI_WARPS);
+};
 constexpr uint32_t TMEM_COLS = 512;  // two 256-column partial accumulators
 constexpr int CTRL_BYTES = 4096;     // barriers, TMEM slot, expert starts, row amax exchange
 constexpr int STAGE_OUT_BYTES = NUM_EPI_WARPS * 2048;  // GEMM2 output staging, 32 rows x 64 B per epilogue warp
@@ -57,7 +65,8 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d, f
 // h = silu(gate) * up, requantised to E4M3 per 1 x 128 (the tile's 128 h columns are one K block of GEMM2).
 // EPI 1 (GEMM2, N = H): tile n covers rows [256n, 256n+256); epilogue bf16(acc * w[row]).
 template <int EPI>
-__global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(const __grid_constant__ Params p) {
+  constexpr int THREADS = Cfg<EPI>::THREADS, EPI_BASE = Cfg<EPI>::EPI_BASE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -110,6 +119,8 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
   const int num_tiles = s_mstart[P] * NT;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
 
+  if (warp < EPI_BASE) {
+  if constexpr (EPI == 0) asm volatile("setmaxnreg.dec.sync.aligned.u32 48;\n" ::: "memory");
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
@@ -195,10 +206,12 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
       volatile int no_abort = 0;
       mbar_wait(mma_done, 0, globaltimer_ns() + 200000000ull, &no_abort);
     }
+  }
   } else {
+    if constexpr (EPI == 0) asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
     // ---------------- epilogue warps: promotion of every K block, then the tile's epilogue
-    const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    const int q = warp & 3;                   // TMEM lane quarter this warp may access
+    const int half = (warp - EPI_BASE) >> 2;  // which half of the tile's columns
     const int row_in_tile = q * 32 + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
     const int NB = p.N / 128;  // 128-row weight blocks per expert
@@ -222,11 +235,28 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
         acc0[i] = 0.f;
         acc1[i] = 0.f;
       }
-      float sa_next = p.sa[row];
+      // the next K block's activation scale (GEMM1: and weight scales) is loaded one step ahead
+      float sa_next = p.sa[row], b0_next = 0.f, b1_next = 0.f;
+      if constexpr (EPI == 0) {
+        b0_next = __ldg(sb0);
+        b1_next = __ldg(sb1);
+      }
       for (int kt = 0; kt < KT; ++kt, ++it) {
-        const float sa = sa_next;
-        if (kt + 1 < KT) sa_next = p.sa[(int64_t)(kt + 1) * p.m_cap + row];
-        const float f0 = sa * __ldg(sb0 + kt), f1 = sa * __ldg(sb1 + kt);
+        float f0, f1;
+        if constexpr (EPI == 0) {
+          f0 = sa_next * b0_next;
+          f1 = sa_next * b1_next;
+          if (kt + 1 < KT) {
+            sa_next = p.sa[(int64_t)(kt + 1) * p.m_cap + row];
+            b0_next = __ldg(sb0 + kt + 1);
+            b1_next = __ldg(sb1 + kt + 1);
+          }
+        } else {
+          const float sa = sa_next;
+          if (kt + 1 < KT) sa_next = p.sa[(int64_t)(kt + 1) * p.m_cap + row];
+          f0 = sa * __ldg(sb0 + kt);
+          f1 = sa * __ldg(sb1 + kt);
+        }
         const uint32_t buf = it & 1u;
         if (!mbar_wait(&acc_full[buf], (it >> 1) & 1u, deadline, abort_flag)) {
           ok = false;
@@ -234,25 +264,48 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
         }
         tc_fence_after();
         const uint32_t tb = t_lane + buf * BN;
-        uint32_t v[32];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld_32x32b_x32(tb + col0 + 32 * c, v);
+        if constexpr (EPI == 0) {  // two TMEM loads in flight per wait (the register split leaves room)
+          uint32_t va[32], vb[32];
+          tmem_ld_32x32b_x32(tb + col0, va);
+          tmem_ld_32x32b_x32(tb + col0 + 32, vb);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc0[32 * c + i] = fmaf(__uint_as_float(v[i]), f0, acc0[32 * c + i]);
-        }
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld_32x32b_x32(tb + col1 + 32 * c, v);
+          for (int i = 0; i < 32; ++i) {
+            acc0[i] = fmaf(__uint_as_float(va[i]), f0, acc0[i]);
+            acc0[32 + i] = fmaf(__uint_as_float(vb[i]), f0, acc0[32 + i]);
+          }
+          tmem_ld_32x32b_x32(tb + col1, va);
+          tmem_ld_32x32b_x32(tb + col1 + 32, vb);
           tmem_wait_ld();
-          if (c == 1) {  // this warp's reads of the buffer are complete: hand it back to the MMA warp
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          tc_fence_before();  // this warp's reads of the buffer are complete: hand it back to the MMA warp
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            acc1[i] = fmaf(__uint_as_float(va[i]), f1, acc1[i]);
+            acc1[32 + i] = fmaf(__uint_as_float(vb[i]), f1, acc1[32 + i]);
+          }
+        } else {
+          uint32_t v[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld_32x32b_x32(tb + col0 + 32 * c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc0[32 * c + i] = fmaf(__uint_as_float(v[i]), f0, acc0[32 * c + i]);
           }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc1[32 * c + i] = fmaf(__uint_as_float(v[i]), f1, acc1[32 * c + i]);
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld_32x32b_x32(tb + col1 + 32 * c, v);
+            tmem_wait_ld();
+            if (c == 1) {  // this warp's reads of the buffer are complete: hand it back to the MMA warp
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc1[32 * c + i] = fmaf(__uint_as_float(v[i]), f1, acc1[32 * c + i]);
+          }
         }
       }
       if (!ok) break;
@@ -292,7 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_fp8_kernel(const __grid_c
         const uint32_t valid_rows = __ballot_sync(0xffffffffu, valid);
         if (!valid_rows) continue;
         const float wr = valid ? p.row_w[row] : 0.f;
-        uint8_t* wb = sOut + (warp - 2) * 2048;
+        uint8_t* wb = sOut + (warp - EPI_BASE) * 2048;
         __nv_bfloat16* out0 = p.out_bf + ((int64_t)m_blk * BM + q * 32) * p.N + (int64_t)n_t * BN + half * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
