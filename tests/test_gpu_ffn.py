@@ -200,3 +200,24 @@ def test_ffn_chain_variant_choice_same_answer(cuda_ok):
         assert moe.rel_l2(o, ref) < TOL
     np.testing.assert_array_equal(outs[0], outs[2])  # the automatic choice took weights-as-M here
     e.release()
+
+
+def test_ffn_chain_duplicate_ids_and_limits(cuda_ok):
+    """Edge cases of the routing input: duplicate expert ids within one token's top-k (each pair counts, as
+    FusedMoE sums them), the largest top-k (32) and the largest local expert count (256), a message of exactly n_max
+    tokens, ids outside the local range."""
+    rng = np.random.default_rng(31)
+    n, k, P, H, I = 96, 32, 256, 256, 128
+    e = Mxfp4Experts.random(P, H, I, seed=12)
+    gate, up, w2 = experts_to_oracle(e)
+    ids = rng.integers(-3, P + 3, (n, k)).astype(np.int32)  # duplicates and non-local ids on purpose
+    ids[:10, 1] = ids[:10, 0]
+    w = rng.random((n, k)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    x = mx.bf16_round(rng.standard_normal((n, H)).astype(np.float32))
+    h = FfnHarness(e, n_max=n, topk=k)
+    h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), seq=5)
+    check_chain(h, x, ids, w, gate, up, w2, 0, P)
+    assert int(h.done[0].item()) == 5
+    h.release()
+    e.release()

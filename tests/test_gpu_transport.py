@@ -251,3 +251,30 @@ def test_staged_dispatch_same_bytes(cuda_ok, staged):
         assert torch.equal(plain.bells[f], stg.bells[f]), f
     with pytest.raises(N.AsapError, match="permutation"):
         stg.dispatch(2, 9, x, ids, w, epochs=[2, 2, 2], staged=[0, 0, 1])
+
+
+def test_dispatch_sixteen_f_ranks(cuda_ok):
+    """The largest F count (ASAP_MAX_F = 16), uneven and empty ranges: routing table, arena bytes and doorbells."""
+    rng = np.random.default_rng(41)
+    n, H, k = 200, 256, 8
+    bounds = [0, 3, 3, 9, 12, 20, 21, 30, 31, 40, 41, 48, 49, 50, 60, 63, 64]
+    F = len(bounds) - 1
+    g = Geometry(1, 1, 1, n, H, k, F)
+    d = FakeDeployment(g, bounds)
+    x = mx.bf16_round(rng.standard_normal((n, H)).astype(np.float32))
+    ids = np.stack([rng.permutation(64)[:k] for _ in range(n)]).astype(np.int32)
+    w = rng.random((n, k)).astype(np.float32)
+    d.dispatch(1, 2, bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+    torch.cuda.synchronize()
+    assert int(d.status.item()) == 0
+    row_of, count, pad = moe.f_rank_tables(ids, bounds)
+    got_rows = d.ws[512: 512 + 4 * F * g.n_max].view(torch.int32).view(F, g.n_max)[:, :n].cpu().numpy()
+    np.testing.assert_array_equal(got_rows, row_of)
+    for f in range(F):
+        c = int(count[f])
+        reg = d.region(f).cpu().numpy()
+        if not pad[f]:
+            sel = row_of[f] >= 0
+            np.testing.assert_array_equal(reg[: c * H * 2].view(np.uint16).reshape(c, H), mx.bf16_bits(x[sel]))
+        word = int(d.bells[f][g.bell_off(0, 0) // 8].item()) & 0xFFFFFFFFFFFFFFFF
+        assert word == pack_doorbell(1, c, 2, 1)
