@@ -324,6 +324,8 @@ def run_single(args):
     experts = make_experts(E, 0, 1, dev)
     lb = Loopback(Geometry(1, 1, 2, T, H, K_TOP, 1), {0: experts}, timeout_s=30.0)
     lb.install()
+    if args.pair_gemm:
+        lb.sched.set_pair_gemm(True)
     shared = SharedExpert(dev) if SHARED else (lambda _x: None)
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
@@ -584,6 +586,8 @@ def run_sweep(args):
     T_max = max(SWEEP_T)
     lb = Loopback(Geometry(1, 1, 2, T_max, H, K_TOP, n_f), per_f, timeout_s=30.0, graphs=args.graphs)
     lb.install()
+    for s in lb.scheds if args.pair_gemm else ():
+        s.set_pair_gemm(True)
     shared = SharedExpert(dev)
     x_all = torch.randn(T_max, H, device=dev, generator=torch.Generator(device=dev).manual_seed(0)).to(torch.bfloat16)
     disp = AsapDispatcher(0)
@@ -691,6 +695,8 @@ def run_stack(args):
         layers = {l: make_experts(E, 0, 1 + l, dev) for l in range(L)}
         lb = Loopback(Geometry(1, 1, 2, Tmb, H, K_TOP, 1), layers, timeout_s=60.0)
         lb.install()
+        if args.pair_gemm:
+            lb.sched.set_pair_gemm(True)
         bounds = [0, E]
     else:
         import torch.distributed as dist
@@ -712,6 +718,8 @@ def run_stack(args):
             server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                                host="127.0.0.1", port=0).start()
             sched = FfnScheduler(server, layers, timeout_s=120.0)
+            if args.pair_gemm:
+                sched.set_pair_gemm(True)
             ep = ("127.0.0.1", server.port)
         eps = [None] * world
         dist.all_gather_object(eps, ep)
@@ -872,6 +880,8 @@ def run_multi(args):
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
         sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s, join=n_a if args.join_replicas else 1)
+        if args.pair_gemm:
+            sched.set_pair_gemm(True)
         ep = ("127.0.0.1", server.port)
     eps = [None] * world
     dist.all_gather_object(eps, ep)
@@ -1102,6 +1112,8 @@ def main():
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
+    ap.add_argument("--pair-gemm", action="store_true",
+                    help="MXFP4 expert GEMMs on 2-CTA clusters (one MMA over two SMs per 256 x 256 tile)")
     ap.add_argument("--staged", action="store_true",
                     help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that order")
     ap.add_argument("--graphs", action="store_true",

@@ -303,6 +303,11 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t rows,
  * 128-row token blocks are on average less than half full). */
 int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode);
 
+/* MXFP4 GEMM tiles of this workspace's jobs: 0 one SM per 128 x 256 tile; 1 one tcgen05 MMA over the two SMs of a
+ * 2-CTA cluster per 256 x 256 tile (each SM stages half the weight tile, so the load pipeline is deeper).  Same
+ * arithmetic either way.  ASAP_EINVAL when no 2-CTA cluster of that kernel fits on the device. */
+int asap_ffn_set_pair_gemm(uint64_t ws_handle, int32_t on);
+
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
  * stream around its 5 stages (routing, quantise+permute, gemm1, gemm2, reduce+reply); last_timing waits
  * for the recorded jobs (the last 64 since enable) and returns each kernel's mean duration in ms (n >= 5). */

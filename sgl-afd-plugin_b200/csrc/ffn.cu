@@ -559,7 +559,10 @@ __device__ __forceinline__ uint64_t sdesc_sf(const void* p) {
 
 struct Params {
   CUtensorMap tmap_a;  // activations [m_cap, K] bytes (E4M3)
-  CUtensorMap tmap_b;  // weights [P * N, K] E2M1 (4-bit, unpacked to 16 B per 16 values in smem)
+  CUtensorMap tmap_b;  // weights [P * N, K] E2M1 (4-bit, unpacked to 16 B per 16 values in smem); the pair kernel:
+                       // 128-row boxes
+  CUtensorMap tmap_sfa;  // pair kernel only: activation scale atoms as [m_cap/128 * K/128] rows of 128 u32
+  CUtensorMap tmap_sfb;  // pair kernel only: weight scale atoms as [P * K/128] rows of N u32
   const uint8_t* sfa;  // activation scale atoms [m_cap/128][K/128][512]
   const uint8_t* sfb;  // weight scale atoms per expert [K/128][N/128][512]
   uint64_t sfb_expert_stride;
@@ -610,6 +613,57 @@ __device__ __forceinline__ void store_rows_bf16x32(const uint32_t (&o)[16], uint
     if ((valid >> row) & 1u) *reinterpret_cast<uint4*>(out0 + row * row_stride + u * 8) = val;
   }
   __syncwarp();
+}
+
+// One epilogue warp's share of a finished 128 x 256 accumulator tile, already drained from TMEM into v: lane = row
+// `row` of quarter q, column half `half`.  EPI 0: h = silu(gate) * up quantised to MXFP8 (gate columns
+// [64 half, 64 half + 64) of the tile, up columns 128 further).  EPI 1: bf16(acc * w[row]) through the warp's 2 KB
+// staging buffer `wb`.
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const Params& p, const uint32_t (&v)[4][32], int64_t row, bool valid,
+                                               int m_blk, int n_t, int q, int half, uint8_t* wb, int lane) {
+  if constexpr (EPI == 1) {  // warp-cooperative stores: every lane takes part, invalid rows are masked
+    const uint32_t valid_rows = __ballot_sync(0xffffffffu, valid);
+    if (!valid_rows) return;
+    const float wr = valid ? p.row_w[row] : 0.f;
+    __nv_bfloat16* out0 = p.out_bf + ((int64_t)m_blk * BM + q * 32) * p.N + (int64_t)n_t * BN + half * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const __nv_bfloat162 b2 =
+            __floats2bfloat162_rn(__uint_as_float(v[c][2 * i]) * wr, __uint_as_float(v[c][2 * i + 1]) * wr);
+        o[i] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      store_rows_bf16x32(o, wb, out0 + c * 32, p.N, valid_rows, lane);
+    }
+  } else {
+    if (!valid) return;
+    const int I = p.N / 2;
+    const int kblocks = I / 32;
+    const float lim = p.swiglu_limit;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float h[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float gv = __uint_as_float(v[c][i]), uv = __uint_as_float(v[2 + c][i]);
+        if (lim > 0.f) {
+          gv = fminf(gv, lim);
+          uv = fminf(fmaxf(uv, -lim), lim);
+        }
+        h[i] = silu_f(gv) * uv;
+      }
+      uint4 lo, hi;
+      const uint32_t sb = mx_quant32(h, lo, hi);
+      const int hcol = n_t * 128 + half * 64 + c * 32;
+      uint4* dst = reinterpret_cast<uint4*>(p.out_q + row * I + hcol);
+      dst[0] = lo;
+      dst[1] = hi;
+      p.out_sf[sf_atom_off(row, hcol / 32, kblocks)] = (uint8_t)sb;
+    }
+  }
 }
 
 // EPI 0: h = silu(gate) * up, quantised to MXFP8 (GEMM1).  EPI 1: bf16(acc * w[row]) (GEMM2).
@@ -788,51 +842,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       acc_phase ^= 1u;
-      if constexpr (EPI == 1) {  // warp-cooperative stores: every lane takes part, invalid rows are masked
-        const uint32_t valid_rows = __ballot_sync(0xffffffffu, valid);
-        if (!valid_rows) continue;
-        const float wr = valid ? p.row_w[row] : 0.f;
-        uint8_t* wb = sOut + (warp - 2) * 2048;
-        __nv_bfloat16* out0 = p.out_bf + ((int64_t)m_blk * BM + q * 32) * p.N + (int64_t)n_t * BN + half * 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const __nv_bfloat162 b2 =
-                __floats2bfloat162_rn(__uint_as_float(v[c][2 * i]) * wr, __uint_as_float(v[c][2 * i + 1]) * wr);
-            o[i] = *reinterpret_cast<const uint32_t*>(&b2);
-          }
-          store_rows_bf16x32(o, wb, out0 + c * 32, p.N, valid_rows, lane);
-        }
-        continue;
-      }
-      if (!valid) continue;
-      if constexpr (EPI == 0) {
-        const int I = p.N / 2;
-        const int kblocks = I / 32;
-        const float lim = p.swiglu_limit;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float h[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float gv = __uint_as_float(v[c][i]), uv = __uint_as_float(v[2 + c][i]);
-            if (lim > 0.f) {
-              gv = fminf(gv, lim);
-              uv = fminf(fmaxf(uv, -lim), lim);
-            }
-            h[i] = silu_f(gv) * uv;
-          }
-          uint4 lo, hi;
-          const uint32_t sb = mx_quant32(h, lo, hi);
-          const int hcol = n_t * 128 + half * 64 + c * 32;
-          uint4* dst = reinterpret_cast<uint4*>(p.out_q + row * I + hcol);
-          dst[0] = lo;
-          dst[1] = hi;
-          p.out_sf[sf_atom_off(row, hcol / 32, kblocks)] = (uint8_t)sb;
-        }
-      }
+      epilogue_store<EPI>(p, v, row, valid, m_blk, n_t, q, half, sOut + (warp - 2) * 2048, lane);
     }
   }
   tc_fence_before();
@@ -845,6 +855,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
 }  // namespace gemm
 
 #include "gemm_fp8.cuh"
+#include "gemm_pair.cuh"
 #include "gemm_small.cuh"
 
 // ------------------------------------------------------------------ K5b: weighted reduce + reply
@@ -957,7 +968,8 @@ static EncodeTiledFn encode_fn() {
 }
 
 static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -968,7 +980,7 @@ static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled(%s) failed: %d", what, (int)r);
     return ASAP_ECUDA;
@@ -982,7 +994,8 @@ struct ExpertsHandle {
   asap_mxfp4_experts_t e;   // kMxfp4 (num_local/expert_base/hidden/inter filled for both kinds)
   asap_fp8_experts_t f8;    // kFp8Block
   CUtensorMap w13_map, w2_map;
-  CUtensorMap w13_map_t, w2_map_t;  // kMxfp4: 128-row boxes for the weights-as-M kernels
+  CUtensorMap w13_map_t, w2_map_t;  // kMxfp4: 128-row boxes (weights-as-M kernels, CTA-pair kernels)
+  CUtensorMap w13_sf_map, w2_sf_map;  // kMxfp4: scale atoms as rows of u32 (CTA-pair kernels)
 };
 constexpr int kTimedKernels = 5;  // routing (count+scan+place), quantise+permute, gemm1, gemm2, finalize_reply
 constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
@@ -990,8 +1003,10 @@ struct WsHandle {
   uint8_t* base;
   WsLayout L;
   CUtensorMap xq_map, hq_map;
+  CUtensorMap xq_sf_map, hq_sf_map;  // activation scale atoms as rows of 128 u32 (CTA-pair kernels)
   bool timing = false;
   int small_mode = 0;  // PermArgs::small_mode (the weights-as-M kernels measured slower: opt-in)
+  int pair_gemm = 0;   // 1: the MXFP4 GEMMs run on CTA pairs (moe_gemm_pair_kernel)
   int jobs = 0;  // jobs recorded since enable
   cudaEvent_t ev[kTimedJobs][kTimedKernels + 1] = {};
 };
@@ -1013,6 +1028,7 @@ static WsHandle* get_ws(uint64_t h) {
 }
 
 static bool gemm_attr_set = false;
+static int g_pair_clusters = 0;  // CTA pairs of moe_gemm_pair_kernel resident at once (0: pairs unavailable)
 
 static int ensure_gemm_attrs() {
   if (gemm_attr_set) return ASAP_OK;
@@ -1028,8 +1044,47 @@ static int ensure_gemm_attrs() {
                                  gemmT::SMEM_BYTES));
   ASAP_CUDA(cudaFuncSetAttribute(gemmT::moe_gemm_t_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  gemmT::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemmP::moe_gemm_pair_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemmP::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(gemmP::moe_gemm_pair_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemmP::SMEM_BYTES));
+  {  // CTA pairs resident at once: the persistent pair grid is sized to it
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    cfg.blockDim = dim3(gemmP::THREADS);
+    cfg.dynamicSmemBytes = gemmP::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n0 = 0, n1 = 0;
+    ASAP_CUDA(cudaOccupancyMaxActiveClusters(&n0, gemmP::moe_gemm_pair_kernel<0>, &cfg));
+    ASAP_CUDA(cudaOccupancyMaxActiveClusters(&n1, gemmP::moe_gemm_pair_kernel<1>, &cfg));
+    g_pair_clusters = std::min(std::min(n0, n1), sm_count() / 2);
+  }
   gemm_attr_set = true;
   return ASAP_OK;
+}
+
+// The CTA-pair GEMM: clusters of 2 along x, one persistent pair per resident cluster slot.
+template <int EPI>
+static cudaError_t launch_pair(const gemm::Params& p, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * g_pair_clusters);
+  cfg.blockDim = dim3(gemmP::THREADS);
+  cfg.dynamicSmemBytes = gemmP::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemmP::moe_gemm_pair_kernel<EPI>, p);
 }
 
 // K5b launch shared by both weight kinds; `mark` records the job's last timing event.
@@ -1090,6 +1145,13 @@ int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
   if (!rc)
     rc = make_tmap_2d(&h->w2_map_t, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2,
                       gemmT::BK, gemmT::BW, "w2 (128-row boxes)");
+  // scale atoms [P][K/128][N/128][512 B] as rows of N u32: one box = the two atoms of a 256-row N tile
+  if (!rc)
+    rc = make_tmap_2d(&h->w13_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, (const void*)e->w13_sf, 2 * I, P * (H / 128),
+                      8 * I, gemmP::SFB_BYTES / 4, 1, "w13 scales", CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&h->w2_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, (const void*)e->w2_sf, H, P * (I / 128), 4 * H,
+                      gemmP::SFB_BYTES / 4, 1, "w2 scales", CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) {
     delete h;
     return rc;
@@ -1179,6 +1241,15 @@ int asap_ffn_ws_register(uint64_t ws, int32_t n_max, int32_t topk, int32_t num_l
   if (!rc)
     rc = make_tmap_2d(&h->hq_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, h->base + h->L.hq, inter, h->L.m_cap, inter,
                       gemm::BK, gemm::BM, "hq");
+  // activation scale atoms [m_cap/128][K/128][512 B] as rows of 128 u32: one box = one atom
+  if (!rc)
+    rc = make_tmap_2d(&h->xq_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, h->base + h->L.xq_sf, 128,
+                      (uint64_t)(h->L.m_cap / 128) * (hidden / 128), 512, 128, 1, "xq scales",
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&h->hq_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, h->base + h->L.hq_sf, 128,
+                      (uint64_t)(h->L.m_cap / 128) * (inter / 128), 512, 128, 1, "hq scales",
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) {
     delete h;
     return rc;
@@ -1536,8 +1607,16 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g1.swiglu_limit = swiglu_limit;
   g1.status = status;
   g1.timeout_ns = timeout_ns;
-  gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
-  ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
+  const bool pairs = wh->pair_gemm != 0 && g_pair_clusters > 0;
+  if (pairs) {
+    g1.tmap_b = eh->w13_map_t;
+    g1.tmap_sfa = wh->xq_sf_map;
+    g1.tmap_sfb = eh->w13_sf_map;
+    ASAP_CUDA(launch_pair<0>(g1, st));
+  } else {
+    gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
+    ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
+  }
   gemmT::Params t1;
   memset(&t1, 0, sizeof(t1));
   t1.tmap_w = eh->w13_map_t;
@@ -1564,7 +1643,9 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
 
   gemm::Params g2 = g1;
   g2.tmap_a = wh->hq_map;
-  g2.tmap_b = eh->w2_map;
+  g2.tmap_b = pairs ? eh->w2_map_t : eh->w2_map;
+  g2.tmap_sfa = wh->hq_sf_map;
+  g2.tmap_sfb = eh->w2_sf_map;
   g2.sfa = B + L.hq_sf;
   g2.sfb = (const uint8_t*)E.w2_sf;
   g2.sfb_expert_stride = (uint64_t)(L.I / 32) * L.H;
@@ -1573,8 +1654,12 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.out_bf = (__nv_bfloat16*)(B + L.y2);
   g2.N = L.H;
   g2.K = L.I;
-  gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
-  ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
+  if (pairs) {
+    ASAP_CUDA(launch_pair<1>(g2, st));
+  } else {
+    gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
+    ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
+  }
   gemmT::Params t2 = t1;
   t2.tmap_w = eh->w2_map_t;
   t2.tmap_x = wh->hq_map;
@@ -1591,6 +1676,20 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   mark(4);
 
   return finalize(desc, L, pa, B, R, rows, st, sms, mark);
+}
+
+int asap_ffn_set_pair_gemm(uint64_t ws_handle, int32_t on) {
+  WsHandle* w = get_ws(ws_handle);
+  if (!w || (on != 0 && on != 1)) {
+    set_error("asap_ffn_set_pair_gemm: unknown workspace handle or value %d outside {0, 1}", on);
+    return ASAP_EINVAL;
+  }
+  if (on && g_pair_clusters < 1) {
+    set_error("asap_ffn_set_pair_gemm: no 2-CTA cluster of the pair GEMM fits on this device");
+    return ASAP_EINVAL;
+  }
+  w->pair_gemm = on;
+  return ASAP_OK;
 }
 
 int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode) {
