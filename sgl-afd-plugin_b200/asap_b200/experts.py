@@ -11,8 +11,10 @@ asap_mxfp4_experts_t):
   w2      uint8 [P, H, I/2]
   w2_sf   uint8 [P, I/128, H/128, 512]
 
-``from_logical`` builds that layout from plain [P, rows, K] codes and [P, rows, K/32] scale bytes (the
-checkpoint layout after SGLang's loader, W13 = [W1; W3]); ``random`` makes seeded synthetic weights.
+``from_packed`` builds that layout from the checkpoint's tensors stacked per layer ([P, rows, K/2] E2M1 pairs,
+[P, rows, K/32] scale bytes, W13 = [W1; W3] as SGLang's loader stacks them; ``asap_b200.ingest`` reads them from
+safetensors shards); ``from_logical`` does the same from unpacked codes; ``random`` makes seeded synthetic
+weights.
 
 FP8 (``Fp8Experts``): E4M3 weights with one fp32 scale per 128 x 128 block, in the checkpoint's own layout
 (include/asap.h, asap_fp8_experts_t): w13 [P, 2I, H] (gate rows then up rows), w13_scale [P, 2I/128, H/128],
@@ -83,29 +85,33 @@ class Mxfp4Experts:
         return cls(w13, w13_sf, w2, w2_sf, num_local=P, expert_base=expert_base, hidden=H, inter=I)
 
     @classmethod
+    def from_packed(cls, w13: torch.Tensor, w13_scales: torch.Tensor, w2: torch.Tensor, w2_scales: torch.Tensor, *,
+                    expert_base: int = 0, device="cuda") -> "Mxfp4Experts":
+        """Checkpoint-order tensors -> device layout on ``device``: w13 [P, 2I, H/2] E2M1 pairs (rows: I gate then
+        I up), w13_scales [P, 2I, H/32] E8M0 bytes, w2 [P, H, I/2], w2_scales [P, H, I/32].  The repacking runs
+        where the inputs are (CPU, or the device for large layers)."""
+        d13, s13, d2, s2 = mxfp4_device_layout(w13, w13_scales, w2, w2_scales)
+        P, two_i, half_h = w13.shape
+
+        def dev(t):
+            owner, view = _aligned_empty(t.numel(), device)
+            view.copy_(t.reshape(-1))
+            return view
+
+        return cls(dev(d13), dev(s13), dev(d2), dev(s2), num_local=P, expert_base=expert_base, hidden=2 * half_h,
+                   inter=two_i // 2)
+
+    @classmethod
     def from_logical(cls, w13_codes: np.ndarray, w13_scales: np.ndarray, w2_codes: np.ndarray,
                      w2_scales: np.ndarray, *, expert_base: int = 0, device="cuda") -> "Mxfp4Experts":
         """w13_codes [P, 2I, H] (rows: I gate then I up), w13_scales [P, 2I, H/32], w2_codes [P, H, I],
         w2_scales [P, H, I/32] -> device layout."""
-        P, two_i, H = w13_codes.shape
-        I = two_i // 2
-        r = np.arange(two_i)
-        b, within = r // 256, r % 256
-        src_rows = np.where(within < 128, 128 * b + within, I + 128 * b + (within - 128))
-        w13_dev = w13_codes[:, src_rows, :]
-        s13_dev = w13_scales[:, src_rows, :]
-        packed13 = (w13_dev[..., 0::2] | (w13_dev[..., 1::2] << 4)).astype(np.uint8)
-        packed2 = (w2_codes[..., 0::2] | (w2_codes[..., 1::2] << 4)).astype(np.uint8)
-        atoms13 = np.stack([_kmajor_atoms(s13_dev[e]) for e in range(P)])
-        atoms2 = np.stack([_kmajor_atoms(w2_scales[e]) for e in range(P)])
+        def pack(c):
+            return torch.from_numpy((c[..., 0::2] | (c[..., 1::2] << 4)).astype(np.uint8))
 
-        def dev(a):
-            owner, view = _aligned_empty(a.size, device)
-            view.copy_(torch.from_numpy(np.ascontiguousarray(a).reshape(-1)))
-            return view
-
-        return cls(dev(packed13), dev(atoms13), dev(packed2), dev(atoms2), num_local=P, expert_base=expert_base,
-                   hidden=H, inter=I)
+        return cls.from_packed(pack(w13_codes), torch.from_numpy(np.ascontiguousarray(w13_scales, np.uint8)),
+                               pack(w2_codes), torch.from_numpy(np.ascontiguousarray(w2_scales, np.uint8)),
+                               expert_base=expert_base, device=device)
 
 
 class Fp8Experts:
@@ -176,12 +182,56 @@ class Fp8Experts:
         return cls(w13, s13, w2, s2, num_local=P, expert_base=expert_base, hidden=H, inter=I)
 
 
-def _kmajor_atoms(sf: np.ndarray) -> np.ndarray:
-    """[N, K/32] scale bytes -> atoms [K/128][N/128][512]: byte (r%32)*16 + ((r/32)%4)*4 + kb%4 of atom
+def _sf_atoms(sf: torch.Tensor) -> torch.Tensor:
+    """[P, N, K/32] scale bytes -> [P, K/128 * N/128 * 512] atoms: byte (r%32)*16 + ((r/32)%4)*4 + kb%4 of atom
     (kb/4, r/128), the order the tcgen05 scale-factor copy (32x128b, 4 warps) reads."""
-    n, kblocks = sf.shape
-    out = np.zeros(n * kblocks, dtype=np.uint8)
-    r, kb = np.meshgrid(np.arange(n), np.arange(kblocks), indexing="ij")
+    P, n, kblocks = sf.shape
+    r = torch.arange(n, device=sf.device).view(n, 1)
+    kb = torch.arange(kblocks, device=sf.device).view(1, kblocks)
     off = ((kb >> 2) * (n >> 7) + (r >> 7)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (kb & 3)
-    out[off] = sf
+    out = torch.empty(P, n * kblocks, dtype=torch.uint8, device=sf.device)
+    out[:, off.reshape(-1)] = sf.reshape(P, -1)
     return out
+
+
+def w13_device_rows(inter: int, device=None) -> torch.Tensor:
+    """Device row r of w13 -> row of the checkpoint's [W1; W3] stack: blocks of 256 device rows hold gate rows
+    128b..128b+127 then up rows 128b..128b+127."""
+    r = torch.arange(2 * inter, device=device)
+    b, within = r // 256, r % 256
+    return torch.where(within < 128, 128 * b + within, inter + 128 * b + (within - 128))
+
+
+def mxfp4_device_layout(w13: torch.Tensor, w13_scales: torch.Tensor, w2: torch.Tensor, w2_scales: torch.Tensor):
+    """Checkpoint-order MXFP4 tensors (see Mxfp4Experts.from_packed) -> the four device-layout byte tensors
+    (w13 [P, 2I, H/2] in 128-row gate/up blocks, w13 scale atoms, w2 [P, H, I/2], w2 scale atoms), on the inputs'
+    device.  Raises ValueError on shapes or dtypes the GEMMs cannot take."""
+    w13, w13_scales, w2, w2_scales = (_as_bytes(t) for t in (w13, w13_scales, w2, w2_scales))
+    if w13.dim() != 3 or w2.dim() != 3:
+        raise ValueError("w13 / w2 must be [P, rows, K/2]")
+    P, two_i, half_h = w13.shape
+    H, I = 2 * half_h, two_i // 2
+    if H % 256 or I % 128 or I < 128:
+        raise ValueError(f"MXFP4 experts need hidden % 256 == 0 and inter % 128 == 0 (got H={H}, I={I})")
+    want = {"w13_scales": (w13_scales, (P, 2 * I, H // 32)), "w2": (w2, (P, H, I // 2)),
+            "w2_scales": (w2_scales, (P, H, I // 32))}
+    for name, (t, shape) in want.items():
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name}: expected shape {shape}, got {tuple(t.shape)}")
+    rows = w13_device_rows(I, w13.device)
+    d13 = w13.index_select(1, rows).contiguous()
+    s13 = _sf_atoms(w13_scales.index_select(1, rows))
+    return d13, s13, w2.contiguous(), _sf_atoms(w2_scales)
+
+
+def _as_bytes(t: torch.Tensor) -> torch.Tensor:
+    """E2M1 pairs / E8M0 scales as stored in checkpoints (uint8, int8, float8_e8m0fnu) -> a uint8 view."""
+    t = torch.as_tensor(t)
+    if t.dtype == torch.uint8:
+        return t
+    if t.dtype in (torch.int8,) + _BYTE_FLOATS:
+        return t.view(torch.uint8)
+    raise ValueError(f"expected a one-byte dtype for MXFP4 codes / scales, got {t.dtype}")
+
+
+_BYTE_FLOATS = tuple(getattr(torch, n) for n in ("float8_e8m0fnu",) if hasattr(torch, n))

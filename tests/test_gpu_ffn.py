@@ -247,3 +247,48 @@ def test_ffn_chain_pair_gemm(cuda_ok, n, k, P, H, I, e0):
         h.release()
     np.testing.assert_array_equal(outs[0], outs[1])
     e.release()
+
+
+def test_ffn_chain_from_checkpoint(cuda_ok, tmp_path):
+    """F-rank weight ingest end to end: a safetensors shard with two ranks' experts over two layers (DeepSeek-V4
+    names, int8 codes and float8_e8m0fnu scales mixed in); `ingest.load_layer` reads this rank's experts of one
+    layer, the registered bytes dequantise to the checkpoint's weights, and the chain matches the oracle."""
+    from safetensors.torch import save_file
+
+    from asap_b200 import ingest
+
+    rng = np.random.default_rng(8)
+    H, I, layer = 256, 128, 1
+    mine, others = range(4, 8), range(0, 4)
+    tensors, logical = {}, {}
+    for l in (0, 1):
+        for e in list(others) + list(mine):
+            for p, name, (rows, kk) in (("gate", "w1", (I, H)), ("up", "w3", (I, H)), ("down", "w2", (H, I))):
+                codes = rng.integers(0, 16, (rows, kk)).astype(np.uint8)
+                scales = rng.integers(117, 121, (rows, kk // 32)).astype(np.uint8)
+                w = torch.from_numpy(mx.pack_nibbles(codes))
+                s = torch.from_numpy(scales)
+                if e % 2:
+                    w = w.view(torch.int8)
+                if e % 3 == 0 and hasattr(torch, "float8_e8m0fnu"):
+                    s = s.view(torch.float8_e8m0fnu)
+                tensors[f"layers.{l}.ffn.experts.{e}.{name}.weight"] = w
+                tensors[f"layers.{l}.ffn.experts.{e}.{name}.scale"] = s
+                logical[l, e, p] = mx.e2m1_decode(codes) * np.repeat(mx.e8m0_value(scales), 32, axis=-1)
+    tensors["layers.1.ffn.shared_experts.w1.weight"] = torch.zeros(4, 4)
+    path = str(tmp_path / "model-00001.safetensors")
+    save_file(tensors, path)
+    e = ingest.load_layer([path], layer, mine, num_layers=2)
+    assert (e.num_local, e.expert_base, e.hidden, e.inter) == (4, 4, H, I)
+    gate, up, w2 = experts_to_oracle(e)
+    for i, ex in enumerate(mine):
+        np.testing.assert_array_equal(gate[i], logical[layer, ex, "gate"])
+        np.testing.assert_array_equal(up[i], logical[layer, ex, "up"])
+        np.testing.assert_array_equal(w2[i], logical[layer, ex, "down"])
+    n, k = 200, 4
+    x, ids, w = random_inputs(rng, n, H, k, 2, 10, bias_expert=4)
+    h = FfnHarness(e, n_max=n, topk=k)
+    h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+    check_chain(h, x, ids, w, gate, up, w2, 4, 4)
+    h.release()
+    e.release()
