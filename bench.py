@@ -243,6 +243,44 @@ def gemm_flops(pairs):
     return 2.0 * pairs * H * (2 * I), 2.0 * pairs * I * H
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
+
+
+def expert_bytes():
+    """Weight bytes of one routed expert in the layer's format (codes + scales)."""
+    if KIND == "fp8":
+        return 3 * H * I + 4 * (3 * (H // 128) * (I // 128))
+    return 3 * H * I // 2 + 3 * H * I // 32
+
+
+def layer_roofline(n_a, T, f_rows, bounds, ms, peaks, peak_kind):
+    """Per-layer roofline of an nA x nF step: for each F rank, the time its inbound rows take over NVLink
+    (x bf16 + ids + weights per routed row), its reply rows outbound, its expert GEMMs at the FP8-rate tensor peak
+    (pairs expected under uniform routing: every replica's T·k pairs spread over the experts), and its weight +
+    activation bytes at the HBM peak.  Bound = the largest of those over F ranks; serial = in + flop + out."""
+    fp8_tflops = 2.0 * peaks["bf16_tflops_sustained"]
+    per_f = []
+    for f, rows in enumerate(f_rows):
+        p_f = bounds[f + 1] - bounds[f]
+        pairs = n_a * T * K_TOP * p_f / E
+        t_in = rows * (2 * H + 8 * K_TOP) / (NVLINK_GBS * 1e9) * 1e3
+        t_out = rows * 2 * H / (NVLINK_GBS * 1e9) * 1e3
+        t_flop = pairs * 6.0 * H * I / (fp8_tflops * 1e12) * 1e3
+        t_hbm = (p_f * expert_bytes() + rows * (2 * H + 8 * K_TOP) + rows * 2 * H) / (peaks["hbm_gbs"] * 1e9) * 1e3
+        per_f.append((t_in, t_out, t_flop, t_hbm))
+    worst = max(per_f, key=lambda t: max(t))
+    names = ("nvlink_in", "nvlink_out", "tensor", "hbm")
+    t_bound = max(max(t) for t in per_f)
+    t_serial = max(t[0] + t[1] + t[2] for t in per_f)
+    return {"bound": names[worst.index(max(worst))], "t_in_ms": round(worst[0], 4), "t_out_ms": round(worst[1], 4),
+            "t_flop_ms": round(worst[2], 4), "t_hbm_ms": round(worst[3], 4), "t_bound_ms": round(t_bound, 4),
+            "t_serial_ms": round(t_serial, 4), "measured_ms": round(ms, 4), "frac": round(t_bound / ms, 4),
+            "frac_serial": round(t_serial / ms, 4),
+            "peaks": {"nvlink_gbs": NVLINK_GBS, "fp8_tflops": round(fp8_tflops, 1), "hbm_gbs": peaks["hbm_gbs"],
+                      "source": f"{peak_kind} MEASURED_PEAKS (FP8 = 2 x bf16 sustained); NVLink measured peer copy"},
+            "pairs": "expected under uniform routing"}
+
+
 class HostPipeline:
     """End-to-end driver of the public API on pinned host buffers: every step copies its inputs host->device and
     its output device->host; step i+1's upload and step i's download run on copy streams while the compute stream
@@ -1057,6 +1095,8 @@ def run_multi(args):
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
             line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
+            if args.routing != "zipf":
+                line["layer_roofline"] = layer_roofline(n_a, T, res["f_rows"], bounds, ms, *load_peaks())
             if "e2e_ms" in res:
                 e = res["e2e_ms"]
                 line["e2e"] = {"value": round(n_a * T / (e * 1e-3), 1), "unit": "tokens/s",

@@ -73,3 +73,21 @@ def test_placement():
         for how in ("block", "interleave"):
             a, f = bench.placement(world, n_a, how)
             assert a[0] == 0 and len(a) == n_a and sorted(a + f) == list(range(world))
+
+
+def test_layer_roofline_4a4f():
+    """The per-layer roofline at 4A4F (config 2): each F rank receives the 90.36% of each replica's tokens that
+    route to its 64 experts, 11.54 TFLOP of expert GEMMs."""
+    peaks = {"hbm_gbs": 6547.5, "bf16_tflops_sustained": 1361.5}
+    rows = round(4 * 16384 * 0.9036)
+    r = bench.layer_roofline(4, 16384, [rows] * 4, [0, 64, 128, 192, 256], 8.06, peaks, "measured")
+    assert r["bound"] == "tensor"
+    assert r["t_flop_ms"] == pytest.approx(11.544e12 / 2723e12 * 1e3, rel=1e-3)   # 4.24 ms
+    assert r["t_in_ms"] == pytest.approx(rows * (2 * 7168 + 64) / 770e9 * 1e3, abs=1e-4)  # 1.11 ms
+    assert r["t_out_ms"] == pytest.approx(rows * 2 * 7168 / 770e9 * 1e3, abs=1e-4)
+    assert r["t_serial_ms"] == pytest.approx(r["t_in_ms"] + r["t_out_ms"] + r["t_flop_ms"], abs=1e-3)
+    assert 6.3 < r["t_serial_ms"] < 6.5
+    assert r["frac"] == pytest.approx(r["t_bound_ms"] / 8.06, abs=1e-4)
+    # uneven F ranks: the most loaded one sets the bound
+    r2 = bench.layer_roofline(2, 16384, [30000, 50000], [0, 100, 256], 5.0, peaks, "measured")
+    assert r2["t_flop_ms"] == pytest.approx(2 * 16384 * 8 * 156 / 256 * 6 * 7168 * 2048 / 2723e12 * 1e3, rel=1e-3)
