@@ -16,6 +16,10 @@
 //             on the leader's `acc_empty` (16 arrivals: both CTAs' epilogue warps).
 // An expert with an odd number of blocks leaves the follower's half of its last pair tile without rows: the
 // follower then loads the leader's block again (every access in bounds) and stores nothing.
+// Every mbarrier wait is bounded by the job's deadline (an expired one raises the CTA's abort flag and reports
+// ASAP_ST_PIPELINE_TIMEOUT).  The two cluster barriers (after set-up, before TMEM is freed) cannot be bounded;
+// both CTAs reach each of them after bounded work only, and the early return for weights-as-M jobs is taken by
+// both CTAs alike (it reads the same job descriptor).
 
 namespace gemmP {
 using gemm::BK;
