@@ -246,6 +246,21 @@ def gemm_flops(pairs):
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
 
 
+def hbm_kernel_gbs(T, pairs, kernel_ms):
+    """Algorithmic GB/s of the two HBM-bound F kernels: quantise+permute reads each token's bf16 row once and
+    writes its activation codes + scales into every local pair row; the weighted reduce reads every pair's bf16 row
+    and writes each token's reply row."""
+    scale_bytes = H // 32 if KIND == "mxfp4" else 4 * (H // 128)
+    qp = T * 2 * H + pairs * (H + scale_bytes)
+    red = pairs * 2 * H + T * 2 * H
+    def gbs(nbytes, ms):
+        return round(nbytes / (ms * 1e-3) / 1e9, 1) if ms and ms > 0 else None
+
+    return {"quantise_permute": gbs(qp, kernel_ms.get("quantise_permute")),
+            "reduce_reply": gbs(red, kernel_ms.get("reduce_reply")),
+            "bytes": {"quantise_permute": qp, "reduce_reply": red}}
+
+
 def expert_bytes():
     """Weight bytes of one routed expert in the layer's format (codes + scales)."""
     if KIND == "fp8":
@@ -471,6 +486,7 @@ def run_single(args):
                      "frac_of_fp4_dense_nominal" if KIND == "mxfp4" else "frac_of_fp8_dense_nominal":
                          round(achieved / (9000.0 if KIND == "mxfp4" else 4500.0), 4)},
         "kernels_ms": {k: round(v, 4) for k, v in kernel_ms.items()},
+        "kernels_gbs": hbm_kernel_gbs(T, pairs, kernel_ms),
         "dispatch_ms": round(statistics.median(dsp), 4), "combine_ms": round(statistics.median(cmb), 4),
         "dispatch_gbs_algorithmic": round(nvlink_bytes_dispatch / (statistics.median(dsp) * 1e-3) / 1e9, 1),
         "pairs": pairs, "gemm_tflops_per_step": round((g1_flops + g2_flops) / 1e12, 3),

@@ -91,3 +91,13 @@ def test_layer_roofline_4a4f():
     # uneven F ranks: the most loaded one sets the bound
     r2 = bench.layer_roofline(2, 16384, [30000, 50000], [0, 100, 256], 5.0, peaks, "measured")
     assert r2["t_flop_ms"] == pytest.approx(2 * 16384 * 8 * 156 / 256 * 6 * 7168 * 2048 / 2723e12 * 1e3, rel=1e-3)
+
+
+def test_hbm_kernel_gbs():
+    T, pairs = 16384, 131072
+    r = bench.hbm_kernel_gbs(T, pairs, {"quantise_permute": 0.42, "reduce_reply": 0.45})
+    qp = T * 2 * 7168 + pairs * (7168 + 7168 // 32)
+    assert r["bytes"]["quantise_permute"] == qp  # 1.20 GB
+    assert r["quantise_permute"] == pytest.approx(qp / 0.42e-3 / 1e9, abs=0.1)
+    assert r["bytes"]["reduce_reply"] == pairs * 2 * 7168 + T * 2 * 7168
+    assert bench.hbm_kernel_gbs(T, pairs, {"quantise_permute": 0.0, "reduce_reply": 0.45})["quantise_permute"] is None
