@@ -303,9 +303,11 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t rows,
  * 128-row token blocks are on average less than half full). */
 int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode);
 
-/* MXFP4 GEMM tiles of this workspace's jobs: 0 one SM per 128 x 256 tile; 1 one tcgen05 MMA over the two SMs of a
- * 2-CTA cluster per 256 x 256 tile (each SM stages half the weight tile, so the load pipeline is deeper).  Same
- * arithmetic either way.  ASAP_EINVAL when no 2-CTA cluster of that kernel fits on the device. */
+/* MXFP4 GEMM tiles of this workspace's jobs: 0 (default) one SM per 128 x 256 tile; 1 one tcgen05 MMA over the two
+ * SMs of a 2-CTA cluster per 256 x 256 tile (each SM stages half the weight tile, 6 pipeline stages instead of 4).
+ * Same arithmetic either way (bit-identical replies).  Measured slower on the DeepSeek-V3-shape layer: the two CTAs'
+ * load rings wait on each other, and experts with an odd number of 128-row blocks pad to a full pair.  ASAP_EINVAL
+ * when no 2-CTA cluster of that kernel fits on the device. */
 int asap_ffn_set_pair_gemm(uint64_t ws_handle, int32_t on);
 
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
