@@ -1,8 +1,8 @@
 // libasap F side: doorbell waits (one message, several joined messages, or the first ready one), the expert-major
 // permutation, activation quantisation (MXFP8, or FP8 per 1x128 for block-FP8 experts), the tcgen05 grouped GEMMs
 // with fused epilogues (MXFP8 x MXFP4 block-scaled here; FP8 x FP8 with block-scale promotion in gemm_fp8.cuh;
-// the weights-as-M variant in gemm_small.cuh), the weighted reduce that writes the replies straight into the A
-// ranks' ResultArenas, and the CUDA-graph capture of whole jobs.
+// the opt-in variants: CTA-pair MMAs in gemm_pair.cuh, weights-as-M in gemm_small.cuh), the weighted reduce that
+// writes the replies straight into the A ranks' ResultArenas, and the CUDA-graph capture of whole jobs.
 //
 // Reference behaviour replaced here (python/sgl_asap_plugin/):
 //   transport/server.py:262-320     FfnServer.poll/_row        -> ffn_wait_kernel (device-side doorbell spin)
