@@ -100,6 +100,18 @@ int asap_arena_close(uint64_t dev_ptr);
 int asap_host_register(uint64_t host_ptr, uint64_t bytes, uint64_t* dev_ptr);
 int asap_host_unregister(uint64_t host_ptr);
 
+/* A shared-memory host page (doorbell page, status words) at `path` (e.g. under /dev/shm): created zeroed (fails
+ * when the file exists) or opened (fails when it is shorter than `bytes`), mapped here and registered for device
+ * access -> its CPU and device addresses.  The owner creates, peers open (memory.py:87-126 does the same in
+ * Python).  Released with asap_release(host_ptr). */
+int asap_host_page_create(const char* path, uint64_t bytes, uint64_t* host_ptr, uint64_t* dev_ptr);
+int asap_host_page_open(const char* path, uint64_t bytes, uint64_t* host_ptr, uint64_t* dev_ptr);
+
+/* Release whatever this library handed out at `ptr`: an asap_arena_alloc arena (freed), an asap_arena_open mapping
+ * (unmapped), or a host page by its CPU address (unregistered, unmapped, and its file removed when this process
+ * created it) -- the Shared.release of memory.py:34-45.  ASAP_EINVAL for any other pointer, or a second release. */
+int asap_release(uint64_t ptr);
+
 /* Fill `count` 32-bit words with `value` on `stream` (replaces cuda_wrapper.py:197-202 memset32). */
 int asap_memset32(uint64_t dev_ptr, uint32_t value, uint64_t count, void* stream);
 

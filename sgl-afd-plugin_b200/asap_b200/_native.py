@@ -67,6 +67,9 @@ _SIGS = {
     "asap_arena_open": (c_int32, [POINTER(c_uint8), POINTER(c_uint64)]),
     "asap_arena_close": (c_int32, [c_uint64]),
     "asap_host_register": (c_int32, [c_uint64, c_uint64, POINTER(c_uint64)]),
+    "asap_host_page_create": (c_int32, [c_char_p, c_uint64, POINTER(c_uint64), POINTER(c_uint64)]),
+    "asap_host_page_open": (c_int32, [c_char_p, c_uint64, POINTER(c_uint64), POINTER(c_uint64)]),
+    "asap_release": (c_int32, [c_uint64]),
     "asap_host_unregister": (c_int32, [c_uint64]),
     "asap_memset32": (c_int32, [c_uint64, c_uint32, c_uint64, c_void_p]),
     "asap_write32": (c_int32, [c_uint64, c_uint32, c_void_p]),

@@ -8,8 +8,16 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <errno.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <mutex>
+#include <string>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -449,6 +457,106 @@ int asap_init(int device) {
   return ASAP_OK;
 }
 
+// What this library handed out, for asap_release: device arenas (asap_arena_alloc), peers' arenas mapped here
+// (asap_arena_open) and host pages (asap_host_page_create / _open, keyed by their CPU address).
+enum OwnedKind { kOwnedArena = 0, kOwnedIpc = 1, kOwnedHostPage = 2 };
+struct OwnedRec {
+  OwnedKind kind;
+  uint64_t bytes;
+  std::string unlink_path;  // host pages this process created: removed on release
+};
+static std::mutex g_owned_mu;
+static std::unordered_map<uint64_t, OwnedRec>& owned() {
+  static std::unordered_map<uint64_t, OwnedRec> m;
+  return m;
+}
+static void own(uint64_t ptr, OwnedKind kind, uint64_t bytes = 0, const char* unlink_path = nullptr) {
+  std::lock_guard<std::mutex> lk(g_owned_mu);
+  owned()[ptr] = OwnedRec{kind, bytes, unlink_path ? unlink_path : ""};
+}
+static void disown(uint64_t ptr) {
+  std::lock_guard<std::mutex> lk(g_owned_mu);
+  owned().erase(ptr);
+}
+
+// Map a shared-memory file of `bytes` (created zeroed, or opened) and register it for device access.  On any
+// failure everything done so far is undone (a file this call created is removed).
+static int host_page_map(const char* what, const char* path, uint64_t bytes, bool create, uint64_t* host_ptr,
+                         uint64_t* dev_ptr) {
+  if (!path || !*path || !bytes || !host_ptr || !dev_ptr) {
+    set_error("%s: need a path, bytes > 0 and non-NULL outputs", what);
+    return ASAP_EINVAL;
+  }
+  const int fd = create ? open(path, O_RDWR | O_CREAT | O_EXCL, 0600) : open(path, O_RDWR);
+  if (fd < 0) {
+    set_error("%s: cannot %s %s: %s", what, create ? "create" : "open", path, strerror(errno));
+    return ASAP_EINVAL;
+  }
+  struct stat st;
+  if ((create && ftruncate(fd, (off_t)bytes) != 0) || fstat(fd, &st) != 0 || (uint64_t)st.st_size < bytes) {
+    set_error("%s: %s is not %llu bytes long", what, path, (unsigned long long)bytes);
+    close(fd);
+    if (create) unlink(path);
+    return ASAP_EINVAL;
+  }
+  void* p = mmap(nullptr, bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  close(fd);
+  if (p == MAP_FAILED) {
+    set_error("%s: mmap of %s failed: %s", what, path, strerror(errno));
+    if (create) unlink(path);
+    return ASAP_EINVAL;
+  }
+  uint64_t d = 0;
+  const int rc = asap_host_register((uint64_t)p, bytes, &d);
+  if (rc != ASAP_OK) {
+    munmap(p, bytes);
+    if (create) unlink(path);
+    return rc;
+  }
+  *host_ptr = (uint64_t)p;
+  *dev_ptr = d;
+  own((uint64_t)p, kOwnedHostPage, bytes, create ? path : nullptr);
+  return ASAP_OK;
+}
+
+int asap_host_page_create(const char* path, uint64_t bytes, uint64_t* host_ptr, uint64_t* dev_ptr) {
+  return host_page_map("asap_host_page_create", path, bytes, true, host_ptr, dev_ptr);
+}
+
+int asap_host_page_open(const char* path, uint64_t bytes, uint64_t* host_ptr, uint64_t* dev_ptr) {
+  return host_page_map("asap_host_page_open", path, bytes, false, host_ptr, dev_ptr);
+}
+
+int asap_release(uint64_t ptr) {
+  OwnedRec rec;
+  {
+    std::lock_guard<std::mutex> lk(g_owned_mu);
+    auto it = owned().find(ptr);
+    if (it == owned().end()) {
+      set_error("asap_release: 0x%llx was not handed out by this library (or is already released)",
+                (unsigned long long)ptr);
+      return ASAP_EINVAL;
+    }
+    rec = it->second;
+    owned().erase(it);
+  }
+  switch (rec.kind) {
+    case kOwnedArena:
+      ASAP_CUDA(cudaFree((void*)ptr));
+      return ASAP_OK;
+    case kOwnedIpc:
+      ASAP_CUDA(cudaIpcCloseMemHandle((void*)ptr));
+      return ASAP_OK;
+    case kOwnedHostPage: {
+      const cudaError_t err = cudaHostUnregister((void*)ptr);
+      munmap((void*)ptr, rec.bytes);
+      if (!rec.unlink_path.empty()) unlink(rec.unlink_path.c_str());
+      return err == cudaSuccess ? ASAP_OK : cuda_fail(err, "cudaHostUnregister");
+    }
+  }
+  return ASAP_EINVAL;
+}
+
 int asap_arena_alloc(uint64_t bytes, uint64_t* dev_ptr, uint8_t ipc_handle[64]) {
   if (!bytes || !dev_ptr) {
     set_error("asap_arena_alloc: bytes must be > 0 and dev_ptr non-NULL");
@@ -466,10 +574,12 @@ int asap_arena_alloc(uint64_t bytes, uint64_t* dev_ptr, uint8_t ipc_handle[64]) 
     memcpy(ipc_handle, &h, 64);
   }
   *dev_ptr = (uint64_t)p;
+  own(*dev_ptr, kOwnedArena);
   return ASAP_OK;
 }
 
 int asap_arena_free(uint64_t dev_ptr) {
+  disown(dev_ptr);
   ASAP_CUDA(cudaFree((void*)dev_ptr));
   return ASAP_OK;
 }
@@ -484,10 +594,12 @@ int asap_arena_open(const uint8_t ipc_handle[64], uint64_t* dev_ptr) {
   void* p = nullptr;
   ASAP_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
   *dev_ptr = (uint64_t)p;
+  own(*dev_ptr, kOwnedIpc);
   return ASAP_OK;
 }
 
 int asap_arena_close(uint64_t dev_ptr) {
+  disown(dev_ptr);
   ASAP_CUDA(cudaIpcCloseMemHandle((void*)dev_ptr));
   return ASAP_OK;
 }

@@ -92,3 +92,30 @@ def test_decode_status(status, expect):
     assert d["what"] == expect
     if status:
         assert (d["f"], d["slot"], d["seq"]) == (3, 1, 77)
+
+
+def test_host_pages_and_release_without_a_gpu(tmp_path):
+    """asap_host_page_create/open and asap_release: every argument and file error is reported before any device
+    call; with no GPU the registration fails and the page this call created is removed again."""
+    lib = N.lib()
+    host, dev = ctypes.c_uint64(), ctypes.c_uint64()
+    assert lib.asap_release(0x1234) == N.ASAP_EINVAL
+    assert "not handed out" in lib.asap_last_error_string().decode()
+    assert lib.asap_host_page_create(None, 4096, ctypes.byref(host), ctypes.byref(dev)) == N.ASAP_EINVAL
+    assert lib.asap_host_page_create(str(tmp_path / "p").encode(), 0, ctypes.byref(host), ctypes.byref(dev)) == \
+        N.ASAP_EINVAL
+    missing = str(tmp_path / "missing").encode()
+    assert lib.asap_host_page_open(missing, 4096, ctypes.byref(host), ctypes.byref(dev)) == N.ASAP_EINVAL
+    assert "cannot open" in lib.asap_last_error_string().decode()
+    short = tmp_path / "short"
+    short.write_bytes(b"\0" * 100)
+    assert lib.asap_host_page_open(str(short).encode(), 4096, ctypes.byref(host), ctypes.byref(dev)) == N.ASAP_EINVAL
+    assert "is not 4096 bytes" in lib.asap_last_error_string().decode()
+    assert lib.asap_host_page_create(str(short).encode(), 4096, ctypes.byref(host), ctypes.byref(dev)) == \
+        N.ASAP_EINVAL  # exists
+    import torch
+
+    if not torch.cuda.is_available():
+        page = tmp_path / "page"
+        rc = lib.asap_host_page_create(str(page).encode(), 4096, ctypes.byref(host), ctypes.byref(dev))
+        assert rc == N.ASAP_ECUDA and not page.exists()

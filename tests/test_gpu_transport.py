@@ -278,3 +278,34 @@ def test_dispatch_sixteen_f_ranks(cuda_ok):
             np.testing.assert_array_equal(reg[: c * H * 2].view(np.uint16).reshape(c, H), mx.bf16_bits(x[sel]))
         word = int(d.bells[f][g.bell_off(0, 0) // 8].item()) & 0xFFFFFFFFFFFFFFFF
         assert word == pack_doorbell(1, c, 2, 1)
+
+
+def test_host_pages_and_release(cuda_ok, tmp_path):
+    """asap_host_page_create / _open / asap_release: a page written on the device is seen by the host and by a
+    second mapping of the same file; release unmaps both and removes the file; arenas and IPC-free pointers go
+    through asap_release too, and a second release is refused."""
+    import os
+    import tempfile
+
+    lib = N.lib()
+    d = tempfile.mkdtemp(dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else None)
+    path = os.path.join(d, "bells").encode()
+    host, dev = ctypes.c_uint64(), ctypes.c_uint64()
+    N.call("asap_host_page_create", path, 4096, ctypes.byref(host), ctypes.byref(dev))
+    host2, dev2 = ctypes.c_uint64(), ctypes.c_uint64()
+    N.call("asap_host_page_open", path, 4096, ctypes.byref(host2), ctypes.byref(dev2))
+    assert host2.value != host.value
+    N.call("asap_write32", dev.value + 64, 0xC0FFEE, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert ctypes.c_uint32.from_address(host.value + 64).value == 0xC0FFEE
+    assert ctypes.c_uint32.from_address(host2.value + 64).value == 0xC0FFEE
+    N.call("asap_release", host2.value)
+    assert os.path.exists(path)       # the opener does not remove the owner's file
+    N.call("asap_release", host.value)
+    assert not os.path.exists(path)   # the creator does
+    assert lib.asap_release(host.value) == N.ASAP_EINVAL
+    arena = ctypes.c_uint64()
+    N.call("asap_arena_alloc", 1 << 20, ctypes.byref(arena), None)
+    N.call("asap_release", arena.value)
+    assert lib.asap_release(arena.value) == N.ASAP_EINVAL
+    os.rmdir(d)
