@@ -24,7 +24,6 @@ w2 [P, H, I], w2_scale [P, H/128, I/128].
 from __future__ import annotations
 
 import ctypes
-from typing import Optional
 
 import numpy as np
 import torch

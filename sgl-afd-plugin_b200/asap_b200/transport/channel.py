@@ -29,7 +29,7 @@ import torch
 
 from .. import _native as N
 from .layout import PROTO_VERSION, SEQ_MASK, ChannelPoisoned, Geometry, HandshakeError
-from .memory import HostWords, Shared
+from .memory import Shared
 from .memory import select as select_memory
 
 MAX_HANDSHAKE_BYTES = 1 << 20
