@@ -27,8 +27,9 @@ from . import mx
 def f_rank_tables(ids: np.ndarray, bounds) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     """Per-F-rank compacted rows.  -> (row_of [F, n] int32 (-1: not routed), count [F], pad [F]).
 
-    Token t goes to F rank f iff one of its ids is in [bounds[f], bounds[f+1]); rows keep token order.  A rank
-    that gets no token is announced one padding row (count 1, pad 1)."""
+    Token t goes to F rank f iff one of its ids is in [bounds[f], bounds[f+1]) (the contiguous expert split of
+    srt/managers/scheduler.py:206-218); rows keep token order.  A rank that gets no token is announced one padding
+    row (count 1, pad 1): a doorbell cannot announce 0 tokens (transport/layout.py:92-102)."""
     ids = np.asarray(ids, dtype=np.int64)
     F = len(bounds) - 1
     n = ids.shape[0]
@@ -45,7 +46,8 @@ def f_rank_tables(ids: np.ndarray, bounds) -> tuple[np.ndarray, np.ndarray, np.n
 
 
 def expert_counts(ids_f: np.ndarray, e0: int, P: int) -> np.ndarray:
-    """Pairs (t, j) per local expert, duplicates counted twice (FusedMoE semantics)."""
+    """Pairs (t, j) per local expert, duplicates counted twice (FusedMoE's per-(token, slot) semantics at
+    srt/managers/scheduler.py:410-412)."""
     e = np.asarray(ids_f, dtype=np.int64).reshape(-1) - e0
     return np.bincount(e[(e >= 0) & (e < P)], minlength=P).astype(np.int32)
 
@@ -129,7 +131,8 @@ def _act_roundtrip(v, act_quant):
 
 
 def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, swiglu_limit=None):
-    """One F rank's reply for one message: bf16 values as fp32 [n_f, H].
+    """One F rank's reply for one message: bf16 values as fp32 [n_f, H] -- the FusedMoE call of
+    srt/managers/scheduler.py:410-412 over the rank's local experts, SwiGLU as srt/models/deepseek_v4.py:51-65.
 
     x_f: bf16 values (fp32 array) [n_f, H]; ids_f/w_f: [n_f, k]; gate/up [P, I, H]; w2 [P, H, I].
     act_quant: True = MXFP8 (E8M0 scale per 32) activations, "fp8" = E4M3 with an fp32 scale per 1 x 128,
@@ -162,7 +165,9 @@ def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, 
 
 
 def combine(parts, row_of, n: int, shared=None):
-    """parts[f]: F rank f's reply rows [n_f, H] (bf16 values); row_of [F, n].  -> bf16 values [n, H]."""
+    """parts[f]: F rank f's reply rows [n_f, H] (bf16 values); row_of [F, n].  -> bf16 values [n, H]: the fp32
+    sum over F ranks in F order cast to bf16 (srt/layers/moe/token_dispatcher/asap.py:174-184), then the
+    shared-expert add (srt/batch_overlap/operations_strategy.py:106-111)."""
     H = parts[0].shape[1]
     acc = np.zeros((n, H), np.float32)
     for f, part in enumerate(parts):
