@@ -309,3 +309,49 @@ def test_host_pages_and_release(cuda_ok, tmp_path):
     N.call("asap_release", arena.value)
     assert lib.asap_release(arena.value) == N.ASAP_EINVAL
     os.rmdir(d)
+
+
+def test_channel_fault_hooks_stale_epoch_and_lost_messages(cuda_ok):
+    """The reference's test hooks AttnChannel(_epoch_override=, _backpressure=False) (channel.py:198-203) provoke
+    the protocol violations the F poll counts (server.py:278-280, 303-305): a doorbell with another epoch is
+    dropped as stale; with backpressure off, a second message on a slot the F rank has not answered overwrites
+    the first, which the F rank counts as lost and serves the newer one."""
+    import os
+    import shutil
+    import tempfile
+
+    from asap_b200.transport.channel import AttnChannel
+    from asap_b200.transport.server import FfnServer
+
+    g = Geometry(1, 1, 2, 64, 256, 2, 1)
+    run_dir = tempfile.mkdtemp(dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else None)
+    x = torch.zeros(8, 256, dtype=torch.bfloat16, device="cuda")
+    ids = torch.tensor([[0, 1]] * 8, dtype=torch.int32, device="cuda")
+    w = torch.full((8, 2), 0.5, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def deployment(**hooks):
+        srv = FfnServer(0, g, device=0, run_dir=run_dir, listen=False).start()
+        ch = AttnChannel(0, g, [("in-process", 0)], device=0, expert_bounds=[0, 8], timeout_s=2.0,
+                         _connector=lambda f, hello: srv.handshake(hello), **hooks).connect()
+        return srv, ch
+
+    srv, ch = deployment(_epoch_override=9)
+    ch.send(3, 0, x.data_ptr(), ids.data_ptr(), w.data_ptr(), 8, stream)
+    torch.cuda.synchronize()
+    assert srv.poll() == [] and srv.stats["stale_epoch"] == 1
+    ch.check()
+    ch.close()
+    srv.close()
+
+    srv, ch = deployment(_backpressure=False)
+    ch.send(3, 0, x.data_ptr(), ids.data_ptr(), w.data_ptr(), 8, stream)
+    ch.send(4, 0, x.data_ptr(), ids.data_ptr(), w.data_ptr(), 5, stream)  # slot 0 again, nothing answered
+    torch.cuda.synchronize()
+    jobs = srv.poll()
+    assert [(j.slot, j.layer_id, j.rows[0].seq, j.rows[0].n_tokens) for j in jobs] == [(0, 4, 2, 5)]
+    assert srv.stats["lost_messages"] == 1
+    ch.check()
+    ch.close()
+    srv.close()
+    shutil.rmtree(run_dir, ignore_errors=True)
