@@ -246,6 +246,14 @@ def gemm_flops(pairs):
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
 
 
+def f_job_launches(rows=1):
+    """Kernels of one F job: the doorbell wait (any / all rows), the routing count + scan + place, the activation
+    quantise + permute, the two GEMMs (MXFP4: also the weights-as-M pair, launched to exit at once unless the job
+    selects it), the weighted reduce + reply, and for a joined job the gather of its rows."""
+    gemms = 4 if KIND == "mxfp4" else 2
+    return 1 + 3 + 1 + gemms + 1 + (1 if rows > 1 else 0)
+
+
 def hbm_kernel_gbs(T, pairs, kernel_ms):
     """Algorithmic GB/s of the two HBM-bound F kernels: quantise+permute reads each token's bf16 row once and
     writes its activation codes + scales into every local pair row; the weighted reduce reads every pair's bf16 row
@@ -477,7 +485,8 @@ def run_single(args):
                    "l2": f"inputs larger than L2 (x {T * H * 2 / 1e6:.0f} MB, weights {experts.nbytes / 1e9:.1f} GB), "
                          "no flush"},
         "e2e": e2e,
-        "gpu_launches": args.steps * 13,  # dispatch 2 + F chain 9 + combine 2 (cuBLAS shared expert not counted)
+        # dispatch 2 (route, pack) + the F job + combine 2 (wait, sum); the cuBLAS shared expert is not counted
+        "gpu_launches": args.steps * (4 + f_job_launches()),
         "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)" if KIND == "mxfp4" else
                      "moe_gemm_fp8_kernel<0> (GEMM1, block-scale promotion + SwiGLU + FP8 requant)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
@@ -694,8 +703,9 @@ def run_sweep(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (fp32 accumulate), bf16 transport",
             "data": "synthetic", "workload_mode": "zipf-sweep",
-            "config": {"workload": f"1 GPU loopback 1A{n_f}F: config 2 layer, T={T}, top-8 "
-                                   f"{'Zipf(s=1.2) popularity over a seeded expert permutation' if args.routing == 'zipf' else 'sigmoid'}",
+            "config": {"workload": f"1 GPU loopback 1A{n_f}F: config 2 layer, T={T}, top-8 " + (
+                           "Zipf(s=1.2) popularity over a seeded expert permutation" if args.routing == "zipf"
+                           else "sigmoid"),
                        "tokens_per_replica": T, "a_replicas": 1, "f_ranks": n_f, "expert_bounds": bounds,
                        "parallelism": f"1A{n_f}F loopback", "routing": args.routing,
                        "f_jobs": "CUDA-graph replays" if args.graphs else "eager launches"},
@@ -704,7 +714,8 @@ def run_sweep(args):
             "f_rows_per_s": round(sum(rows) / statistics.median(busy), 1),
             "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4), "f0_kernels_ms": f0_ms,
             "weights_gb_read_per_step": round(E * (2 * I * H + H * I) * (0.5 + 1 / 32) / 1e9, 3),
-            "e2e": None, "gpu_launches": args.steps * (4 + 9 * n_f), "roofline": None, "cpu_baseline": None,
+            "e2e": None, "gpu_launches": args.steps * (4 + f_job_launches() * n_f), "roofline": None,
+            "cpu_baseline": None,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -722,9 +733,9 @@ def run_stack(args):
     slots 0 and 1 (two-batch overlap): per layer dispatch(mb0), shared(mb0), dispatch(mb1), shared(mb1),
     combine(mb0), combine(mb1) through the public API (AsapDispatcher per layer), so each micro-batch's shared
     expert runs while its routed experts are away and the F ranks always hold the other slot's job.  The output of
-    layer l, RMS-normalised, is the input of layer l+1.  N = 1: loopback (one F rank with all experts of all layers); N > 1: the
-    --topology split (2a4f on 6 GPUs is the benchmark's), F jobs enqueued by a feeder thread.  value = tokens of
-    all A replicas per second through the whole stack."""
+    layer l, RMS-normalised, is the input of layer l+1.  N = 1: loopback (one F rank with all experts of all
+    layers); N > 1: the --topology split (2a4f on 6 GPUs is the benchmark's), F jobs enqueued by a feeder
+    thread.  value = tokens of all A replicas per second through the whole stack."""
     from datetime import timedelta
 
     import torch
@@ -860,7 +871,7 @@ def run_stack(args):
                        "a_replicas": n_a, "f_ranks": n_f, "layers": L, "parallelism": f"{n_a}A{n_f}F",
                        "expert_bounds": bounds},
             "layer_tokens_per_s": round(n_a * T * L / (ms * 1e-3), 1), "output_finite": finite,
-            "e2e": None, "gpu_launches": args.steps * L * 2 * (4 + 9 * n_f) * n_a,
+            "e2e": None, "gpu_launches": args.steps * L * 2 * (4 + f_job_launches() * n_f) * n_a,
             "roofline": None, "cpu_baseline": None, "clocks": clocks_summary,
         }
         print(json.dumps(line), flush=True)
@@ -1086,7 +1097,8 @@ def run_multi(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE[KIND], "data": "synthetic",
             "gpu_launches": args.steps * ((3 + (n_f if args.staged else 1)) * n_a +
-                                          (10 if args.join_replicas else 9 * n_a) * n_f), "roofline": None,
+                                          (f_job_launches(n_a) if args.join_replicas else f_job_launches() * n_a)
+                                          * n_f), "roofline": None,
             "cpu_baseline": None,
             "clocks": clock_summary,
         }
@@ -1106,7 +1118,8 @@ def run_multi(args):
                 "f_jobs": ("one joined job per step (all replicas' messages)" if args.join_replicas else
                            "one job per message" + (", first ready replica first (round robin on the device)"
                                                     if args.any_order else ""))
-                          + (", CUDA-graph replays" if args.graphs else ""), "host_binding": binding, "dispatch": "staged (one F rank at a time)" if args.staged else
+                          + (", CUDA-graph replays" if args.graphs else ""), "host_binding": binding,
+                "dispatch": "staged (one F rank at a time)" if args.staged else
                           "all F ranks at once", "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
@@ -1171,7 +1184,8 @@ def main():
     ap.add_argument("--pair-gemm", action="store_true",
                     help="MXFP4 expert GEMMs on 2-CTA clusters (one MMA over two SMs per 256 x 256 tile)")
     ap.add_argument("--staged", action="store_true",
-                    help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that order")
+                    help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that "
+                         "order")
     ap.add_argument("--graphs", action="store_true",
                     help="F jobs as CUDA-graph replays (FfnScheduler.run_graph; zipf-sweep and N>1)")
     ap.add_argument("--placement", choices=("block", "interleave"), default="interleave",

@@ -101,3 +101,10 @@ def test_hbm_kernel_gbs():
     assert r["quantise_permute"] == pytest.approx(qp / 0.42e-3 / 1e9, abs=0.1)
     assert r["bytes"]["reduce_reply"] == pairs * 2 * 7168 + T * 2 * 7168
     assert bench.hbm_kernel_gbs(T, pairs, {"quantise_permute": 0.0, "reduce_reply": 0.45})["quantise_permute"] is None
+
+
+def test_f_job_launches(monkeypatch):
+    monkeypatch.setattr(bench, "KIND", "mxfp4")
+    assert bench.f_job_launches() == 10 and bench.f_job_launches(4) == 11
+    monkeypatch.setattr(bench, "KIND", "fp8")
+    assert bench.f_job_launches() == 8
