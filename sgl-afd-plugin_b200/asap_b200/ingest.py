@@ -92,6 +92,8 @@ def layer_tensors(collected: Dict[int, Dict[str, Dict[str, torch.Tensor]]], expe
     """One layer's experts (``collect_layer``'s output; every expert of the contiguous ``experts`` range present)
     stacked in checkpoint order on ``device``: ("mxfp4" | "fp8", w13 [P, 2I, .] (gate rows then up rows), w13
     scales, w2, w2 scales)."""
+    if len(experts) == 0:
+        raise ValueError("no experts to load")
     missing = [e for e in experts if e not in collected]
     if missing:
         raise ValueError(f"experts missing from the checkpoint: {missing[:8]}{'...' if len(missing) > 8 else ''}")
@@ -106,14 +108,23 @@ def layer_tensors(collected: Dict[int, Dict[str, Dict[str, torch.Tensor]]], expe
             return t
         return _as_bytes(t)  # E2M1 pairs, E8M0 scales: one byte each, whatever dtype the checkpoint used
 
-    kinds = {part(e, p, "weight").dtype == torch.float8_e4m3fn for e in experts for p in ("gate", "up", "down")}
-    if len(kinds) != 1:
+    parts = {(e, p, k): part(e, p, k) for e in experts for p in ("gate", "up", "down") for k in ("weight", "scale")}
+    if len({parts[e, p, "weight"].dtype == torch.float8_e4m3fn for e in experts for p in ("gate", "up", "down")}) != 1:
         raise ValueError("the layer mixes FP8 and MXFP4 expert weights")
-    w13 = torch.stack([torch.cat([part(e, "gate", "weight"), part(e, "up", "weight")]) for e in experts])
-    s13 = torch.stack([torch.cat([part(e, "gate", "scale"), part(e, "up", "scale")]) for e in experts])
-    w2 = torch.stack([part(e, "down", "weight") for e in experts])
-    s2 = torch.stack([part(e, "down", "scale") for e in experts])
-    if kinds.pop():
+    for p in ("gate", "up", "down"):
+        for k in ("weight", "scale"):
+            shapes = {tuple(parts[e, p, k].shape) for e in experts}
+            if len(shapes) != 1:
+                raise ValueError(f"{p} {k} tensors differ in shape across experts: {sorted(shapes)}")
+    for k in ("weight", "scale"):
+        if parts[experts[0], "gate", k].shape != parts[experts[0], "up", k].shape:
+            raise ValueError(f"gate and up {k} shapes differ: {tuple(parts[experts[0], 'gate', k].shape)} vs "
+                             f"{tuple(parts[experts[0], 'up', k].shape)}")
+    w13 = torch.stack([torch.cat([parts[e, "gate", "weight"], parts[e, "up", "weight"]]) for e in experts])
+    s13 = torch.stack([torch.cat([parts[e, "gate", "scale"], parts[e, "up", "scale"]]) for e in experts])
+    w2 = torch.stack([parts[e, "down", "weight"] for e in experts])
+    s2 = torch.stack([parts[e, "down", "scale"] for e in experts])
+    if w13.dtype == torch.float8_e4m3fn:
         return "fp8", w13, s13.float(), w2, s2.float()
     return "mxfp4", w13, s13, w2, s2
 

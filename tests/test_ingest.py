@@ -141,3 +141,20 @@ def test_ingest_errors():
                             torch.zeros(1, H, 64, dtype=torch.uint8), torch.zeros(1, H, 4, dtype=torch.uint8))
     with pytest.raises(ValueError, match="not a decoder layer"):
         ingest.load_layer([], 61, range(0, 2), num_layers=61, device="cpu")
+
+
+def test_ingest_shape_checks():
+    rng = np.random.default_rng(2)
+    H, I = 256, 128
+    items, _ = _mxfp4_checkpoint(rng, [0, 1], 0, H, I, DSV4, DSV4_PROJ)
+    collected = ingest.collect_layer(items, 0, range(0, 2))
+    with pytest.raises(ValueError, match="no experts"):
+        ingest.layer_tensors(collected, range(0, 0))
+    collected[1]["gate"]["weight"] = collected[1]["gate"]["weight"][:64]
+    with pytest.raises(ValueError, match="differ in shape across experts"):
+        ingest.layer_tensors(collected, range(0, 2))
+    collected = ingest.collect_layer(items, 0, range(0, 2))
+    collected[0]["up"]["weight"] = collected[0]["up"]["weight"][:, :64]
+    collected[1]["up"]["weight"] = collected[1]["up"]["weight"][:, :64]
+    with pytest.raises(ValueError, match="gate and up weight shapes differ"):
+        ingest.layer_tensors(collected, range(0, 2))
