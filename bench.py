@@ -243,15 +243,13 @@ def gemm_flops(pairs):
     return 2.0 * pairs * H * (2 * I), 2.0 * pairs * I * H
 
 
-NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
+NVLINK_NOMINAL_GBS = 900.0  # NVLink 5 per direction per GPU (nominal)
 
 
 def f_job_launches(rows=1):
     """Kernels of one F job: the doorbell wait (any / all rows), the routing count + scan + place, the activation
-    quantise + permute, the two GEMMs (MXFP4: also the weights-as-M pair, launched to exit at once unless the job
-    selects it), the weighted reduce + reply, and for a joined job the gather of its rows."""
-    gemms = 4 if KIND == "mxfp4" else 2
-    return 1 + 3 + 1 + gemms + 1 + (1 if rows > 1 else 0)
+    quantise + permute, the two GEMMs, the weighted reduce + reply, and for a joined job the gather of its rows."""
+    return 1 + 3 + 1 + 2 + 1 + (1 if rows > 1 else 0)
 
 
 def hbm_kernel_gbs(T, pairs, kernel_ms):
@@ -276,18 +274,21 @@ def expert_bytes():
     return 3 * H * I // 2 + 3 * H * I // 32
 
 
-def layer_roofline(n_a, T, f_rows, bounds, ms, peaks, peak_kind):
+def layer_roofline(n_a, T, f_rows, bounds, ms, peaks, peak_kind, nvlink_gbs=None):
     """Per-layer roofline of an nA x nF step: for each F rank, the time its inbound rows take over NVLink
     (x bf16 + ids + weights per routed row), its reply rows outbound, its expert GEMMs at the FP8-rate tensor peak
     (pairs expected under uniform routing: every replica's T·k pairs spread over the experts), and its weight +
-    activation bytes at the HBM peak.  Bound = the largest of those over F ranks; serial = in + flop + out."""
+    activation bytes at the HBM peak.  Bound = the largest of those over F ranks; serial = in + flop + out.
+    ``nvlink_gbs``: the link rate measured in the same run (copy-engine peer write), else the nominal 900 GB/s."""
     fp8_tflops = 2.0 * peaks["bf16_tflops_sustained"]
+    link_src = "copy-engine peer write measured in this run" if nvlink_gbs else "nominal NVLink 5 per direction"
+    nvlink_gbs = nvlink_gbs or NVLINK_NOMINAL_GBS
     per_f = []
     for f, rows in enumerate(f_rows):
         p_f = bounds[f + 1] - bounds[f]
         pairs = n_a * T * K_TOP * p_f / E
-        t_in = rows * (2 * H + 8 * K_TOP) / (NVLINK_GBS * 1e9) * 1e3
-        t_out = rows * 2 * H / (NVLINK_GBS * 1e9) * 1e3
+        t_in = rows * (2 * H + 8 * K_TOP) / (nvlink_gbs * 1e9) * 1e3
+        t_out = rows * 2 * H / (nvlink_gbs * 1e9) * 1e3
         t_flop = pairs * 6.0 * H * I / (fp8_tflops * 1e12) * 1e3
         t_hbm = (p_f * expert_bytes() + rows * (2 * H + 8 * K_TOP) + rows * 2 * H) / (peaks["hbm_gbs"] * 1e9) * 1e3
         per_f.append((t_in, t_out, t_flop, t_hbm))
@@ -299,8 +300,8 @@ def layer_roofline(n_a, T, f_rows, bounds, ms, peaks, peak_kind):
             "t_flop_ms": round(worst[2], 4), "t_hbm_ms": round(worst[3], 4), "t_bound_ms": round(t_bound, 4),
             "t_serial_ms": round(t_serial, 4), "measured_ms": round(ms, 4), "frac": round(t_bound / ms, 4),
             "frac_serial": round(t_serial / ms, 4),
-            "peaks": {"nvlink_gbs": NVLINK_GBS, "fp8_tflops": round(fp8_tflops, 1), "hbm_gbs": peaks["hbm_gbs"],
-                      "source": f"{peak_kind} MEASURED_PEAKS (FP8 = 2 x bf16 sustained); NVLink measured peer copy"},
+            "peaks": {"nvlink_gbs": round(nvlink_gbs, 1), "fp8_tflops": round(fp8_tflops, 1), "hbm_gbs": peaks["hbm_gbs"],
+                      "source": f"{peak_kind} MEASURED_PEAKS (FP8 = 2 x bf16 sustained); NVLink: {link_src}"},
             "pairs": "expected under uniform routing"}
 
 
@@ -385,8 +386,6 @@ def run_single(args):
     experts = make_experts(E, 0, 1, dev)
     lb = Loopback(Geometry(1, 1, 2, T, H, K_TOP, 1), {0: experts}, timeout_s=30.0)
     lb.install()
-    if args.pair_gemm:
-        lb.sched.set_pair_gemm(True)
     shared = SharedExpert(dev) if SHARED else (lambda _x: None)
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
@@ -464,12 +463,24 @@ def run_single(args):
                "path": "AsapDispatcher.dispatch/combine (+ shared expert) per step, H2D of x/ids/w from pinned host "
                        "and D2H of the output overlapped with the previous/next step on copy streams"}
 
+    # parity of the timed configuration: one more step on the same inputs, its buffers against the oracle (the
+    # CPU-baseline leg, which then times the reference's torch semantics on the same tokens and weights)
+    parity, cpu = None, None
+    if not args.no_cpu:
+        d = disp.dispatch(x, topk)
+        s_out = shared(x)
+        out = disp.combine(d, shared=s_out)
+        torch.cuda.synchronize()
+        lb.check()
+        parity, inputs = check_single(x, ids, w, experts, lb.sched, out, s_out, n_experts=args.cpu_experts)
+        cpu = cpu_baseline(args.cpu_experts, inputs=inputs, steps=3)
+
     peaks, peak_kind = load_peaks()
     g1_flops, g2_flops = gemm_flops(pairs)
-    fp8_peak = 2.0 * peaks["bf16_tflops_sustained"]  # kind::f8f6f4 runs at twice the bf16 rate
+    fp8_burst = 2.0 * peaks["bf16_tflops"]  # kind::f8f6f4 runs at twice the bf16 rate
+    fp8_sustained = 2.0 * peaks["bf16_tflops_sustained"]
     achieved = g1_flops / (kernel_ms["gemm1"] * 1e-3) / 1e12
     traffic = load_traffic("gemm1" if KIND == "mxfp4" else "gemm1_fp8", pairs)
-    cpu = cpu_baseline(args.cpu_experts) if not args.no_cpu else None
     clk = clocks.summary()
     nvlink_bytes_dispatch = T * (2 * H + 8 * K_TOP)
     workload = (f"1 GPU loopback A+F: config 2 layer (T={T}, H=7168, {E} experts, top-8 sigmoid, I=2048, MXFP4 "
@@ -489,9 +500,10 @@ def run_single(args):
         "gpu_launches": args.steps * (4 + f_job_launches()),
         "roofline": {"kernel": "moe_gemm_kernel<0> (GEMM1 + SwiGLU + MXFP8 requant)" if KIND == "mxfp4" else
                      "moe_gemm_fp8_kernel<0> (GEMM1, block-scale promotion + SwiGLU + FP8 requant)", "bound": "tensor",
-                     "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / fp8_peak, 4), "traffic": traffic,
-                     "peak_source": f"{peak_kind} bf16_tflops_sustained x 2 (FP8-rate tensor kind)",
+                     "achieved": round(achieved, 1), "peak": round(fp8_burst, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_burst, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} bf16_tflops (burst) x 2 (FP8-rate tensor kind)",
+                     "frac_of_sustained": round(achieved / fp8_sustained, 4),
                      "frac_of_fp4_dense_nominal" if KIND == "mxfp4" else "frac_of_fp8_dense_nominal":
                          round(achieved / (9000.0 if KIND == "mxfp4" else 4500.0), 4)},
         "kernels_ms": {k: round(v, 4) for k, v in kernel_ms.items()},
@@ -499,7 +511,7 @@ def run_single(args):
         "dispatch_ms": round(statistics.median(dsp), 4), "combine_ms": round(statistics.median(cmb), 4),
         "dispatch_gbs_algorithmic": round(nvlink_bytes_dispatch / (statistics.median(dsp) * 1e-3) / 1e9, 1),
         "pairs": pairs, "gemm_tflops_per_step": round((g1_flops + g2_flops) / 1e12, 3),
-        "cpu_baseline": cpu, "clocks": clk,
+        "cpu_baseline": cpu, "parity": parity, "clocks": clk,
     }
     print(json.dumps(line), flush=True)
     lb.close()
@@ -519,55 +531,157 @@ def load_traffic(kernel, pairs):
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline
-def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0):
-    """The oracle (the reference's torch semantics restated in numpy, with the same activation rounding as the
-    GPU path: MXFP8 for config 2, E4M3 per 1x128 for config 4) on the host cores: every (token, slot) pair of the
-    layer that routes to experts [0, n_experts), dequantised weights (dequantisation not timed).  tokens/s counts
-    pairs / top-k."""
+def _cpu_cores():
+    return len(os.sched_getaffinity(0))
+
+
+def _dequant_first(experts, n_experts):
+    """Dequantised (gate, up, w2) fp32 numpy arrays of local experts [0, n_experts) of device-layout experts."""
+    from oracle import moe
+
+    n = n_experts
+    if getattr(experts, "kind", "mxfp4") == "fp8":
+        return moe.dequant_fp8(experts.w13[:n].cpu().numpy(), experts.w13_scale[:n].cpu().numpy(),
+                               experts.w2[:n].cpu().numpy(), experts.w2_scale[:n].cpu().numpy())
+    P, Hh, Ii = experts.num_local, experts.hidden, experts.inter
+    w13 = experts.w13.view(P, -1)[:n].cpu().numpy()
+    sf13 = experts.w13_sf.view(P, -1)[:n].cpu().numpy()
+    w2 = experts.w2.view(P, -1)[:n].cpu().numpy()
+    sf2 = experts.w2_sf.view(P, -1)[:n].cpu().numpy()
+    gate, up = moe.dequant_w13(w13, sf13, n, Hh, Ii)
+    return gate, up, moe.dequant_w2(w2, sf2, n, Hh, Ii)
+
+
+def _time_torch_cpu(x, ids, w, weights, n_experts, act, reps):
+    """Median seconds of the torch CPU restatement (oracle/torch_cpu.py) over ``reps`` runs: every pair of the
+    message that routes to experts [0, n_experts), dequantised weights (dequantisation not timed)."""
+    import torch
+
+    from oracle import torch_cpu as tc
+
+    torch.set_num_threads(_cpu_cores())
+    gate, up, w2 = (torch.from_numpy(a) for a in weights)
+    xt, it, wt = torch.from_numpy(x), torch.from_numpy(ids.astype("int64")), torch.from_numpy(w)
+    times = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        tc.reduce_pairs(*tc.ffn_pairs(xt, it, wt, gate, up, w2, 0, range(n_experts), act_quant=act))
+        times.append(time.perf_counter() - t)
+    return statistics.median(times), torch.get_num_threads()
+
+
+def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0, inputs=None):
+    """The reference's torch semantics on the host cores (oracle/torch_cpu.py, with the GPU path's activation
+    rounding: MXFP8 for config 2, E4M3 per 1x128 for config 4): every (token, slot) pair of the layer that routes
+    to experts [0, n_experts).  ``inputs`` = (x bf16 values, ids, w, (gate, up, w2)) as numpy arrays: the
+    benchmark's own tokens and dequantised weights; without it, seeded random ones of the same shapes.
+    tokens/s counts pairs / top-k."""
     import numpy as np
 
     from oracle import moe, mx
 
-    cores = len(os.sched_getaffinity(0))
     rng = np.random.default_rng(seed)
     T = T_DEFAULT
-    logits = rng.standard_normal((T, E))
-    ids, w = moe.topk_routing(logits, K_TOP, ROUTING)
-    sel = np.any(ids < n_experts, axis=1)
-    x = mx.bf16_round(rng.standard_normal((int(sel.sum()), H)).astype(np.float32))
+    act = "fp8" if KIND == "fp8" else True
     P = n_experts
-    if KIND == "fp8":
-        # E4M3 codes with magnitudes 2^-1 .. 2^3 and random signs, one scale per 128x128 block
-        q13 = (rng.integers(0x30, 0x50, (P, 2 * I, H), dtype=np.uint8) | (rng.integers(0, 2, (P, 2 * I, H),
-                                                                                       dtype=np.uint8) << 7))
-        q2 = rng.integers(0x30, 0x50, (P, H, I), dtype=np.uint8) | (rng.integers(0, 2, (P, H, I), dtype=np.uint8) << 7)
-        s13 = rng.uniform(0.002, 0.01, (P, 2 * I // 128, H // 128)).astype(np.float32)
-        s2 = rng.uniform(0.002, 0.01, (P, H // 128, I // 128)).astype(np.float32)
-        gate, up, w2 = moe.dequant_fp8(q13, s13, q2, s2)
-        act = "fp8"
+    if inputs is None:
+        logits = rng.standard_normal((T, E))
+        ids, w = moe.topk_routing(logits, K_TOP, ROUTING)
+        x = mx.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        if KIND == "fp8":
+            # E4M3 codes with magnitudes 2^-1 .. 2^3 and random signs, one scale per 128x128 block
+            sign = lambda shape: rng.integers(0, 2, shape, dtype=np.uint8) << 7  # noqa: E731
+            q13 = rng.integers(0x30, 0x50, (P, 2 * I, H), dtype=np.uint8) | sign((P, 2 * I, H))
+            q2 = rng.integers(0x30, 0x50, (P, H, I), dtype=np.uint8) | sign((P, H, I))
+            s13 = rng.uniform(0.002, 0.01, (P, 2 * I // 128, H // 128)).astype(np.float32)
+            s2 = rng.uniform(0.002, 0.01, (P, H // 128, I // 128)).astype(np.float32)
+            weights = moe.dequant_fp8(q13, s13, q2, s2)
+        else:
+            codes13 = rng.integers(0, 256, (P, 2 * I, H // 2), dtype=np.uint8)
+            sf13 = rng.integers(117, 121, (P, 2 * I * H // 32), dtype=np.uint8)
+            codes2 = rng.integers(0, 256, (P, H, I // 2), dtype=np.uint8)
+            sf2 = rng.integers(117, 121, (P, H * I // 32), dtype=np.uint8)
+            weights = (*moe.dequant_w13(codes13, sf13, P, H, I), moe.dequant_w2(codes2, sf2, P, H, I))
+        source = "seeded random tokens and weights of the layer's shapes"
     else:
-        codes13 = rng.integers(0, 256, (P, 2 * I, H // 2), dtype=np.uint8)
-        sf13 = rng.integers(117, 121, (P, 2 * I * H // 32), dtype=np.uint8)
-        codes2 = rng.integers(0, 256, (P, H, I // 2), dtype=np.uint8)
-        sf2 = rng.integers(117, 121, (P, H * I // 32), dtype=np.uint8)
-        gate, up = moe.dequant_w13(codes13, sf13, P, H, I)
-        w2 = moe.dequant_w2(codes2, sf2, P, H, I)
-        act = True
+        x, ids, w, weights = inputs
+        source = "the benchmark's own tokens, routing and dequantised expert weights"
+    sel = np.any(ids < n_experts, axis=1)
     pairs = int(np.sum(ids[sel] < n_experts))
-    times = []
-    for i in range(warmup + steps):
-        t = time.perf_counter()
-        moe.ffn_rank(x, ids[sel], w[sel], gate, up, w2, 0, P, act_quant=act)
-        if i >= warmup:
-            times.append(time.perf_counter() - t)
-    dt = statistics.median(times)
+    for _ in range(warmup):
+        _time_torch_cpu(x[sel], ids[sel], w[sel], weights, P, act, 1)
+    dt, threads = _time_torch_cpu(x[sel], ids[sel], w[sel], weights, P, act, max(steps, 1))
     cfg = "config-2" if KIND == "mxfp4" else "config-4"
-    c1 = cpu_config1()
-    return {"value": round(pairs / K_TOP / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+    return {"value": round(pairs / K_TOP / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"all {pairs} (token, expert) pairs of the T={T} {cfg} layer that route to experts "
-                      f"0..{n_experts - 1} (numpy oracle, {'FP8 1x128' if act == 'fp8' else 'MXFP8'} activation "
-                      f"emulation, {cores} host threads); tokens = pairs / top-k; {dt:.2f} s per sample",
-            "config1": c1}
+                      f"0..{n_experts - 1} ({source}; torch CPU fp32, {'FP8 1x128' if act == 'fp8' else 'MXFP8'} "
+                      f"activation emulation, {threads} threads); tokens = pairs / top-k; {dt:.2f} s per sample",
+            "config1": cpu_config1()}
+
+
+def check_single(x, ids, w, experts, sched, out, shared_out, n_experts=4, n_tokens=64, seed=0):
+    """Parity of the timed configuration (the CPU-baseline leg's check; oracle/ is the checker): the last step's
+    device buffers against the oracle on the benchmark's own inputs.
+      * routing: per-local-expert counts and the expert-major position of every (token, slot) pair, bit-exact
+        (all pairs of the step);
+      * experts [0, n_experts): MXFP8 activation codes + scales of their pairs bit-exact (config 2), and the
+        weighted GEMM2 rows within relative L2 1e-2 of the oracle's ffn_pairs;
+      * n_tokens sampled tokens: reply = fp32 sum of their pair rows in slot order and the combined output
+        (+ shared expert) bit-exact from the device's own pair rows.
+    -> (parity dict, inputs for cpu_baseline)."""
+    import numpy as np
+    import torch
+
+    from asap_b200.transport.server import _raw_bytes
+    from oracle import moe, mx
+
+    dev = x.device
+    ids_np, w_np = ids.cpu().numpy(), w.cpu().numpy()
+    T, k = ids_np.shape
+    P = experts.num_local
+    dbg = sched.debug_tensors()
+    counts = dbg["expert_counts"].cpu().numpy()
+    pos = dbg["pair_pos"][:T].cpu().numpy()
+    pos_ref, _, counts_ref = moe.expert_permutation(ids_np, experts.expert_base, P)
+    tables = bool(np.array_equal(counts, counts_ref) and np.array_equal(pos, pos_ref))
+    x_np = x.float().cpu().numpy()
+    weights = _dequant_first(experts, n_experts)
+    sel = np.any(ids_np < n_experts, axis=1)
+    tsel = np.nonzero(sel)[0]
+    y_ref, used = moe.ffn_pairs(x_np[sel], ids_np[sel], w_np[sel], *weights, 0, n_experts,
+                                act_quant="fp8" if KIND == "fp8" else True)
+    tt, jj = np.nonzero(used)
+    prow = torch.from_numpy(pos_ref[tsel[tt], jj].astype(np.int64)).to(dev)
+    rows = int(pos_ref.max()) + 1
+    y2 = _raw_bytes(dbg["y2"], rows * H * 2, dev.index).view(torch.bfloat16).view(rows, H)
+    y_gpu = y2.index_select(0, prow).float().cpu().numpy()
+    rel = moe.rel_l2(y_gpu, y_ref[tt, jj])
+    act_ok = None
+    if KIND == "mxfp4":
+        xq = _raw_bytes(dbg["xq"], rows * H, dev.index).view(rows, H).index_select(0, prow).cpu().numpy()
+        kb = H // 32
+        sfb = _raw_bytes(dbg["xq_sf"], -(-rows // 128) * 128 * kb, dev.index).cpu().numpy()
+        pr = prow.cpu().numpy()[:, None]
+        sf = sfb[mx.sf_atom_offset(pr, np.arange(kb)[None, :], kb)]
+        q_ref, s_ref = mx.mx_quantize(x_np[tsel[tt]])
+        act_ok = bool(np.array_equal(xq, q_ref) and np.array_equal(sf, s_ref))
+    rng = np.random.default_rng(seed)
+    toks = np.sort(rng.choice(T, size=min(n_tokens, T), replace=False))
+    tp = pos_ref[toks]
+    live = tp >= 0
+    gathered = y2.index_select(0, torch.from_numpy(np.where(live, tp, 0).reshape(-1).astype(np.int64)).to(dev))
+    y_tok = gathered.float().cpu().numpy().reshape(len(toks), k, H)
+    reply = moe.reduce_pairs(y_tok, live)
+    shared_rows = shared_out[toks].float().cpu().numpy() if shared_out is not None else None
+    want = moe.combine([reply], np.arange(len(toks))[None, :].astype(np.int32), len(toks), shared_rows)
+    got = out[toks].float().cpu().numpy()
+    combine_ok = bool(np.array_equal(got, want))
+    parity = {"checked": "timed configuration, last step's buffers", "tables_bitexact": tables,
+              "pairs": int(counts_ref.sum()), "experts_checked": n_experts, "pairs_checked": int(len(tt)),
+              "rel_l2": round(rel, 6), "tol": 1e-2, "act_codes_bitexact": act_ok,
+              "tokens_checked": int(len(toks)), "reply_combine_bitexact": combine_ok,
+              "pass": bool(tables and rel < 1e-2 and act_ok is not False and combine_ok)}
+    return parity, (x_np, ids_np, w_np, weights)
 
 
 def cpu_config1(reps=3):
@@ -649,8 +763,6 @@ def run_sweep(args):
     T_max = max(SWEEP_T)
     lb = Loopback(Geometry(1, 1, 2, T_max, H, K_TOP, n_f), per_f, timeout_s=30.0, graphs=args.graphs)
     lb.install()
-    for s in lb.scheds if args.pair_gemm else ():
-        s.set_pair_gemm(True)
     shared = SharedExpert(dev)
     x_all = torch.randn(T_max, H, device=dev, generator=torch.Generator(device=dev).manual_seed(0)).to(torch.bfloat16)
     disp = AsapDispatcher(0)
@@ -760,8 +872,6 @@ def run_stack(args):
         layers = {l: make_experts(E, 0, 1 + l, dev) for l in range(L)}
         lb = Loopback(Geometry(1, 1, 2, Tmb, H, K_TOP, 1), layers, timeout_s=60.0)
         lb.install()
-        if args.pair_gemm:
-            lb.sched.set_pair_gemm(True)
         bounds = [0, E]
     else:
         import torch.distributed as dist
@@ -783,8 +893,6 @@ def run_stack(args):
             server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                                host="127.0.0.1", port=0).start()
             sched = FfnScheduler(server, layers, timeout_s=120.0)
-            if args.pair_gemm:
-                sched.set_pair_gemm(True)
             ep = ("127.0.0.1", server.port)
         eps = [None] * world
         dist.all_gather_object(eps, ep)
@@ -903,6 +1011,134 @@ def expert_bounds(num_f):
     return [(f * E) // num_f for f in range(num_f + 1)]
 
 
+def twin_check(check, bounds, dev, local):
+    """An A replica's parity-step output against a 1-GPU loopback twin: the same experts (regenerated from the F
+    ranks' seeds on this GPU), the same tokens, routing and shared-expert rows, one F scheduler per F rank over the
+    same transport.  The kernels are deterministic, so the combined output and the per-F row counts must match
+    byte for byte; the counts are also checked against the routing itself (tokens with an expert in each F rank's
+    range)."""
+    import torch
+
+    from asap_b200.dispatcher import AsapBuffer, AsapDispatcher
+    from asap_b200.loopback import Loopback
+    from asap_b200.sglang_shim import StandardTopKOutput
+    from asap_b200.transport.layout import Geometry
+
+    x, ids, w, s, out, counts = check
+    T, n_f = x.shape[0], len(bounds) - 1
+    per_f = [{0: make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + f, dev)} for f in range(n_f)]
+    lb = Loopback(Geometry(1, 1, 1, T, H, K_TOP, n_f), per_f, device=local, timeout_s=30.0)
+    prev = AsapBuffer._buffer
+    lb.install()
+    try:
+        disp = AsapDispatcher(0)
+        d = disp.dispatch(x, StandardTopKOutput(w, ids))
+        twin = disp.combine(d, shared=s)
+        torch.cuda.synchronize()
+        lb.check()
+        twin_counts = lb.channel.dispatch_info(d.ticket.slot, torch.cuda.current_stream().cuda_stream)["counts"]
+        ids64 = ids.long()
+        want = [int(((ids64 >= bounds[f]) & (ids64 < bounds[f + 1])).any(dim=1).sum().item()) or 1
+                for f in range(n_f)]  # a rank with no token is announced one padding row
+        res = {"output_bitexact": bool(torch.equal(out.view(torch.int16), twin.view(torch.int16))),
+               "tables_bitexact": list(counts) == list(twin_counts),
+               "counts_match_routing": list(counts) == want}
+    finally:
+        lb.close()
+        AsapBuffer.install(prev)
+        for dct in per_f:
+            dct[0].release()
+    res["pass"] = all(res.values())
+    return res
+
+
+def measure_links(args, is_a, channel, sched, stream, send_stream, x_all, a_idx, n_a, n_f, a_ranks, f_ranks, seqs,
+                  rank, world, dev, T, rounds=5):
+    """NVLink rates of an N-GPU run, measured on the device (CUDA events), max/median over ranks by gather:
+      * dispatch: each A rank's algorithmic bytes (x row + ids + weights per routed row, every F rank) / the
+        dispatch kernels' time, all replicas sending at once (as in a step);
+      * reply: each F rank's reply bytes (one bf16 row per routed row) / its reduce+reply kernel time;
+      * ce_peer_write: a 256 MB copy-engine write from each A rank into F rank (a mod F)'s unused slot-1 region,
+        the link rate the layer roofline divides by.
+    Every rank takes the same collective steps."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from asap_b200 import _native as N
+    from asap_b200.transport.server import _raw_bytes
+
+    res = {}
+    if not is_a:
+        N.call("asap_ffn_enable_timing", sched.ws_handle, 1)
+        for r in range(rounds):
+            for a in range(n_a):
+                sched.run_device_wait(a, 0, seqs[a] + 1 + r, 0, stream.cuda_stream)
+    dist.barrier()
+    if is_a:
+        ids_l, w_l = make_routing(T, 10 + a_idx, dev)
+        xx = x_all[:T]
+        times, nbytes = [], 0
+        for r in range(rounds):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            send_stream.wait_stream(stream)
+            e0.record(send_stream)
+            t = channel.send(0, 0, xx.data_ptr(), ids_l.data_ptr(), w_l.data_ptr(), T, send_stream.cuda_stream)
+            e1.record(send_stream)
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+            channel.combine(t, out.data_ptr(), stream.cuda_stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        counts = channel.dispatch_info(0, stream.cuda_stream)["counts"]
+        nbytes = sum(counts) * (2 * H + 8 * K_TOP)
+        res = {"dispatch_ms": statistics.median(times), "dispatch_bytes": nbytes, "counts": counts}
+    else:
+        torch.cuda.synchronize()
+        kms = (ctypes.c_float * 5)()
+        N.call("asap_ffn_last_timing", sched.ws_handle, kms, 5)
+        N.call("asap_ffn_enable_timing", sched.ws_handle, 0)
+        res = {"reply_ms": float(kms[4])}  # mean over this rank's jobs of the rounds
+    dist.barrier()
+    # copy-engine peer write, each A rank into one F rank's slot-1 region (unused by this benchmark)
+    if is_a:
+        f = a_idx % n_f
+        g = channel.g
+        nb = min(256 << 20, g.region_bytes)
+        dst = _raw_bytes(channel._recv[f] + g.region_off(a_idx, 1), nb, torch.cuda.current_device())
+        src = torch.empty(nb, dtype=torch.uint8, device=dev)
+        dst.copy_(src)
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    if is_a:
+        c0.record()
+        for _ in range(10):
+            dst.copy_(src)
+        c1.record()
+        torch.cuda.synchronize()
+        res["ce_write_gbs"] = 10 * nb / (c0.elapsed_time(c1) * 1e-3) / 1e9
+    dist.barrier()
+    allr = [None] * world
+    dist.all_gather_object(allr, res)
+    a_res = [allr[r] for r in a_ranks]
+    f_res = [allr[r] for r in f_ranks]
+    disp = [ar["dispatch_bytes"] / (ar["dispatch_ms"] * 1e-3) / 1e9 for ar in a_res]
+    # F rank f's mean reply: one bf16 row per row it received, averaged over the replicas' messages
+    rows_f = [statistics.mean(ar["counts"][f] for ar in a_res) for f in range(n_f)]
+    reply = [rows_f[f] * 2 * H / (fr["reply_ms"] * 1e-3) / 1e9 if fr["reply_ms"] > 0 else None
+             for f, fr in enumerate(f_res)]
+    ce = [ar["ce_write_gbs"] for ar in a_res]
+    return {"dispatch_gbs_per_a": [round(v, 1) for v in disp],
+            "dispatch_ms_per_a": [round(ar["dispatch_ms"], 4) for ar in a_res],
+            "reply_gbs_per_f": [round(v, 1) if v else None for v in reply],
+            "ce_peer_write_gbs": [round(v, 1) for v in ce], "ce_peer_write_gbs_median": round(statistics.median(ce), 1),
+            "nominal_gbs_per_direction": NVLINK_NOMINAL_GBS,
+            "note": "dispatch = P2P stores of every replica at once (an F rank's inbound link is shared by all "
+                    "replicas); reply = the F rank's reduce+reply kernel, whose stores cross NVLink into the A rank; "
+                    "CUDA events on the launching streams, median of the rounds"}
+
+
 def run_multi(args):
     """N GPUs, one process each: ranks [0, n_a) are A replicas, the rest F ranks (--topology, default half/half).
     Each F rank's jobs are enqueued by a feeder thread (each job starts with a bounded device wait for its
@@ -945,8 +1181,6 @@ def run_multi(args):
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
         sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s, join=n_a if args.join_replicas else 1)
-        if args.pair_gemm:
-            sched.set_pair_gemm(True)
         ep = ("127.0.0.1", server.port)
     eps = [None] * world
     dist.all_gather_object(eps, ep)
@@ -958,7 +1192,7 @@ def run_multi(args):
     feeder = None
     if not is_a:
         stream = torch.cuda.Stream(dev)
-        queued = phases * steps_per_phase
+        queued = phases * steps_per_phase + 1  # + the parity-check step
 
         def feed():
             torch.cuda.set_device(local)
@@ -1053,6 +1287,18 @@ def run_multi(args):
                     pipe.run(1)
             res["e2e_ms"] = timed(e2e_step if is_a else (lambda: None), pipe.finish if is_a else None)
         results.append(res)
+    # parity step: every replica sends its last message once more; its output is checked against a 1-GPU
+    # loopback twin below (after the F ranks have answered everything)
+    check = None
+    if is_a:
+        send_stream.wait_stream(stream)
+        s_chk = shared(x) if shared is not None else None
+        t_chk = channel.send(0, 0, x.data_ptr(), ids.data_ptr(), w.data_ptr(), T, send_stream.cuda_stream)
+        out_chk = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        channel.combine(t_chk, out_chk.data_ptr(), stream.cuda_stream, s_chk.data_ptr() if s_chk is not None else 0)
+        torch.cuda.synchronize()
+        channel.check()
+        check = (x, ids, w, s_chk, out_chk, channel.dispatch_info(0, stream.cuda_stream)["counts"])
     if feeder is not None:
         feeder.join()
     torch.cuda.synchronize()  # F: every queued job has now been answered
@@ -1060,9 +1306,13 @@ def run_multi(args):
         channel.check()
     else:
         sched.check()
+    parity = twin_check(check, bounds, dev, local) if is_a else None
+    parities = [None] * world
+    dist.all_gather_object(parities, parity)
+    parities = [p for p in parities if p is not None]
     # doorbell latency: one message at a time from A rank 0, F ranks idle and already spinning on their doorbell
     lat = []
-    seq_next = phases * steps_per_phase + 1
+    seq_next = phases * steps_per_phase + 2
     for r in range(lat_iters):
         T = t_list[0]
         if not is_a:
@@ -1085,6 +1335,22 @@ def run_multi(args):
             busy = [(i["t_reply_ns"] - i["t_seen_ns"]) * 1e-3 for i in fi]
             rt = (a0["t_replies_ns"] - a0["t_ring_ns"]) * 1e-3
             lat.append({"round_trip_us": rt, "f_busy_us": busy, "signal_us": rt - max(busy)})
+    if is_a:
+        channel.check()
+    else:
+        sched.check()
+    dist.barrier()
+    # NVLink rates: every replica sends one message at a time (all replicas at once, F ranks idle and already
+    # waiting), CUDA events around each A rank's dispatch and the F ranks' per-stage timing of their replies; then
+    # a copy-engine write of 256 MB from each A rank into one F rank's unused slot-1 region (the link rate the
+    # roofline uses)
+    seq_a = phases * steps_per_phase + 1 + (lat_iters if a_idx == 0 else 0)  # the replica's last message
+    seqs = [None] * world
+    dist.all_gather_object(seqs, seq_a if is_a else None)
+    seqs = [seqs[r] for r in a_ranks]
+    link = measure_links(args, is_a, channel if is_a else None, sched if not is_a else None,
+                         stream, send_stream if is_a else None, x_all if is_a else None, a_idx, n_a, n_f, a_ranks,
+                         f_ranks, seqs, rank, world, dev, T)
     if is_a:
         channel.check()
     else:
@@ -1125,7 +1391,17 @@ def run_multi(args):
             line["f_rows"] = res["f_rows"]
             line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
             if args.routing != "zipf":
-                line["layer_roofline"] = layer_roofline(n_a, T, res["f_rows"], bounds, ms, *load_peaks())
+                line["layer_roofline"] = layer_roofline(n_a, T, res["f_rows"], bounds, ms, *load_peaks(),
+                                                        nvlink_gbs=link["ce_peer_write_gbs_median"])
+            line["parity"] = {"mode": "each A replica's parity-step output and per-F row counts against a 1-GPU "
+                                      "loopback twin (same experts, same tokens), byte for byte, and the row counts "
+                                      "against the routing", "tokens_per_replica": t_list[-1],
+                              "replicas": len(parities),
+                              "output_bitexact": all(p["output_bitexact"] for p in parities),
+                              "tables_bitexact": all(p["tables_bitexact"] for p in parities),
+                              "counts_match_routing": all(p["counts_match_routing"] for p in parities),
+                              "pass": all(p["pass"] for p in parities)}
+            line["nvlink"] = link
             if "e2e_ms" in res:
                 e = res["e2e_ms"]
                 line["e2e"] = {"value": round(n_a * T / (e * 1e-3), 1), "unit": "tokens/s",
@@ -1181,8 +1457,6 @@ def main():
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
-    ap.add_argument("--pair-gemm", action="store_true",
-                    help="MXFP4 expert GEMMs on 2-CTA clusters (one MMA over two SMs per 256 x 256 tile)")
     ap.add_argument("--staged", action="store_true",
                     help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that "
                          "order")

@@ -182,7 +182,10 @@ int asap_dispatch_staged(const asap_geometry_t* g, int32_t a, int32_t slot, uint
  * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.  It calls no
  * cudaMalloc/cudaFree.  Every call shares the array: a slot's table keeps the last call's contents until the next
  * dispatch on that slot overwrites it, so dispatches on one slot that overlap on the GPU (or a dispatch that
- * overlaps the combine still reading the slot's table) race.  Otherwise identical to asap_dispatch. */
+ * overlaps the combine still reading the slot's table) race.  The 8 tables are shared by every caller on the
+ * device: every A replica and geometry of the process that dispatches through this entry point on that GPU.  The
+ * looked-up address is cached per device ordinal for the life of the process: do not use this entry point across a
+ * cudaDeviceReset (or any reset of the device's primary context).  Otherwise identical to asap_dispatch. */
 int asap_dispatch_noalloc(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
                           const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
                           int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
@@ -314,13 +317,6 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t rows,
  * than the default on this build, so opt-in); -1 chooses per job on the device (weights-as-M when the experts'
  * 128-row token blocks are on average less than half full). */
 int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode);
-
-/* MXFP4 GEMM tiles of this workspace's jobs: 0 (default) one SM per 128 x 256 tile; 1 one tcgen05 MMA over the two
- * SMs of a 2-CTA cluster per 256 x 256 tile (each SM stages half the weight tile, 6 pipeline stages instead of 4).
- * Same arithmetic either way (bit-identical replies).  Measured slower on the DeepSeek-V3-shape layer: the two CTAs'
- * load rings wait on each other, and experts with an odd number of 128-row blocks pad to a full pair.  ASAP_EINVAL
- * when no 2-CTA cluster of that kernel fits on the device. */
-int asap_ffn_set_pair_gemm(uint64_t ws_handle, int32_t on);
 
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
  * stream around its 5 stages (routing, quantise+permute, gemm1, gemm2, reduce+reply); last_timing waits

@@ -130,13 +130,16 @@ def _act_roundtrip(v, act_quant):
     return mx.mx_roundtrip(v) if act_quant else v
 
 
-def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, swiglu_limit=None):
-    """One F rank's reply for one message: bf16 values as fp32 [n_f, H] -- the FusedMoE call of
-    srt/managers/scheduler.py:410-412 over the rank's local experts, SwiGLU as srt/models/deepseek_v4.py:51-65.
+def ffn_pairs(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, swiglu_limit=None, experts=None):
+    """The weighted expert output of every local (token, slot) pair of one message, before the per-token sum:
+    -> (y2 [n, k, H] bf16 values as fp32, used [n, k] bool).  One pair = one term of the FusedMoE call of
+    srt/managers/scheduler.py:410-412, w[t,j] * W2_e (silu(W1_e x_t) * W3_e x_t) with SwiGLU as
+    srt/models/deepseek_v4.py:51-65, rounded to bf16 as the CUDA path stores it.
 
-    x_f: bf16 values (fp32 array) [n_f, H]; ids_f/w_f: [n_f, k]; gate/up [P, I, H]; w2 [P, H, I].
-    act_quant: True = MXFP8 (E8M0 scale per 32) activations, "fp8" = E4M3 with an fp32 scale per 1 x 128,
-    False = none."""
+    x_f: bf16 values (fp32 array) [n_f, H]; ids_f/w_f: [n_f, k]; gate/up [P, I, H]; w2 [P, H, I] (or, with
+    ``experts`` = an iterable of local expert indices, only those experts are evaluated and gate/up/w2 are
+    indexed by position in that iterable).  act_quant: True = MXFP8 (E8M0 scale per 32) activations, "fp8" = E4M3
+    with an fp32 scale per 1 x 128, False = none."""
     x_f = np.asarray(x_f, np.float32)
     ids_f = np.asarray(ids_f, np.int64)
     w_f = np.asarray(w_f, np.float32)
@@ -144,24 +147,40 @@ def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, 
     H = x_f.shape[1]
     y2 = np.zeros((n, k, H), np.float32)
     used = np.zeros((n, k), bool)
-    for e in range(P):
+    which = range(P) if experts is None else experts
+    for slot, e in enumerate(which):
         tt, jj = np.nonzero(ids_f == e0 + e)
         if tt.size == 0:
             continue
+        wi = e if experts is None else slot
         xa = _act_roundtrip(x_f[tt], act_quant)
-        g = xa @ gate[e].T
-        u = xa @ up[e].T
+        g = xa @ gate[wi].T
+        u = xa @ up[wi].T
         if swiglu_limit:
             g = np.minimum(g, swiglu_limit)
             u = np.clip(u, -swiglu_limit, swiglu_limit)
         h = _act_roundtrip((silu(g) * u).astype(np.float32), act_quant)
-        y = h @ w2[e].T
+        y = h @ w2[wi].T
         y2[tt, jj] = mx.bf16_round(y * w_f[tt, jj][:, None])
         used[tt, jj] = True
-    out = np.zeros((n, H), np.float32)
-    for j in range(k):  # ascending slot order, fp32
-        out += np.where(used[:, j, None], y2[:, j], 0.0)
+    return y2, used
+
+
+def reduce_pairs(y2, used):
+    """Per-token reply row from its pairs' rows: fp32 sum in ascending slot order, rounded to bf16 (the F
+    rank's partial sum that server.py:340-350 sends back; the order is the CUDA reduce's)."""
+    y2 = np.asarray(y2, np.float32)
+    out = np.zeros((y2.shape[0], y2.shape[2]), np.float32)
+    for j in range(y2.shape[1]):
+        out += np.where(np.asarray(used)[:, j, None], y2[:, j], 0.0)
     return mx.bf16_round(out)
+
+
+def ffn_rank(x_f, ids_f, w_f, gate, up, w2, e0: int, P: int, *, act_quant=True, swiglu_limit=None):
+    """One F rank's reply for one message: bf16 values as fp32 [n_f, H] -- the FusedMoE call of
+    srt/managers/scheduler.py:410-412 over the rank's local experts (``ffn_pairs`` then ``reduce_pairs``)."""
+    return reduce_pairs(*ffn_pairs(x_f, ids_f, w_f, gate, up, w2, e0, P, act_quant=act_quant,
+                                   swiglu_limit=swiglu_limit))
 
 
 def combine(parts, row_of, n: int, shared=None):

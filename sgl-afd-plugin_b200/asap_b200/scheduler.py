@@ -111,7 +111,6 @@ class FfnScheduler:
         N.call("asap_ffn_ws_register", self.ws.data_ptr(), cap, g.topk, first.num_local, first.hidden,
                first.inter, ctypes.byref(h))
         self.ws_handle = h.value
-        self.pair_gemm = False
         self.status = HostWords(1)
         # CUDA-graph mode: per (A rank, slot) the last consumed seq lives on the device (asap_ffn_wait_state), so a
         # chain captured once replays for every message; _dev_seq mirrors what those words will hold
@@ -346,13 +345,6 @@ class FfnScheduler:
         topk_ids = arena[ids_off: ids_off + n * g.topk * 4].view(torch.int32).view(n, g.topk)
         topk_weights = arena[w_off: w_off + n * g.topk * 4].view(torch.float32).view(n, g.topk)
         return x, topk_ids, topk_weights
-
-    def set_pair_gemm(self, on: bool) -> None:
-        """Run this scheduler's MXFP4 expert GEMMs as one MMA over the two SMs of a 2-CTA cluster per 256 x 256
-        tile (same arithmetic as the one-SM tiles; asap_ffn_set_pair_gemm).  Chains captured in CUDA graphs
-        before the switch keep the kernels they were captured with."""
-        N.call("asap_ffn_set_pair_gemm", self.ws_handle, int(bool(on)))
-        self.pair_gemm = bool(on)
 
     def debug_tensors(self) -> dict:
         """Device buffers of the last job (tests): per-local-expert counts and the pair permutation."""

@@ -29,8 +29,8 @@ def nvcc_path() -> str:
 
 def build(debug: bool = False, verbose: bool = False) -> str:
     srcs = [os.path.join(CSRC, s) for s in SOURCES]
-    deps = srcs + [os.path.join(CSRC, "common.cuh"), os.path.join(CSRC, "gemm_fp8.cuh"), os.path.join(CSRC, "gemm_small.cuh"),
-            os.path.join(CSRC, "gemm_pair.cuh"), os.path.join(HERE, "..", "include", "asap.h")]
+    deps = srcs + [os.path.join(CSRC, n) for n in os.listdir(CSRC) if n.endswith(".cuh")]
+    deps.append(os.path.join(HERE, "..", "include", "asap.h"))
     if os.path.exists(OUT) and not debug:
         newest = max(os.path.getmtime(p) for p in deps)
         if os.path.getmtime(OUT) >= newest:

@@ -1,7 +1,7 @@
 // libasap F side: doorbell waits (one message, several joined messages, or the first ready one), the expert-major
 // permutation, activation quantisation (MXFP8, or FP8 per 1x128 for block-FP8 experts), the tcgen05 grouped GEMMs
 // with fused epilogues (MXFP8 x MXFP4 block-scaled here; FP8 x FP8 with block-scale promotion in gemm_fp8.cuh;
-// the opt-in variants: CTA-pair MMAs in gemm_pair.cuh, weights-as-M in gemm_small.cuh), the weighted reduce that
+// the opt-in weights-as-M variant in gemm_small.cuh), the weighted reduce that
 // writes the replies straight into the A ranks' ResultArenas, and the CUDA-graph capture of whole jobs.
 //
 // Reference behaviour replaced here (python/sgl_asap_plugin/):
@@ -559,10 +559,7 @@ __device__ __forceinline__ uint64_t sdesc_sf(const void* p) {
 
 struct Params {
   CUtensorMap tmap_a;  // activations [m_cap, K] bytes (E4M3)
-  CUtensorMap tmap_b;  // weights [P * N, K] E2M1 (4-bit, unpacked to 16 B per 16 values in smem); the pair kernel:
-                       // 128-row boxes
-  CUtensorMap tmap_sfa;  // pair kernel only: activation scale atoms as [m_cap/128 * K/128] rows of 128 u32
-  CUtensorMap tmap_sfb;  // pair kernel only: weight scale atoms as [P * K/128] rows of N u32
+  CUtensorMap tmap_b;  // weights [P * N, K] E2M1 (4-bit, unpacked to 16 B per 16 values in smem)
   const uint8_t* sfa;  // activation scale atoms [m_cap/128][K/128][512]
   const uint8_t* sfb;  // weight scale atoms per expert [K/128][N/128][512]
   uint64_t sfb_expert_stride;
@@ -855,7 +852,6 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
 }  // namespace gemm
 
 #include "gemm_fp8.cuh"
-#include "gemm_pair.cuh"
 #include "gemm_small.cuh"
 
 // ------------------------------------------------------------------ K5b: weighted reduce + reply
@@ -994,8 +990,7 @@ struct ExpertsHandle {
   asap_mxfp4_experts_t e;   // kMxfp4 (num_local/expert_base/hidden/inter filled for both kinds)
   asap_fp8_experts_t f8;    // kFp8Block
   CUtensorMap w13_map, w2_map;
-  CUtensorMap w13_map_t, w2_map_t;  // kMxfp4: 128-row boxes (weights-as-M kernels, CTA-pair kernels)
-  CUtensorMap w13_sf_map, w2_sf_map;  // kMxfp4: scale atoms as rows of u32 (CTA-pair kernels)
+  CUtensorMap w13_map_t, w2_map_t;  // kMxfp4: 128-row boxes (weights-as-M kernels)
 };
 constexpr int kTimedKernels = 5;  // routing (count+scan+place), quantise+permute, gemm1, gemm2, finalize_reply
 constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
@@ -1003,10 +998,8 @@ struct WsHandle {
   uint8_t* base;
   WsLayout L;
   CUtensorMap xq_map, hq_map;
-  CUtensorMap xq_sf_map, hq_sf_map;  // activation scale atoms as rows of 128 u32 (CTA-pair kernels)
   bool timing = false;
   int small_mode = 0;  // PermArgs::small_mode (the weights-as-M kernels measured slower: opt-in)
-  int pair_gemm = 0;   // 1: the MXFP4 GEMMs run on CTA pairs (moe_gemm_pair_kernel)
   int jobs = 0;  // jobs recorded since enable
   cudaEvent_t ev[kTimedJobs][kTimedKernels + 1] = {};
 };
@@ -1028,7 +1021,6 @@ static WsHandle* get_ws(uint64_t h) {
 }
 
 static bool gemm_attr_set = false;
-static int g_pair_clusters = 0;  // CTA pairs of moe_gemm_pair_kernel resident at once (0: pairs unavailable)
 
 static int ensure_gemm_attrs() {
   if (gemm_attr_set) return ASAP_OK;
@@ -1044,47 +1036,8 @@ static int ensure_gemm_attrs() {
                                  gemmT::SMEM_BYTES));
   ASAP_CUDA(cudaFuncSetAttribute(gemmT::moe_gemm_t_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  gemmT::SMEM_BYTES));
-  ASAP_CUDA(cudaFuncSetAttribute(gemmP::moe_gemm_pair_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 gemmP::SMEM_BYTES));
-  ASAP_CUDA(cudaFuncSetAttribute(gemmP::moe_gemm_pair_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 gemmP::SMEM_BYTES));
-  {  // CTA pairs resident at once: the persistent pair grid is sized to it
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * (sm_count() / 2));
-    cfg.blockDim = dim3(gemmP::THREADS);
-    cfg.dynamicSmemBytes = gemmP::SMEM_BYTES;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n0 = 0, n1 = 0;
-    ASAP_CUDA(cudaOccupancyMaxActiveClusters(&n0, gemmP::moe_gemm_pair_kernel<0>, &cfg));
-    ASAP_CUDA(cudaOccupancyMaxActiveClusters(&n1, gemmP::moe_gemm_pair_kernel<1>, &cfg));
-    g_pair_clusters = std::min(std::min(n0, n1), sm_count() / 2);
-  }
   gemm_attr_set = true;
   return ASAP_OK;
-}
-
-// The CTA-pair GEMM: clusters of 2 along x, one persistent pair per resident cluster slot.
-template <int EPI>
-static cudaError_t launch_pair(const gemm::Params& p, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(2 * g_pair_clusters);
-  cfg.blockDim = dim3(gemmP::THREADS);
-  cfg.dynamicSmemBytes = gemmP::SMEM_BYTES;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemmP::moe_gemm_pair_kernel<EPI>, p);
 }
 
 // K5b launch shared by both weight kinds; `mark` records the job's last timing event.
@@ -1145,13 +1098,6 @@ int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
   if (!rc)
     rc = make_tmap_2d(&h->w2_map_t, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2,
                       gemmT::BK, gemmT::BW, "w2 (128-row boxes)");
-  // scale atoms [P][K/128][N/128][512 B] as rows of N u32: one box = the two atoms of a 256-row N tile
-  if (!rc)
-    rc = make_tmap_2d(&h->w13_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, (const void*)e->w13_sf, 2 * I, P * (H / 128),
-                      8 * I, gemmP::SFB_BYTES / 4, 1, "w13 scales", CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (!rc)
-    rc = make_tmap_2d(&h->w2_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, (const void*)e->w2_sf, H, P * (I / 128), 4 * H,
-                      gemmP::SFB_BYTES / 4, 1, "w2 scales", CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) {
     delete h;
     return rc;
@@ -1241,15 +1187,6 @@ int asap_ffn_ws_register(uint64_t ws, int32_t n_max, int32_t topk, int32_t num_l
   if (!rc)
     rc = make_tmap_2d(&h->hq_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, h->base + h->L.hq, inter, h->L.m_cap, inter,
                       gemm::BK, gemm::BM, "hq");
-  // activation scale atoms [m_cap/128][K/128][512 B] as rows of 128 u32: one box = one atom
-  if (!rc)
-    rc = make_tmap_2d(&h->xq_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, h->base + h->L.xq_sf, 128,
-                      (uint64_t)(h->L.m_cap / 128) * (hidden / 128), 512, 128, 1, "xq scales",
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (!rc)
-    rc = make_tmap_2d(&h->hq_sf_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, h->base + h->L.hq_sf, 128,
-                      (uint64_t)(h->L.m_cap / 128) * (inter / 128), 512, 128, 1, "hq scales",
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) {
     delete h;
     return rc;
@@ -1607,13 +1544,10 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g1.swiglu_limit = swiglu_limit;
   g1.status = status;
   g1.timeout_ns = timeout_ns;
-  const bool pairs = wh->pair_gemm != 0 && g_pair_clusters > 0;
-  if (pairs) {
-    g1.tmap_b = eh->w13_map_t;
-    g1.tmap_sfa = wh->xq_sf_map;
-    g1.tmap_sfb = eh->w13_sf_map;
-    ASAP_CUDA(launch_pair<0>(g1, st));
-  } else {
+  // Which GEMM pair runs is decided per job on the device (JobDesc::small) only in mode -1; in modes 0 / 1 the
+  // host launches just the token-major / weights-as-M kernels, so no launch exits without work.
+  const bool token_major = wh->small_mode != 1, weights_as_m = wh->small_mode != 0;
+  if (token_major) {
     gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
     ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
   }
@@ -1637,15 +1571,15 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   t1.swiglu_limit = swiglu_limit;
   t1.status = status;
   t1.timeout_ns = timeout_ns;
-  gemmT::moe_gemm_t_kernel<0><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t1);
-  ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<0>");
+  if (weights_as_m) {
+    gemmT::moe_gemm_t_kernel<0><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t1);
+    ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<0>");
+  }
   mark(3);
 
   gemm::Params g2 = g1;
   g2.tmap_a = wh->hq_map;
-  g2.tmap_b = pairs ? eh->w2_map_t : eh->w2_map;
-  g2.tmap_sfa = wh->hq_sf_map;
-  g2.tmap_sfb = eh->w2_sf_map;
+  g2.tmap_b = eh->w2_map;
   g2.sfa = B + L.hq_sf;
   g2.sfb = (const uint8_t*)E.w2_sf;
   g2.sfb_expert_stride = (uint64_t)(L.I / 32) * L.H;
@@ -1654,9 +1588,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.out_bf = (__nv_bfloat16*)(B + L.y2);
   g2.N = L.H;
   g2.K = L.I;
-  if (pairs) {
-    ASAP_CUDA(launch_pair<1>(g2, st));
-  } else {
+  if (token_major) {
     gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
     ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
   }
@@ -1671,25 +1603,13 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   t2.out_bf = g2.out_bf;
   t2.N = L.H;
   t2.K = L.I;
-  gemmT::moe_gemm_t_kernel<1><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t2);
-  ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<1>");
+  if (weights_as_m) {
+    gemmT::moe_gemm_t_kernel<1><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t2);
+    ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<1>");
+  }
   mark(4);
 
   return finalize(desc, L, pa, B, R, rows, st, sms, mark);
-}
-
-int asap_ffn_set_pair_gemm(uint64_t ws_handle, int32_t on) {
-  WsHandle* w = get_ws(ws_handle);
-  if (!w || (on != 0 && on != 1)) {
-    set_error("asap_ffn_set_pair_gemm: unknown workspace handle or value %d outside {0, 1}", on);
-    return ASAP_EINVAL;
-  }
-  if (on && g_pair_clusters < 1) {
-    set_error("asap_ffn_set_pair_gemm: no 2-CTA cluster of the pair GEMM fits on this device");
-    return ASAP_EINVAL;
-  }
-  w->pair_gemm = on;
-  return ASAP_OK;
 }
 
 int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode) {

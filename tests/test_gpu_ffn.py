@@ -223,32 +223,6 @@ def test_ffn_chain_duplicate_ids_and_limits(cuda_ok):
     e.release()
 
 
-@pytest.mark.parametrize("n,k,P,H,I,e0", [
-    (64, 2, 4, 256, 128, 4),        # one block per expert: the follower half of every pair tile is empty
-    (300, 4, 6, 512, 256, 0),       # two and three blocks per expert, two n-tiles in both GEMMs
-    (1000, 4, 8, 2048, 512, 0),     # 16 K steps, more pair tiles than CTA pairs (TMEM reuse across tiles)
-    (64, 12, 16, 256, 128, 0),      # more than 8 local experts per token
-])
-def test_ffn_chain_pair_gemm(cuda_ok, n, k, P, H, I, e0):
-    """The GEMMs on CTA pairs (one tcgen05 MMA over two SMs): the oracle checks of every stage, and replies
-    bit-identical to the one-SM kernels'."""
-    rng = np.random.default_rng(n + 500)
-    e = Mxfp4Experts.random(P, H, I, expert_base=e0, seed=n + 9)
-    gate, up, w2 = experts_to_oracle(e)
-    x, ids, w = random_inputs(rng, n, H, k, e0 - 2, e0 + P + 2, bias_expert=e0)
-    outs = []
-    for pair in (1, 0):
-        h = FfnHarness(e, n_max=n, topk=k, pair_gemm=pair)
-        h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), seq=29)
-        if pair:
-            check_chain(h, x, ids, w, gate, up, w2, e0, P)
-        assert int(h.done[0].item()) == 29
-        outs.append(np_from_bf16(h.reply[:n]))
-        h.release()
-    np.testing.assert_array_equal(outs[0], outs[1])
-    e.release()
-
-
 def test_ffn_chain_from_checkpoint(cuda_ok, tmp_path):
     """F-rank weight ingest end to end: a safetensors shard with two ranks' experts over two layers (DeepSeek-V4
     names, int8 codes and float8_e8m0fnu scales mixed in); `ingest.load_layer` reads this rank's experts of one

@@ -101,6 +101,46 @@ def test_noalloc_dispatch_matches_dispatch(cuda_ok):
         assert torch.equal(out_ref, out_noa)
 
 
+def test_noalloc_dispatch_last_slot_at_the_maximum(cuda_ok):
+    """Slot 7 (the last static table) with num_f * n_max = 131072 (the maximum): the full table equals
+    asap_dispatch's, its address is the 8th slot's, and the neighbouring slot 6 is left untouched."""
+    g = Geometry(1, 1, 8, 32768, 512, 4, 4)
+    assert g.num_f * g.n_max == 1 << 17
+    bounds, epochs, slot, n = [0, 6, 12, 18, 24], [1, 1, 1, 1], 7, 32768
+    ref, noa = Arenas(g), Arenas(g)
+    ws_bytes = N.lib().asap_route_ws_bytes(ctypes.byref(N.geometry_struct(g)))
+    route_ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rng = np.random.default_rng(7)
+    x = torch.from_numpy(rng.standard_normal((n, 512)).astype(np.float32)).cuda().to(torch.bfloat16)
+    ids = torch.from_numpy(np.stack([rng.permutation(24)[:4] for _ in range(n)]).astype(np.int32)).cuda()
+    w = torch.from_numpy(rng.random((n, 4)).astype(np.float32)).cuda()
+    # one small call on slot 6 gives its table's address; snapshot that table
+    small = Geometry(1, 1, 8, 8, 512, 4, 4)
+    ar0 = Arenas(small)
+    slot6_addr = ctypes.c_uint64()
+    N.call("asap_dispatch_noalloc", *_args(small, ar0, 6, 1, x[:8], ids[:8], w[:8], bounds, epochs), 1,
+           ar0.status.data_ptr(), int(2e9), stream, ctypes.byref(slot6_addr))
+    torch.cuda.synchronize()
+    slot_bytes = N.lib().asap_route_ws_bytes(ctypes.byref(N.geometry_struct(g)))  # 512 + 4 * 131072
+    slot6 = torch.as_tensor(_DevBytes(slot6_addr.value, slot_bytes), device="cuda").clone()
+    N.call("asap_dispatch", *_args(g, ref, slot, 1, x, ids, w, bounds, epochs), route_ws.data_ptr(), 1,
+           ref.status.data_ptr(), int(2e9), stream)
+    got = ctypes.c_uint64()
+    N.call("asap_dispatch_noalloc", *_args(g, noa, slot, 1, x, ids, w, bounds, epochs), 1, noa.status.data_ptr(),
+           int(2e9), stream, ctypes.byref(got))
+    torch.cuda.synchronize()
+    assert int(ref.status.item()) == 0 and int(noa.status.item()) == 0
+    assert got.value == slot6_addr.value + slot_bytes  # slot 7 follows slot 6
+    table = torch.as_tensor(_DevBytes(got.value, slot_bytes), device="cuda").clone()
+    rows = slice(512, slot_bytes)
+    assert torch.equal(route_ws[rows], table[rows])  # every row of the table, the last F rank's included
+    assert torch.equal(route_ws[:256].view(torch.int32)[: g.num_f], table[:256].view(torch.int32)[: g.num_f])
+    assert torch.equal(torch.as_tensor(_DevBytes(slot6_addr.value, slot_bytes), device="cuda"), slot6)
+    for f in range(g.num_f):
+        assert torch.equal(ref.recv[f], noa.recv[f]) and torch.equal(ref.bells[f], noa.bells[f])
+
+
 def test_noalloc_dispatch_rejects_sizes_beyond_its_maximum(cuda_ok):
     out = ctypes.c_uint64()
     x = torch.zeros(4, 512, dtype=torch.bfloat16, device="cuda")
