@@ -1105,7 +1105,7 @@ def measure_links(args, is_a, channel, sched, stream, send_stream, x_all, a_idx,
         f = a_idx % n_f
         g = channel.g
         nb = min(256 << 20, g.region_bytes)
-        dst = _raw_bytes(channel._recv[f] + g.region_off(a_idx, 1), nb, torch.cuda.current_device())
+        dst = _raw_bytes(channel.recv_bases[f] + g.region_off(a_idx, 1), nb, torch.cuda.current_device())
         src = torch.empty(nb, dtype=torch.uint8, device=dev)
         dst.copy_(src)
         torch.cuda.synchronize()

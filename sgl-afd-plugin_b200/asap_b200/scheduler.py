@@ -248,8 +248,7 @@ class FfnScheduler:
             rows.append(row)
             targets.append(target)
             if (a, slot) not in self._dev_owned:  # the device word takes over from the host's bookkeeping
-                with server._lock:
-                    last = server._last[a * self.g.slots + slot]
+                last = server.last_seq(a, slot)
                 N.call("asap_write32", self._state_ptr(a, slot), last & SEQ_MASK, ctypes.c_void_p(stream))
                 self._dev_owned.add((a, slot))
                 self._dev_seq[(a, slot)] = None

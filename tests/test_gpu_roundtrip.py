@@ -67,12 +67,12 @@ def test_config1_round_trip(pair):
     assert moe.rel_l2(got, plain) < 8e-2
     # wire bytes of the message: region rows, doorbell word, routing table
     g = lb.g
-    seq = lb.channel._seq[0]
+    seq = lb.channel._last_sent[0]
     reg = torch.as_tensor(lb.sched.recv_arena[g.region_off(0, 0): g.region_off(0, 1)]).cpu().numpy()
     np.testing.assert_array_equal(reg[: T * 1024 * 2].view(np.uint16).reshape(T, 1024), mx.bf16_bits(x))
     np.testing.assert_array_equal(reg[g.ids_off: g.ids_off + T * 2 * 4].view(np.int32).reshape(T, 2), ids)
-    word = int(lb.server._bells[0])
-    assert word == pack_doorbell(seq, T, 0, lb.channel._epoch[0])
+    word = int(lb.server.bell_words[0])
+    assert word == pack_doorbell(seq, T, 0, lb.channel.epochs[0])
     row_of = lb.channel.route_ws(0)[512: 512 + 4 * T].view(torch.int32).cpu().numpy()
     np.testing.assert_array_equal(row_of, np.arange(T))
 

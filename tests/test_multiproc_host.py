@@ -167,7 +167,8 @@ def _f_rank(run_dir):
 
 
 def _a_rank(run_dir):
-    from asap_b200.transport.channel import AttnChannel, request
+    from asap_b200.transport.channel import AttnChannel
+    from asap_b200.transport.wire import exchange as request
 
     obj = [None]
     dist.broadcast_object_list(obj, src=0)
@@ -175,10 +176,10 @@ def _a_rank(run_dir):
     ch = AttnChannel(1, G, [("127.0.0.1", port)], device=0, hello={"model": MODEL}, connect_timeout_s=20.0)
     ch.mem = HostMem(run_dir)
     ch.connect()
-    assert ch._epoch == [1] and ch.expert_bounds == [0, 8]
+    assert ch.epochs == [1] and ch.expert_bounds == [0, 8]
     flags = np.ctypeslib.as_array((ctypes.c_uint32 * (G.flags_bytes // 4)).from_address(ch.result_base))
     assert (flags == 0).all()  # seq_base
-    bell = ch._bells[0]
+    bell = ch.bell_bases[0]
     u64(bell + G.bell_off(1, 0)).value = pack_doorbell(1, 5, 3, 1)
     u64(bell + G.bell_off(1, 1)).value = pack_doorbell(1, 7, 4, 1)
     dist.barrier()
@@ -202,8 +203,8 @@ def _a_rank(run_dir):
     dist.barrier()  # F polls the doorbells above
     dist.barrier()
     ch.reconnect()
-    assert ch._epoch == [2]
-    u64(ch._bells[0] + G.bell_off(1, 0)).value = pack_doorbell(1, 3, 5, 2)
+    assert ch.epochs == [2]
+    u64(ch.bell_bases[0] + G.bell_off(1, 0)).value = pack_doorbell(1, 3, 5, 2)
     dist.barrier()
     dist.barrier()
     ch.unmap_peers()

@@ -58,7 +58,7 @@ def hello(g, a):
 
 
 def ring(srv, a, s, seq, n, layer, epoch):
-    srv._bells[a * srv.g.slots + s] = pack_doorbell(seq, n, layer, epoch)
+    srv.bell_words[a * srv.g.slots + s] = pack_doorbell(seq, n, layer, epoch)
 
 
 def test_epoch_cycles_through_31():
