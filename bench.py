@@ -900,7 +900,7 @@ def run_stack(args):
         if is_a:
             channel = AttnChannel(a_ranks.index(rank), g, endpoints, device=local, expert_bounds=bounds,
                                   timeout_s=120.0).connect()
-            AsapBuffer.connect(channel, local)
+            AsapBuffer.attach(channel, local)
         dist.barrier()
         feeder = None
         if not is_a:

@@ -61,6 +61,24 @@ def from_cli_args(ns: argparse.Namespace) -> Asap:
     return args
 
 
+_process_args: Optional[Asap] = None
+
+
+def set_asap_args(args: Optional[Asap]) -> None:
+    """Install this process's ASAP arguments (srt/server_args.py:88-90); None forgets them."""
+    global _process_args
+    _process_args = args
+
+
+def get_asap_args() -> Asap:
+    """This process's ASAP arguments: the installed ones, else those the launcher exported as ASAP_* environment
+    variables (role "null" outside an ASAP deployment; srt/server_args.py:93-97)."""
+    global _process_args
+    if _process_args is None:
+        _process_args = from_env()
+    return _process_args
+
+
 def export_env(args: Asap) -> None:
     for f in fields(args):
         os.environ.pop(f.name.upper(), None)

@@ -70,8 +70,15 @@ class AsapBuffer:
         self.channel, self.device = channel, device
         self.n_max = channel.g.n_max
         self.hidden = channel.g.hidden
-        self.send_stream = torch.cuda.Stream(device)
+        self._send_stream = None
         self.local_ffn = local_ffn
+
+    @property
+    def send_stream(self) -> torch.cuda.Stream:
+        """The stream every dispatch runs on (made on first use, on this buffer's device)."""
+        if self._send_stream is None:
+            self._send_stream = torch.cuda.Stream(self.device)
+        return self._send_stream
 
     @classmethod
     def get(cls) -> "AsapBuffer":
@@ -85,9 +92,50 @@ class AsapBuffer:
         return buffer
 
     @classmethod
-    def connect(cls, channel, device: int, local_ffn=None) -> "AsapBuffer":
-        """asap.py:99-147 without SGLang's model runner: connect ``channel`` (an AttnChannel) and install the
-        buffer as this process's singleton."""
+    def connect(cls, model_runner) -> "AsapBuffer":
+        """Connect this attention rank to every FFN rank and install the buffer (asap.py:99-147).  Called after
+        the model is loaded and before the KV cache is sized, so the ResultArena exists before SGLang hands the
+        free memory to the KV pool.
+
+        The geometry comes from the --asap-* flags (``args.transport_geometry``: attention DP x TP ranks, micro-
+        batch slots, max dispatch tokens, F ranks) and the model's AsapMoE layers (hidden size, top-k); the F
+        endpoints are --asap-bootstrap-addr's port + f; the A rank is (base replica + DP rank) x TP size + TP rank;
+        the hello carries the model fingerprint the F ranks check.  ASAP_WAITING_TIMEOUT (s, default 60) bounds
+        every device wait, ASAP_BOOTSTRAP_TIMEOUT (s, default 1800) the wait for the F ranks to listen."""
+        import os
+
+        from .args import bootstrap_endpoints, get_asap_args, transport_geometry
+        from .sglang_shim import get_parallel
+        from .transport.channel import AttnChannel
+
+        layers = sorted((m for m in model_runner.model.modules()
+                         if isinstance(getattr(m, "dispatcher", None), AsapDispatcher)), key=lambda m: m.layer_id)
+        if not layers:
+            raise RuntimeError("--asap-ffn-size is set, but the model has no AsapMoE layer")
+        args, parallel = get_asap_args(), get_parallel()
+        if args.asap_ffn_size is None or args.asap_attn_dp_size is None or args.asap_attn_tp_size is None:
+            raise RuntimeError("AsapBuffer.connect needs --asap-ffn-size, --asap-attn-dp-size and --asap-attn-tp-size")
+        # the global replica number: other attention instances may share the F ranks
+        replica = args.asap_attn_base_replica + (parallel.dp_rank or 0)
+        rank = replica * args.asap_attn_tp_size + parallel.tp_rank
+        first = layers[0]
+        model = {"hidden": first.hidden_size, "topk": first.top_k, "n_experts": first.num_experts,
+                 "moe_layers": [m.layer_id for m in layers]}
+        channel = AttnChannel(rank, transport_geometry(args, model["hidden"], model["topk"]),
+                              bootstrap_endpoints(args), device=model_runner.gpu_id, memory=args.asap_transport_mem,
+                              hello={"model": model},
+                              timeout_s=float(os.environ.get("ASAP_WAITING_TIMEOUT", "60")),
+                              connect_timeout_s=float(os.environ.get("ASAP_BOOTSTRAP_TIMEOUT", "1800"))).connect()
+        buffer = cls.install(cls(channel, model_runner.gpu_id))
+        served = [{k: answer.get(k) for k in ("f", "experts", "quant_method")} for answer in channel.replies]
+        logger.info(f"[ASAP] attention rank {rank} connected to {len(served)} FFN ranks over {channel.mem.kind} "
+                    f"memory ({channel.mem.reason}): {served}")
+        return buffer
+
+    @classmethod
+    def attach(cls, channel, device: int, local_ffn=None) -> "AsapBuffer":
+        """Install a buffer over an existing AttnChannel (connecting it first if needed): deployments that build
+        the channel themselves (benchmarks, one-GPU loopback, tests)."""
         if channel.result_base is None:
             channel.connect()
         return cls.install(cls(channel, device, local_ffn))

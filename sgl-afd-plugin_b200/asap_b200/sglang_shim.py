@@ -2,12 +2,14 @@
 
 When ``sglang`` is importable its own classes are used (the drop-in case); otherwise these stand-ins with the
 same names and fields are: ``BaseDispatcher`` (pre-combine hooks), ``StandardTopKOutput`` /
-``TopKOutputChecker`` (sglang.srt.layers.moe.topk) and ``MoeRunnerConfig``
-(sglang.srt.layers.moe.moe_runner.base).
+``TopKOutputChecker`` (sglang.srt.layers.moe.topk), ``MoeRunnerConfig`` (sglang.srt.layers.moe.moe_runner.base)
+and ``get_parallel`` (sglang.srt.runtime_context: this rank's attention DP and TP ranks; the stand-in reads
+ASAP_DP_RANK / ASAP_TP_RANK, 0 when unset).
 """
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Any, Callable, List, NamedTuple, Optional
 
@@ -15,6 +17,7 @@ try:  # pragma: no cover - exercised only where SGLang is installed
     from sglang.srt.layers.moe.moe_runner.base import MoeRunnerConfig  # type: ignore
     from sglang.srt.layers.moe.token_dispatcher.base import BaseDispatcher  # type: ignore
     from sglang.srt.layers.moe.topk import StandardTopKOutput, TopKOutput, TopKOutputChecker  # type: ignore
+    from sglang.srt.runtime_context import get_parallel  # type: ignore
 
     HAVE_SGLANG = True
 except Exception:  # noqa: BLE001
@@ -67,3 +70,11 @@ except Exception:  # noqa: BLE001
         inplace: bool = False
         routed_scaling_factor: Optional[float] = None
         activation: str = "silu"
+
+    class ParallelRanks(NamedTuple):
+        dp_rank: Optional[int]
+        tp_rank: int
+
+    def get_parallel() -> ParallelRanks:
+        """This process's attention data-parallel and tensor-parallel ranks."""
+        return ParallelRanks(int(os.environ.get("ASAP_DP_RANK", "0")), int(os.environ.get("ASAP_TP_RANK", "0")))
