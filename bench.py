@@ -475,6 +475,8 @@ def run_single(args):
         parity, inputs = check_single(x, ids, w, experts, lb.sched, out, s_out, n_experts=args.cpu_experts)
         cpu = cpu_baseline(args.cpu_experts, inputs=inputs, steps=3)
 
+    bar = flashinfer_bar(x, ids, w, args.steps) if KIND == "mxfp4" and not args.no_flashinfer else None
+
     peaks, peak_kind = load_peaks()
     g1_flops, g2_flops = gemm_flops(pairs)
     fp8_burst = 2.0 * peaks["bf16_tflops"]  # kind::f8f6f4 runs at twice the bf16 rate
@@ -507,6 +509,8 @@ def run_single(args):
                      "frac_of_fp4_dense_nominal" if KIND == "mxfp4" else "frac_of_fp8_dense_nominal":
                          round(achieved / (9000.0 if KIND == "mxfp4" else 4500.0), 4)},
         "kernels_ms": {k: round(v, 4) for k, v in kernel_ms.items()},
+        "f_chain_ms": round(sum(kernel_ms.values()), 4),
+        "flashinfer_bar": bar,
         "kernels_gbs": hbm_kernel_gbs(T, pairs, kernel_ms),
         "dispatch_ms": round(statistics.median(dsp), 4), "combine_ms": round(statistics.median(cmb), 4),
         "dispatch_gbs_algorithmic": round(nvlink_bytes_dispatch / (statistics.median(dsp) * 1e-3) / 1e9, 1),
@@ -516,6 +520,50 @@ def run_single(args):
     print(json.dumps(line), flush=True)
     lb.close()
     experts.release()
+
+
+def flashinfer_bar(x, ids, w, steps):
+    """The reference's expert backend on the same layer, same GPU: FlashInfer's trtllm-gen MXFP4 MoE
+    (trtllm_fp4_block_scale_routed_moe, as srt/layers/quantization/mxfp4_flashinfer_trtllm_moe.py:68-99 calls it)
+    over this step's tokens and routing with synthetic MXFP4 experts of the same distribution, activations
+    pre-quantised to MXFP8.  The call is timed with CUDA events (median over ``steps`` calls after 3 warm-up calls);
+    compare with this build's F chain (f_chain_ms: routing + quantise + both GEMMs + reduce).  Test and benchmark
+    infrastructure under tests/golden; null-equivalent with the reason when the prebuilt module is absent."""
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    try:
+        import flashinfer_ref
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+    why = flashinfer_ref.available()
+    if why:
+        return {"unavailable": why}
+    try:
+        weights = flashinfer_ref.random_weights(E, H, I, seed=11)
+        xq, xsf = flashinfer_ref.mxfp8_quantize(x)
+        out = torch.empty(x.shape[0], H, dtype=torch.bfloat16, device=x.device)
+        for _ in range(3):
+            flashinfer_ref.run(xq, xsf, ids, w, weights, E, I, out=out)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(max(steps, 3)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            flashinfer_ref.run(xq, xsf, ids, w, weights, E, I, out=out)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        finite = bool(torch.isfinite(out.float()).all().item())
+        del weights
+        torch.cuda.empty_cache()
+        return {"ms": round(ms, 4), "tflops": round(6.0 * H * I * int(ids.numel()) / (ms * 1e-3) / 1e12, 1),
+                "output_finite": finite, "calls": len(times),
+                "what": "flashinfer trtllm_fp4_block_scale_routed_moe (MXFP8 x MXFP4, SwiGLU, weighted sum), "
+                        "same tokens and routing, synthetic experts; excludes the activation quantisation"}
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
 
 
 def load_traffic(kernel, pairs):
@@ -1449,6 +1497,7 @@ def main():
     ap.add_argument("--cpu-experts", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-flashinfer", action="store_true", help="skip the FlashInfer expert-backend bar")
     ap.add_argument("--workload", choices=("layer", "fp8-layer", "zipf-sweep", "stack"), default="layer",
                     help="layer: config 2 (MXFP4); fp8-layer: config 4 (FP8 block-scaled); zipf-sweep: config 5, "
                          "T in 256/1024/4096/16384 with skewed routing, one line per T; stack: config 3, 8 layers "
