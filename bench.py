@@ -1234,8 +1234,7 @@ def run_multi(args):
     dist.all_gather_object(eps, ep)
     endpoints = [e for e in eps if e is not None]
     if is_a:
-        channel = AttnChannel(a_idx, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s,
-                              staged=args.staged).connect()
+        channel = AttnChannel(a_idx, g, endpoints, device=local, expert_bounds=bounds, timeout_s=timeout_s).connect()
     dist.barrier()
     feeder = None
     if not is_a:
@@ -1257,8 +1256,8 @@ def run_multi(args):
                         sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream,
                                                   graph=args.graphs)
                     continue
-                # staged dispatch: answer the A ranks in the order their messages complete here
-                for a in (serve_order(f, n_a, n_f) if args.staged else range(n_a)):
+                # fixed order: answer the A ranks in the order their messages complete here (send_order)
+                for a in serve_order(f, n_a, n_f):
                     if args.graphs:
                         sched.run_graph([(a, 0, s + 1)], 0, stream.cuda_stream)
                     else:
@@ -1410,7 +1409,7 @@ def run_multi(args):
             "metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE[KIND], "data": "synthetic",
-            "gpu_launches": args.steps * ((3 + (n_f if args.staged else 1)) * n_a +
+            "gpu_launches": args.steps * (4 * n_a +
                                           (f_job_launches(n_a) if args.join_replicas else f_job_launches() * n_a)
                                           * n_f), "roofline": None,
             "cpu_baseline": None,
@@ -1433,8 +1432,8 @@ def run_multi(args):
                            "one job per message" + (", first ready replica first (round robin on the device)"
                                                     if args.any_order else ""))
                           + (", CUDA-graph replays" if args.graphs else ""), "host_binding": binding,
-                "dispatch": "staged (one F rank at a time)" if args.staged else
-                          "all F ranks at once", "l2": "inputs larger than L2, no flush"
+                "dispatch": "one pass, F ranks filled in turn from a*F/A (each doorbell rung when its rows are stored)",
+                "l2": "inputs larger than L2, no flush"
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
             line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
@@ -1506,9 +1505,6 @@ def main():
                     help="default: sigmoid for the layer workload, zipf for the sweep")
     ap.add_argument("--topology", default="half", help="N>1: half (NA/NF), 2a6f (8 GPUs), 2a4f (6 GPUs)")
     ap.add_argument("--latency-iters", type=int, default=10, help="zipf-sweep: single-message latency samples")
-    ap.add_argument("--staged", action="store_true",
-                    help="N>1: A ranks send to one F rank at a time (asap_dispatch_staged), F ranks answer in that "
-                         "order")
     ap.add_argument("--graphs", action="store_true",
                     help="F jobs as CUDA-graph replays (FfnScheduler.run_graph; zipf-sweep and N>1)")
     ap.add_argument("--placement", choices=("block", "interleave"), default="interleave",
@@ -1531,7 +1527,7 @@ def main():
         args.warmup = 3
     if args.routing is None:
         args.routing = "zipf" if args.workload == "zipf-sweep" else ROUTING
-    args.any_order = not args.fixed_order and not args.staged
+    args.any_order = not args.fixed_order
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "stack":

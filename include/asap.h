@@ -119,7 +119,8 @@ int asap_memset32(uint64_t dev_ptr, uint32_t value, uint64_t count, void* stream
  * the watchdog to release waits). */
 int asap_write32(uint64_t dev_ptr, uint32_t value, void* stream);
 
-/* Bytes of the per-slot routing workspace asap_dispatch fills and asap_combine reads. */
+/* Bytes of the per-slot routing workspace asap_dispatch fills and asap_combine reads: 512 + 8 * num_f * n_max
+ * (each F rank's token -> row table and its row -> token list). */
 uint64_t asap_route_ws_bytes(const asap_geometry_t* g);
 
 /* ---------------------------------------------------------------- A side ------------------------ */
@@ -138,6 +139,9 @@ uint64_t asap_route_ws_bytes(const asap_geometry_t* g);
  *  route_ws asap_route_ws_bytes() of device memory for this slot; combine reads it
  * Each F rank receives only the tokens routed to it (compacted, ascending token order); the doorbell
  * announces that count. A rank that receives no token gets one row whose ids are all -1.
+ * Each F rank's doorbell is released as soon as its own rows are stored, and A rank a sends to F rank
+ * a*num_f/num_a first, then the next ones in turn, so that concurrent A ranks start on different F ranks and
+ * each F rank has a complete first message after about 1/num_f of the transfer.
  * The kernel first waits (bounded by timeout_ns) until done[f][slot] >= seq-1 for every f when
  * backpressure != 0; on timeout it writes ASAP_ST_BACKPRESSURE_TIMEOUT and sends nothing. */
 int asap_dispatch(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
@@ -155,28 +159,16 @@ int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n
                  void* stream);
 
 /* Read back a routing workspace after a dispatch and its combine (debug/measurement): the row count announced to
- * each F rank, the globaltimer (ns) at which the doorbells were released and the one at which asap_combine's wait
+ * each F rank, the globaltimer (ns) at which the last of its doorbells was released and the one at which asap_combine's wait
  * saw every done flag. Synchronizes `stream`. */
 int asap_dispatch_info(uint64_t route_ws, int32_t num_f, int32_t* counts, uint64_t* t_ring_ns,
                        uint64_t* t_replies_ns, void* stream);
-
-/* asap_dispatch with the payload sent one F rank at a time (no counterpart in the reference: its AttnChannel.send
- * copies to every F rank and rings every doorbell in one pass, channel.py:340-355): F rank f_order[i]'s rows are
- * packed by the i-th grid, which rings that F rank's doorbell as soon as they are out, so an F rank can start on
- * the message while the next F rank's rows still cross NVLink.  f_order is a permutation of [0, num_f); NULL
- * rotates by the A rank (F ranks a*num_f/num_a, +1, ...), so that the A replicas start on different F ranks.
- * Same checks, routing table, arena bytes and doorbell words as asap_dispatch. */
-int asap_dispatch_staged(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
-                         const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
-                         int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
-                         const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
-                         uint64_t status, uint64_t timeout_ns, void* stream, const int32_t* f_order);
 
 /* Allocation-free asap_dispatch (no counterpart in the reference).  Some callers cannot allocate device memory:
  * an attention rank whose free memory SGLang has already handed to the KV-cache pool, or a host that binds this
  * ABI from another language and only holds the transport's mapped arenas.  This entry point needs no routing
  * workspace from them: the routing table of each slot lives in a static device array inside the library (8
- * slots, num_f * n_max <= 131072 rows per slot, about 4 MiB held by every GPU that loads the library until the
+ * slots, num_f * n_max <= 131072 rows per slot, about 8 MiB held by every GPU that loads the library until the
  * process exits), and *route_ws_out returns its device address for asap_combine / asap_wait_replies.  Larger
  * geometries or slot >= 8 are rejected with ASAP_EINVAL.  The first call on a device looks the array up
  * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.  It calls no

@@ -78,10 +78,6 @@ _SIGS = {
                                 c_uint64, c_uint64, c_int32, c_uint64, c_int32, c_int32, POINTER(c_int32),
                                 POINTER(c_uint64), POINTER(c_uint64), c_uint64, c_uint64, c_int32, c_uint64,
                                 c_uint64, c_void_p]),
-    "asap_dispatch_staged": (c_int32, [POINTER(Geometry_t), c_int32, c_int32, c_uint32, c_int32, POINTER(c_int32),
-                                       c_uint64, c_uint64, c_int32, c_uint64, c_int32, c_int32, POINTER(c_int32),
-                                       POINTER(c_uint64), POINTER(c_uint64), c_uint64, c_uint64, c_int32, c_uint64,
-                                       c_uint64, c_void_p, POINTER(c_int32)]),
     "asap_dispatch_noalloc": (c_int32, [POINTER(Geometry_t), c_int32, c_int32, c_uint32, c_int32, POINTER(c_int32),
                                         c_uint64, c_uint64, c_int32, c_uint64, c_int32, c_int32, POINTER(c_int32),
                                         POINTER(c_uint64), POINTER(c_uint64), c_uint64, c_int32, c_uint64, c_uint64,

@@ -72,7 +72,7 @@ class AttnChannel:
 
     def __init__(self, a: int, geometry: Geometry, endpoints: Sequence[Tuple[str, int]], *, device: int,
                  seq_base: int = 0, timeout_s: float = 60.0, connect_timeout_s: float = 60.0, memory: str = "auto",
-                 hello: Optional[dict] = None, expert_bounds: Optional[Sequence[int]] = None, staged: bool = False,
+                 hello: Optional[dict] = None, expert_bounds: Optional[Sequence[int]] = None,
                  _backpressure: bool = True, _epoch_override: Optional[int] = None, _connector=None):
         if len(endpoints) != geometry.num_f:
             raise ValueError(f"need one endpoint per F rank ({geometry.num_f}), got {len(endpoints)}")
@@ -86,9 +86,6 @@ class AttnChannel:
         self._backpressure, self._epoch_override, self._connector = _backpressure, _epoch_override, _connector
         self.memory, self.mem = memory, None
         self.expert_bounds = list(expert_bounds) if expert_bounds is not None else None
-        # staged: the payload goes to one F rank at a time, each doorbell rung as soon as its rows are out
-        # (asap_dispatch_staged), in the order staged_order(a, num_a, num_f)
-        self.staged = bool(staged) and geometry.num_f > 1
         self.links: List[_FLink] = []
         self.status = None
         self._arena: Optional[Shared] = None
@@ -258,10 +255,7 @@ class AttnChannel:
                 int(w_is_bf16), n_tokens, self._c_bounds, self._c_recv, self._c_bells, self.result_base,
                 self._ws_ptr(slot), int(self._backpressure), self.status.ptr, int(self.timeout_s * 1e9),
                 ctypes.c_void_p(stream))
-        if self.staged:
-            N.call("asap_dispatch_staged", *args, None)
-        else:
-            N.call("asap_dispatch", *args)
+        N.call("asap_dispatch", *args)
         return Ticket(slot, seq, layer_id, n_tokens)
 
     def wait(self, ticket: Ticket, stream: int) -> List[int]:
@@ -283,13 +277,14 @@ class AttnChannel:
                int(self.timeout_s * 1e9), ctypes.c_void_p(stream))
 
 
-def staged_order(a: int, num_a: int, num_f: int) -> List[int]:
-    """The F ranks in the order A rank a's staged dispatch sends to them (asap_dispatch_staged's default):
-    rotated by a * num_f // num_a, so that the A ranks start on different F ranks."""
+def send_order(a: int, num_a: int, num_f: int) -> List[int]:
+    """The F ranks in the order A rank a's dispatch fills them (each F rank's doorbell rings when its rows are
+    stored): starting at a * num_f // num_a, so that concurrent A ranks start on different F ranks."""
     off = a * num_f // max(1, num_a)
     return [(off + i) % num_f for i in range(num_f)]
 
 
 def serve_order(f: int, num_a: int, num_f: int) -> List[int]:
-    """The A ranks in the order their staged messages complete at F rank f (the order f should answer them)."""
-    return sorted(range(num_a), key=lambda a: (staged_order(a, num_a, num_f).index(f), a))
+    """The A ranks in the order their messages complete at F rank f (the order a fixed-order F rank should answer
+    them)."""
+    return sorted(range(num_a), key=lambda a: (send_order(a, num_a, num_f).index(f), a))

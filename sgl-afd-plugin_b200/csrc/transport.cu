@@ -64,12 +64,14 @@ static int check_geometry(const asap_geometry_t* g) {
 // ------------------------------------------------------------------ routing workspace layout
 // [0, 256)      int32 count[ASAP_MAX_F]  (rows announced to F rank f, >= 1)
 // [256, 320)    int32 pad[ASAP_MAX_F]    (1 when f received no token and gets one row of ids -1)
-// [320, 384)    uint32 arrive counters of the pack grids: [0] for a pack to every F rank, [f] for F rank f alone
-// [384, 392)    uint64 globaltimer (ns) when the doorbells were released
+// [320, 384)    uint32 chunks[ASAP_MAX_F]: 8-row chunks of F rank f the pack kernel has stored so far
+// [384, 392)    uint64 globaltimer (ns) when the last doorbell was released
 // [392, 400)    uint64 globaltimer (ns) when the combine's wait saw every done flag
-// [400, 512)    reserved
+// [400, 404)    uint32 doorbells released so far by the pack kernel
+// [404, 512)    reserved
 // [512, ...)    int32 row_of[num_f][n_max]: compacted row of token t in f's region, -1 if not routed
-constexpr uint64_t kWsCount = 0, kWsPad = 256, kWsSync = 320, kWsRing = 384, kWsRows = 512;
+//               int32 tok_of[num_f][n_max]: token of compacted row r of f's region (rows < count[f])
+constexpr uint64_t kWsCount = 0, kWsPad = 256, kWsSync = 320, kWsRing = 384, kWsRung = 400, kWsRows = 512;
 
 // K1: one CTA. Backpressure wait, then the per-F-rank compacted row index of every token (ascending token
 // order, a stable compaction).
@@ -94,6 +96,7 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
   int32_t* count = reinterpret_cast<int32_t*>(ws + kWsCount);
   int32_t* pad = reinterpret_cast<int32_t*>(ws + kWsPad);
   int32_t* row_of = reinterpret_cast<int32_t*>(ws + kWsRows);
+  int32_t* tok_of = row_of + (int64_t)F * g.n_max;
 
   // Backpressure (channel.py:337-339): the previous message of this slot must be answered by every F.
   if (backpressure && tid < F) {
@@ -164,6 +167,7 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
         if (f >= F) break;
         const int32_t r = ((mask >> f) & 1u) ? wcnt[warp][f] + __popc(bal[f] & lt) : -1;
         row_of[(int64_t)f * g.n_max + t] = r;
+        if (r >= 0) tok_of[(int64_t)f * g.n_max + r] = t;
       }
     }
     __syncthreads();
@@ -174,106 +178,121 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
     pad[tid] = total > 0 ? 0 : 1;
   }
   if (tid < ASAP_MAX_F) reinterpret_cast<uint32_t*>(ws + kWsSync)[tid] = 0;
+  if (tid == 0) *reinterpret_cast<uint32_t*>(ws + kWsRung) = 0;
 }
 
-// K2: pack every routed token into every F rank that owns one of its experts, then the last CTA to finish
-// releases the doorbells.  One warp per token; 16-byte vector loads and stores.  With only_f >= 0 the grid packs
-// F rank only_f's rows alone and rings only its doorbell (staged dispatch: one launch per F rank, in an order
-// that lets each F rank start on its first message early).
+// K2: pack the routed rows into the F ranks' arenas and ring each F rank's doorbell as soon as all of its rows
+// are stored.  The work is F ranks' compacted row lists (tok_of) cut into chunks of 8 rows, taken in phase order:
+// F rank first_f first, then first_f + 1, ... (mod num_f).  A ranks start at different F ranks (first_f =
+// a * num_f / num_a), so during the first phase every F rank receives one A rank's rows instead of a share of
+// all of them, and its first message is complete (and its expert chain can start) after about 1 / num_f of the
+// transfer.  One warp per chunk: 16-byte loads of the bf16 row, four in flight per lane, 16-byte stores into the
+// (peer) region, the row's ids and weights beside it.  After a chunk the warp's stores are fenced system-wide
+// and counted; the chunk that completes an F rank releases its doorbell.
+constexpr int kPackRows = 8;
+
 struct PackArgs {
   asap_geometry_t g;
   int32_t a, slot, layer_id, n;
   uint32_t seq;
   int32_t ids_is_int64, w_is_bf16;
+  int32_t first_f;
   const uint8_t* x;
   const void* ids;
   const void* w;
-  const uint8_t* ws;
+  uint8_t* ws;
   uint8_t* recv[ASAP_MAX_F];
   uint64_t* bell[ASAP_MAX_F];
   uint32_t epoch[ASAP_MAX_F];
-  int32_t only_f;  // -1: every F rank
-  int32_t stamp;   // record the doorbell release time (the first launch of a dispatch)
 };
+
+__device__ __forceinline__ void ring_doorbell(const PackArgs& p, int f, uint32_t count) {
+  __threadfence_system();
+  st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.bell[f]) + bell_off(p.g, p.a, p.slot)),
+                     pack_doorbell(p.seq, count, (uint32_t)p.layer_id, p.epoch[f]));
+  // the last doorbell of this message records the release time (asap_dispatch_info)
+  if (atomicAdd(reinterpret_cast<uint32_t*>(p.ws + kWsRung), 1u) == (uint32_t)p.g.num_f - 1u)
+    *reinterpret_cast<uint64_t*>(p.ws + kWsRing) = globaltimer_ns();
+}
 
 __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constant__ PackArgs p) {
   const asap_geometry_t& g = p.g;
   const int F = g.num_f;
   const int32_t* count = reinterpret_cast<const int32_t*>(p.ws + kWsCount);
   const int32_t* pad = reinterpret_cast<const int32_t*>(p.ws + kWsPad);
-  const int32_t* row_of = reinterpret_cast<const int32_t*>(p.ws + kWsRows);
+  const int32_t* tok_of = reinterpret_cast<const int32_t*>(p.ws + kWsRows) + (int64_t)F * g.n_max;
+  uint32_t* chunks_done = reinterpret_cast<uint32_t*>(p.ws + kWsSync);
   if (count[0] < 0) return;  // backpressure timed out: send nothing
   const Offsets o = offsets_of(g);
   const int lane = threadIdx.x & 31;
-  const int warps_per_cta = blockDim.x >> 5;
-  const int64_t gwarp = (int64_t)blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * warps_per_cta;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const uint64_t row_bytes = (uint64_t)g.hidden * 2;
   const int nvec = (int)(row_bytes / 16);
   const uint64_t roff = region_off(g, o, p.a, p.slot);
 
-  for (int64_t t = gwarp; t < p.n; t += nwarps) {
-    int32_t rows[ASAP_MAX_F];
-    uint32_t mask = 0;
-    for (int f = 0; f < F; ++f) {
-      rows[f] = row_of[(int64_t)f * g.n_max + t];
-      if (rows[f] >= 0 && (p.only_f < 0 || p.only_f == f)) mask |= 1u << f;
-    }
-    if (!mask) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(p.x + (uint64_t)t * row_bytes);
-    for (int c = lane; c < nvec; c += 32) {
-      const uint4 v = __ldg(src + c);
-      for (uint32_t m = mask; m; m &= m - 1) {
-        const int f = __ffs(m) - 1;
-        uint4* dst = reinterpret_cast<uint4*>(p.recv[f] + roff + (uint64_t)rows[f] * row_bytes);
-        dst[c] = v;
-      }
-    }
-    if (lane < g.topk) {
-      int32_t id;
-      float wt;
-      if (p.ids_is_int64)
-        id = (int32_t)reinterpret_cast<const int64_t*>(p.ids)[(int64_t)t * g.topk + lane];
-      else
-        id = reinterpret_cast<const int32_t*>(p.ids)[(int64_t)t * g.topk + lane];
-      if (p.w_is_bf16)
-        wt = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.w)[(int64_t)t * g.topk + lane]);
-      else
-        wt = reinterpret_cast<const float*>(p.w)[(int64_t)t * g.topk + lane];
-      for (uint32_t m = mask; m; m &= m - 1) {
-        const int f = __ffs(m) - 1;
-        uint8_t* base = p.recv[f] + roff;
-        reinterpret_cast<int32_t*>(base + o.ids_off)[(uint64_t)rows[f] * g.topk + lane] = id;
-        reinterpret_cast<float*>(base + o.w_off)[(uint64_t)rows[f] * g.topk + lane] = wt;
-      }
-    }
+  // chunk prefix in phase order (every thread: num_f <= 16)
+  int32_t first[ASAP_MAX_F + 1];
+  first[0] = 0;
+  for (int i = 0; i < F; ++i) {
+    const int f = (p.first_f + i) % F;
+    first[i + 1] = first[i] + (pad[f] ? 0 : (count[f] + kPackRows - 1) / kPackRows);
   }
-  // F ranks that got no token: one row whose ids name no expert (F's experts skip it, the reply row is 0).
-  if (blockIdx.x == 0 && threadIdx.x < 32) {
+  const int32_t total = first[F];
+
+  // F ranks that got no token: one row whose ids name no expert (F's experts skip it, the reply row is 0), and
+  // the doorbell at once
+  if (gwarp == 0) {
     for (int f = 0; f < F; ++f) {
-      if (!pad[f] || (p.only_f >= 0 && p.only_f != f)) continue;
+      if (!pad[f]) continue;
       uint8_t* base = p.recv[f] + roff;
       if (lane < g.topk) {
         reinterpret_cast<int32_t*>(base + o.ids_off)[lane] = -1;
         reinterpret_cast<float*>(base + o.w_off)[lane] = 0.f;
       }
+      __syncwarp();
+      if (lane == 0) ring_doorbell(p, f, 1u);
     }
   }
-  // Completion: payload visible system-wide before the doorbells (channel.py:350 ordering).
-  __syncthreads();
-  __shared__ uint32_t last;
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    uint32_t* sync = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(p.ws) + kWsSync) + (p.only_f < 0 ? 0 : p.only_f);
-    last = (atomicAdd(sync, 1u) == gridDim.x - 1);
-  }
-  __syncthreads();
-  const int f = p.only_f < 0 ? (int)threadIdx.x : p.only_f;
-  if (last && (p.only_f < 0 ? (int)threadIdx.x < F : threadIdx.x == 0)) {
-    __threadfence_system();
-    if (p.stamp && threadIdx.x == 0) *reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(p.ws) + kWsRing) = globaltimer_ns();
-    st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.bell[f]) + bell_off(g, p.a, p.slot)),
-                       pack_doorbell(p.seq, (uint32_t)count[f], (uint32_t)p.layer_id, p.epoch[f]));
+
+  for (int64_t c = gwarp; c < total; c += nwarps) {
+    int i = 0;
+    while (c >= first[i + 1]) ++i;
+    const int f = (p.first_f + i) % F;
+    const int32_t r0 = (int32_t)(c - first[i]) * kPackRows;
+    const int32_t r1 = min(r0 + kPackRows, count[f]);
+    uint8_t* base = p.recv[f] + roff;
+    for (int32_t r = r0; r < r1; ++r) {
+      const int64_t t = tok_of[(int64_t)f * g.n_max + r];
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + (uint64_t)t * row_bytes);
+      uint4* dst = reinterpret_cast<uint4*>(base + (uint64_t)r * row_bytes);
+      int v = lane;
+      for (; v + 96 < nvec; v += 128) {  // four 16-byte loads in flight per lane
+        const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64), a3 = __ldg(src + v + 96);
+        dst[v] = a0;
+        dst[v + 32] = a1;
+        dst[v + 64] = a2;
+        dst[v + 96] = a3;
+      }
+      for (; v < nvec; v += 32) dst[v] = __ldg(src + v);
+      if (lane < g.topk) {
+        const int64_t k = t * g.topk + lane;
+        const int32_t id = p.ids_is_int64 ? (int32_t)reinterpret_cast<const int64_t*>(p.ids)[k]
+                                          : reinterpret_cast<const int32_t*>(p.ids)[k];
+        const float wt = p.w_is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.w)[k])
+                                     : reinterpret_cast<const float*>(p.w)[k];
+        reinterpret_cast<int32_t*>(base + o.ids_off)[(uint64_t)r * g.topk + lane] = id;
+        reinterpret_cast<float*>(base + o.w_off)[(uint64_t)r * g.topk + lane] = wt;
+      }
+    }
+    // the chunk's stores are visible system-wide before it is counted (channel.py:350 ordering: payload, then
+    // doorbell); the chunk that completes F rank f rings f's doorbell
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_system();
+      const uint32_t done = atomicAdd(&chunks_done[f], 1u) + 1u;
+      if (done == (uint32_t)(first[i + 1] - first[i])) ring_doorbell(p, f, (uint32_t)count[f]);
+    }
   }
 }
 
@@ -379,10 +398,10 @@ int sm_count() {
 
 // ------------------------------------------------------------------ allocation-free dispatch scratch
 // Routing tables of asap_dispatch_noalloc: one per slot, in a file-scope device array that every GPU loading
-// the library holds until the process exits (8 slots x 512 KiB + headers, about 4 MiB).
+// the library holds until the process exits (8 slots x (512 B + 1 MiB), about 8 MiB).
 constexpr int kNoAllocSlots = 8;
 constexpr uint64_t kNoAllocEntries = 1ull << 17;  // num_f * n_max routing-table rows per slot
-constexpr uint64_t kNoAllocSlotBytes = kWsRows + 4ull * kNoAllocEntries;
+constexpr uint64_t kNoAllocSlotBytes = kWsRows + 8ull * kNoAllocEntries;
 static __device__ __align__(256) uint8_t g_noalloc_route[kNoAllocSlots][kNoAllocSlotBytes];
 
 // Device address of g_noalloc_route on the current device, looked up once per device (the host-side symbol is
@@ -641,14 +660,14 @@ int asap_write32(uint64_t dev_ptr, uint32_t value, void* stream) {
 
 uint64_t asap_route_ws_bytes(const asap_geometry_t* g) {
   if (!g || g->num_f < 1 || g->n_max < 1) return 0;
-  return kWsRows + (uint64_t)g->num_f * g->n_max * 4;
+  return kWsRows + (uint64_t)g->num_f * g->n_max * 8;  // row_of and tok_of
 }
 
 static int dispatch_impl(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
                          const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
                          int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
                          const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
-                         uint64_t status, uint64_t timeout_ns, void* stream, const int32_t* f_order) {
+                         uint64_t status, uint64_t timeout_ns, void* stream) {
   int rc = check_geometry(g);
   if (rc) return rc;
   if (g->num_f > ASAP_MAX_F || g->topk > 32) {
@@ -706,28 +725,19 @@ static int dispatch_impl(const asap_geometry_t* g, int32_t a, int32_t slot, uint
   p.x = (const uint8_t*)x;
   p.ids = (const void*)ids;
   p.w = (const void*)w;
-  p.ws = (const uint8_t*)route_ws;
+  p.ws = (uint8_t*)route_ws;
+  p.first_f = (int32_t)((int64_t)a * g->num_f / g->num_a);
   for (int f = 0; f < g->num_f; ++f) {
     p.recv[f] = (uint8_t*)recv[f];
     p.bell[f] = (uint64_t*)bells[f];
     p.epoch[f] = (uint32_t)epochs[f];
   }
+  // one warp per 8-row chunk: at most num_f * n / 8 + num_f chunks, and at most 4 CTAs of 8 warps per SM
   const int warps = 8;
-  int blocks = (n + warps - 1) / warps;
-  blocks = std::min(blocks, sm_count() * 4);
-  if (!f_order) {
-    p.only_f = -1;
-    p.stamp = 1;
-    dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
-    ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
-    return ASAP_OK;
-  }
-  for (int i = 0; i < g->num_f; ++i) {  // one grid per F rank, each ringing its own doorbell when its rows are out
-    p.only_f = f_order[i];
-    p.stamp = i == 0;
-    dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
-    ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
-  }
+  const int64_t chunks = ((int64_t)g->num_f * n + kPackRows - 1) / kPackRows + g->num_f;
+  const int blocks = (int)std::min<int64_t>((chunks + warps - 1) / warps, (int64_t)sm_count() * 4);
+  dispatch_pack_kernel<<<blocks, warps * 32, 0, st>>>(p);
+  ASAP_CHECK_LAUNCH("dispatch_pack_kernel");
   return ASAP_OK;
 }
 
@@ -737,32 +747,7 @@ int asap_dispatch(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t se
                   const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
                   uint64_t status, uint64_t timeout_ns, void* stream) {
   return dispatch_impl(g, a, slot, seq, layer_id, epochs, x, ids, ids_is_int64, w, w_is_bf16, n, expert_bounds, recv,
-                       bells, result, route_ws, backpressure, status, timeout_ns, stream, nullptr);
-}
-
-int asap_dispatch_staged(const asap_geometry_t* g, int32_t a, int32_t slot, uint32_t seq, int32_t layer_id,
-                         const int32_t* epochs, uint64_t x, uint64_t ids, int32_t ids_is_int64, uint64_t w,
-                         int32_t w_is_bf16, int32_t n, const int32_t* expert_bounds, const uint64_t* recv,
-                         const uint64_t* bells, uint64_t result, uint64_t route_ws, int32_t backpressure,
-                         uint64_t status, uint64_t timeout_ns, void* stream, const int32_t* f_order) {
-  int rc = check_geometry(g);
-  if (rc) return rc;
-  if (g->num_f > ASAP_MAX_F) {
-    set_error("asap_dispatch_staged: num_f=%d (max %d) unsupported", g->num_f, ASAP_MAX_F);
-    return ASAP_EINVAL;
-  }
-  int32_t order[ASAP_MAX_F];
-  uint32_t seen = 0;
-  for (int i = 0; i < g->num_f; ++i) {  // default: rotated by the A rank, so the A ranks start on different F ranks
-    order[i] = f_order ? f_order[i] : (int32_t)(((int64_t)a * g->num_f / std::max(1, g->num_a) + i) % g->num_f);
-    if (order[i] < 0 || order[i] >= g->num_f || (seen >> order[i]) & 1u) {
-      set_error("asap_dispatch_staged: f_order must be a permutation of the F ranks");
-      return ASAP_EINVAL;
-    }
-    seen |= 1u << order[i];
-  }
-  return dispatch_impl(g, a, slot, seq, layer_id, epochs, x, ids, ids_is_int64, w, w_is_bf16, n, expert_bounds, recv,
-                       bells, result, route_ws, backpressure, status, timeout_ns, stream, order);
+                       bells, result, route_ws, backpressure, status, timeout_ns, stream);
 }
 
 int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n, uint64_t result,

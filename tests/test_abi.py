@@ -83,7 +83,7 @@ def test_ws_bytes_scale():
 
 def test_route_ws_bytes():
     g = N.Geometry_t(4, 1, 2, 16384, 7168, 8, 4)
-    assert N.lib().asap_route_ws_bytes(ctypes.byref(g)) == 512 + 4 * 16384 * 4
+    assert N.lib().asap_route_ws_bytes(ctypes.byref(g)) == 512 + 8 * 16384 * 4  # row_of + tok_of per F rank
 
 
 @pytest.mark.parametrize("status,expect", [(0, "ok"), (1 | (3 << 8) | (1 << 16) | (77 << 32), "backpressure timeout")])

@@ -33,9 +33,7 @@ class FakeDeployment:
         self.status = torch.zeros(1, dtype=torch.int64, device=dev)
 
     def dispatch(self, seq, layer, x, ids, w, epochs=None, backpressure=True, timeout_s=2.0, ids64=False,
-                 wbf16=False, staged=None):
-        """staged: None -> asap_dispatch; "default" -> asap_dispatch_staged with its rotated order; a list -> that
-        F order."""
+                 wbf16=False):
         g, F = self.g, self.g.num_f
         epochs = epochs or [1] * F
         args = (ctypes.byref(self.gs), self.a, 0, seq, layer, (ctypes.c_int32 * F)(*epochs),
@@ -44,11 +42,7 @@ class FakeDeployment:
                 (ctypes.c_uint64 * F)(*[b.data_ptr() for b in self.bells]), self.result.data_ptr(),
                 self.ws.data_ptr(), int(backpressure), self.status.data_ptr(), int(timeout_s * 1e9),
                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-        if staged is None:
-            N.call("asap_dispatch", *args)
-        else:
-            order = None if staged == "default" else (ctypes.c_int32 * F)(*staged)
-            N.call("asap_dispatch_staged", *args, order)
+        N.call("asap_dispatch", *args)
 
     def done_flags(self):
         return self.result[: self.g.flags_bytes].view(torch.int32)
@@ -97,8 +91,11 @@ def test_dispatch_arena_bytes_and_combine(cuda_ok, n, H, k, bounds, ids64):
     torch.cuda.synchronize()
     assert int(d.status.item()) == 0
     row_of, count, pad = moe.f_rank_tables(ids, bounds)
-    got_rows = d.ws[512: 512 + 4 * F * g.n_max].view(torch.int32).view(F, g.n_max)[:, :n].cpu().numpy()
-    np.testing.assert_array_equal(got_rows, row_of)
+    tables = d.ws[512: 512 + 8 * F * g.n_max].view(torch.int32).view(2, F, g.n_max).cpu().numpy()
+    np.testing.assert_array_equal(tables[0][:, :n], row_of)
+    for f in range(F):  # each F rank's row -> token list: the inverse of its row_of
+        if not pad[f]:
+            np.testing.assert_array_equal(tables[1][f, : count[f]], np.nonzero(row_of[f] >= 0)[0])
     for f in range(F):
         reg = d.region(f).cpu().numpy()
         c = int(count[f])
@@ -230,27 +227,28 @@ def test_doorbell_wait_runs_out_and_rejects_stale_epoch(cuda_ok):
     e.release()
 
 
-@pytest.mark.parametrize("staged", ["default", [2, 0, 1]])
-def test_staged_dispatch_same_bytes(cuda_ok, staged):
-    """asap_dispatch_staged (one grid per F rank, each ringing its own doorbell) leaves the same routing table,
-    arena bytes and doorbell words as asap_dispatch, including an F rank that gets only the padding row."""
+@pytest.mark.parametrize("a,num_a", [(0, 2), (1, 2), (2, 3)])
+def test_dispatch_rotation_same_bytes(cuda_ok, a, num_a):
+    """A ranks fill the F ranks in turn from a*num_f/num_a (each doorbell rung when its own rows are stored): the
+    routing table, arena bytes and doorbell words are the same whichever F rank comes first, including an F rank
+    that gets only the padding row."""
     rng = np.random.default_rng(21)
     n, H, k, bounds = 300, 512, 4, [0, 10, 10, 24]
-    g = Geometry(2, 1, 2, n, H, k, 3)
     x = bf16_tensor_from_np(mx.bf16_round(rng.standard_normal((n, H)).astype(np.float32)))
     ids = torch.from_numpy(np.stack([rng.permutation(26)[:k] - 1 for _ in range(n)]).astype(np.int32)).cuda()
     w = torch.from_numpy(rng.random((n, k)).astype(np.float32)).cuda()
-    plain, stg = FakeDeployment(g, bounds, a=1), FakeDeployment(g, bounds, a=1)
-    plain.dispatch(1, 9, x, ids, w, epochs=[2, 2, 2])  # seq 1: backpressure needs done >= 0, already true
-    stg.dispatch(1, 9, x, ids, w, epochs=[2, 2, 2], staged=staged)
+    ref = FakeDeployment(Geometry(1, 1, 2, n, H, k, 3), bounds, a=0)
+    rot = FakeDeployment(Geometry(num_a, 1, 2, n, H, k, 3), bounds, a=a)
+    ref.dispatch(1, 9, x, ids, w, epochs=[2, 2, 2])  # seq 1: backpressure needs done >= 0, already true
+    rot.dispatch(1, 9, x, ids, w, epochs=[2, 2, 2])
     torch.cuda.synchronize()
-    assert int(plain.status.item()) == 0 and int(stg.status.item()) == 0
-    assert torch.equal(plain.ws[:320], stg.ws[:320]) and torch.equal(plain.ws[512:], stg.ws[512:])
+    assert int(ref.status.item()) == 0 and int(rot.status.item()) == 0
+    assert torch.equal(ref.ws[:320], rot.ws[:320]) and torch.equal(ref.ws[512:], rot.ws[512:])
     for f in range(3):
-        assert torch.equal(plain.region(f), stg.region(f)), f
-        assert torch.equal(plain.bells[f], stg.bells[f]), f
-    with pytest.raises(N.AsapError, match="permutation"):
-        stg.dispatch(2, 9, x, ids, w, epochs=[2, 2, 2], staged=[0, 0, 1])
+        assert torch.equal(ref.region(f), rot.region(f)), f
+        word_ref = int(ref.bells[f][ref.g.bell_off(0, 0) // 8].item())
+        word_rot = int(rot.bells[f][rot.g.bell_off(a, 0) // 8].item())
+        assert word_ref == word_rot, f
 
 
 def test_dispatch_sixteen_f_ranks(cuda_ok):
@@ -268,8 +266,11 @@ def test_dispatch_sixteen_f_ranks(cuda_ok):
     torch.cuda.synchronize()
     assert int(d.status.item()) == 0
     row_of, count, pad = moe.f_rank_tables(ids, bounds)
-    got_rows = d.ws[512: 512 + 4 * F * g.n_max].view(torch.int32).view(F, g.n_max)[:, :n].cpu().numpy()
-    np.testing.assert_array_equal(got_rows, row_of)
+    tables = d.ws[512: 512 + 8 * F * g.n_max].view(torch.int32).view(2, F, g.n_max).cpu().numpy()
+    np.testing.assert_array_equal(tables[0][:, :n], row_of)
+    for f in range(F):  # each F rank's row -> token list: the inverse of its row_of
+        if not pad[f]:
+            np.testing.assert_array_equal(tables[1][f, : count[f]], np.nonzero(row_of[f] >= 0)[0])
     for f in range(F):
         c = int(count[f])
         reg = d.region(f).cpu().numpy()

@@ -23,6 +23,8 @@ TOL = 1e-2
 
 def load_golden():
     path = GOLDEN / "flashinfer_moe_golden.npz"
+    if not path.exists():
+        pytest.skip("no FlashInfer golden outputs (tests/golden/make_flashinfer_golden.py writes them on a B200)")
     d = np.load(path)
     return mx.bf16_from_bits(d["out_bits"]), json.loads(str(d["meta"]))
 
