@@ -56,6 +56,20 @@ struct Params {
   uint64_t status, timeout_ns;
 };
 
+// acc[i] += x[i] * f for 32 consecutive accumulators, two per instruction (the packed fp32 FMA of sm_100; each
+// lane is one fused multiply-add with one rounding, the same result as fmaf): the promotion of a K block is
+// FMA-issue-bound next to the TMEM loads, and the pairs halve its issue slots.
+__device__ __forceinline__ void fma32_pairs(float* acc, const uint32_t (&x)[32], float f) {
+  const float2 ff = make_float2(f, f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 r = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), ff,
+                                make_float2(acc[2 * i], acc[2 * i + 1]));
+    acc[2 * i] = r.x;
+    acc[2 * i + 1] = r.y;
+  }
+}
+
 // E4M3 codes of 4 values (scaled by inv) packed little-endian into one word.
 __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d, float inv) {
   return cvt_e4m3x2(a * inv, b * inv) | (cvt_e4m3x2(c * inv, d * inv) << 16);
@@ -269,30 +283,23 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
           tmem_ld_32x32b_x32(tb + col0, va);
           tmem_ld_32x32b_x32(tb + col0 + 32, vb);
           tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            acc0[i] = fmaf(__uint_as_float(va[i]), f0, acc0[i]);
-            acc0[32 + i] = fmaf(__uint_as_float(vb[i]), f0, acc0[32 + i]);
-          }
+          fma32_pairs(acc0, va, f0);
+          fma32_pairs(acc0 + 32, vb, f0);
           tmem_ld_32x32b_x32(tb + col1, va);
           tmem_ld_32x32b_x32(tb + col1 + 32, vb);
           tmem_wait_ld();
           tc_fence_before();  // this warp's reads of the buffer are complete: hand it back to the MMA warp
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            acc1[i] = fmaf(__uint_as_float(va[i]), f1, acc1[i]);
-            acc1[32 + i] = fmaf(__uint_as_float(vb[i]), f1, acc1[32 + i]);
-          }
+          fma32_pairs(acc1, va, f1);
+          fma32_pairs(acc1 + 32, vb, f1);
         } else {
           uint32_t v[32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             tmem_ld_32x32b_x32(tb + col0 + 32 * c, v);
             tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc0[32 * c + i] = fmaf(__uint_as_float(v[i]), f0, acc0[32 * c + i]);
+            fma32_pairs(acc0 + 32 * c, v, f0);
           }
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -303,8 +310,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
               __syncwarp();
               if (lane == 0) mbar_arrive(&acc_empty[buf]);
             }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc1[32 * c + i] = fmaf(__uint_as_float(v[i]), f1, acc1[32 * c + i]);
+            fma32_pairs(acc1 + 32 * c, v, f1);
           }
         }
       }
