@@ -274,6 +274,27 @@ def expert_bytes():
     return 3 * H * I // 2 + 3 * H * I // 32
 
 
+def step_roofline(flop_busiest_f, weight_bytes_busiest_f, ms, what):
+    """The roofline of a multi-kernel step whose F chain dominates: the busiest F rank's expert GEMM FLOPs at the
+    FP8-rate tensor peak (2 x the measured sustained bf16 rate: a step-long timed region) and its weight bytes at
+    the measured HBM rate; bound = the larger; achieved = FLOP / measured step time (whole step, so transfers and
+    the HBM-bound kernels count against it)."""
+    peaks, peak_kind = load_peaks()
+    fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    t_flop = flop_busiest_f / (fp8 * 1e12) * 1e3
+    t_hbm = weight_bytes_busiest_f / (peaks["hbm_gbs"] * 1e9) * 1e3
+    if t_flop >= t_hbm:
+        achieved = flop_busiest_f / (ms * 1e-3) / 1e12
+        return {"kernel": what, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp8, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / fp8, 4), "traffic": None,
+                "peak_source": f"{peak_kind} bf16_tflops_sustained x 2 (FP8-rate tensor kind)",
+                "t_flop_ms": round(t_flop, 4), "t_hbm_ms": round(t_hbm, 4)}
+    achieved = weight_bytes_busiest_f / (ms * 1e-3) / 1e9
+    return {"kernel": what, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": f"{peak_kind} hbm_gbs",
+            "t_flop_ms": round(t_flop, 4), "t_hbm_ms": round(t_hbm, 4)}
+
+
 def layer_roofline(n_a, T, f_rows, bounds, ms, peaks, peak_kind, nvlink_gbs=None):
     """Per-layer roofline of an nA x nF step: for each F rank, the time its inbound rows take over NVLink
     (x bf16 + ids + weights per routed row), its reply rows outbound, its expert GEMMs at the FP8-rate tensor peak
@@ -847,6 +868,11 @@ def run_sweep(args):
             N.call("asap_ffn_enable_timing", lb.scheds[0].ws_handle, 0)
             f0_ms = dict(zip(("routing", "quantise_permute", "gemm1", "gemm2", "reduce_reply"),
                              [round(v, 4) for v in kms]))
+        pairs_f = [int(sc.debug_tensors()["expert_counts"].sum().item()) for sc in lb.scheds]
+        busiest = max(range(n_f), key=lambda f: pairs_f[f])
+        roof = step_roofline(6.0 * H * I * pairs_f[busiest],
+                             (bounds[busiest + 1] - bounds[busiest]) * expert_bytes(), ms,
+                             f"step of the busiest F rank ({pairs_f[busiest]} pairs, its weights read once)")
         lat, busy, rows = [], [], None
         for _ in range(max(args.latency_iters, 1)):
             _, ticket = step()
@@ -874,8 +900,8 @@ def run_sweep(args):
             "f_rows_per_s": round(sum(rows) / statistics.median(busy), 1),
             "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4), "f0_kernels_ms": f0_ms,
             "weights_gb_read_per_step": round(E * (2 * I * H + H * I) * (0.5 + 1 / 32) / 1e9, 3),
-            "e2e": None, "gpu_launches": args.steps * (4 + f_job_launches() * n_f), "roofline": None,
-            "cpu_baseline": None,
+            "e2e": None, "gpu_launches": args.steps * (4 + f_job_launches() * n_f), "roofline": roof,
+            "f_pairs": pairs_f, "cpu_baseline": None,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -1028,7 +1054,11 @@ def run_stack(args):
                        "expert_bounds": bounds},
             "layer_tokens_per_s": round(n_a * T * L / (ms * 1e-3), 1), "output_finite": finite,
             "e2e": None, "gpu_launches": args.steps * L * 2 * (4 + f_job_launches() * n_f) * n_a,
-            "roofline": None, "cpu_baseline": None, "clocks": clocks_summary,
+            "roofline": step_roofline(
+                6.0 * H * I * L * n_a * T * K_TOP * max(bounds[f + 1] - bounds[f] for f in range(n_f)) / E,
+                L * max(bounds[f + 1] - bounds[f] for f in range(n_f)) * expert_bytes(), ms,
+                "stack step of the busiest F rank (uniform routing: its share of every layer's pairs)"),
+            "cpu_baseline": None, "clocks": clocks_summary,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1411,7 +1441,7 @@ def run_multi(args):
             "dtype": DTYPE[KIND], "data": "synthetic",
             "gpu_launches": args.steps * (4 * n_a +
                                           (f_job_launches(n_a) if args.join_replicas else f_job_launches() * n_a)
-                                          * n_f), "roofline": None,
+                                          * n_f), "roofline": None,  # set per line below
             "cpu_baseline": None,
             "clocks": clock_summary,
         }
@@ -1437,6 +1467,9 @@ def run_multi(args):
                 if T >= 4096 else "x smaller than L2 (weights 6 GB are not)"}
             line["f_rows"] = res["f_rows"]
             line["f_imbalance"] = round(max(res["f_rows"]) / mean_f, 4) if mean_f else None
+            p_max = max(bounds[f + 1] - bounds[f] for f in range(n_f))
+            line["roofline"] = step_roofline(6.0 * H * I * n_a * T * K_TOP * p_max / E, p_max * expert_bytes(), ms,
+                                             "layer step of the busiest F rank (expected pairs of uniform routing)")
             if args.routing != "zipf":
                 line["layer_roofline"] = layer_roofline(n_a, T, res["f_rows"], bounds, ms, *load_peaks(),
                                                         nvlink_gbs=link["ce_peer_write_gbs_median"])
