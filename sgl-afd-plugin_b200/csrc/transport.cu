@@ -186,10 +186,10 @@ __global__ void __launch_bounds__(kRouteThreads) dispatch_route_kernel(
 // F rank first_f first, then first_f + 1, ... (mod num_f).  A ranks start at different F ranks (first_f =
 // a * num_f / num_a), so during the first phase every F rank receives one A rank's rows instead of a share of
 // all of them, and its first message is complete (and its expert chain can start) after about 1 / num_f of the
-// transfer.  One warp per chunk: 16-byte loads of the bf16 row, four in flight per lane, 16-byte stores into the
+// transfer.  One warp per chunk: 16-byte loads of the bf16 row, eight in flight per lane, 16-byte stores into the
 // (peer) region, the row's ids and weights beside it.  After a chunk the warp's stores are fenced system-wide
 // and counted; the chunk that completes an F rank releases its doorbell.
-constexpr int kPackRows = 8;
+constexpr int kPackRows = 4;
 
 struct PackArgs {
   asap_geometry_t g;
@@ -231,13 +231,16 @@ __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constan
   const int nvec = (int)(row_bytes / 16);
   const uint64_t roff = region_off(g, o, p.a, p.slot);
 
-  // chunk prefix in phase order (every thread: num_f <= 16)
-  int32_t first[ASAP_MAX_F + 1];
-  first[0] = 0;
-  for (int i = 0; i < F; ++i) {
-    const int f = (p.first_f + i) % F;
-    first[i + 1] = first[i] + (pad[f] ? 0 : (count[f] + kPackRows - 1) / kPackRows);
+  // chunk prefix in phase order
+  __shared__ int32_t first[ASAP_MAX_F + 1];
+  if (threadIdx.x == 0) {
+    first[0] = 0;
+    for (int i = 0; i < F; ++i) {
+      const int f = (p.first_f + i) % F;
+      first[i + 1] = first[i] + (pad[f] ? 0 : (count[f] + kPackRows - 1) / kPackRows);
+    }
   }
+  __syncthreads();
   const int32_t total = first[F];
 
   // F ranks that got no token: one row whose ids name no expert (F's experts skip it, the reply row is 0), and
@@ -266,15 +269,15 @@ __global__ void __launch_bounds__(256) dispatch_pack_kernel(const __grid_constan
       const int64_t t = tok_of[(int64_t)f * g.n_max + r];
       const uint4* src = reinterpret_cast<const uint4*>(p.x + (uint64_t)t * row_bytes);
       uint4* dst = reinterpret_cast<uint4*>(base + (uint64_t)r * row_bytes);
-      int v = lane;
-      for (; v + 96 < nvec; v += 128) {  // four 16-byte loads in flight per lane
-        const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64), a3 = __ldg(src + v + 96);
-        dst[v] = a0;
-        dst[v + 32] = a1;
-        dst[v + 64] = a2;
-        dst[v + 96] = a3;
+      for (int v0 = lane; v0 < nvec; v0 += 256) {  // eight 16-byte loads in flight per lane, then their stores
+        uint4 buf[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (v0 + 32 * u < nvec) buf[u] = __ldg(src + v0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (v0 + 32 * u < nvec) dst[v0 + 32 * u] = buf[u];
       }
-      for (; v < nvec; v += 32) dst[v] = __ldg(src + v);
       if (lane < g.topk) {
         const int64_t k = t * g.topk + lane;
         const int32_t id = p.ids_is_int64 ? (int32_t)reinterpret_cast<const int64_t*>(p.ids)[k]
