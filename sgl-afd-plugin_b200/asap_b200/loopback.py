@@ -28,9 +28,10 @@ class LocalFfn:
     the other on one stream.  That stream has the highest priority: the F chain is the critical path of the step,
     so its kernels take SMs ahead of A-side work queued beside them (the shared expert)."""
 
-    def __init__(self, schedulers: List[FfnScheduler], a: int, slots: int, device: int, graphs: bool = False):
+    def __init__(self, schedulers: List[FfnScheduler], a: int, slots: int, device: int, graphs: bool = False,
+                 priority: int = -1):
         self.scheds, self.a, self.device, self.graphs = schedulers, a, device, graphs
-        self.stream = torch.cuda.Stream(device, priority=-1)
+        self.stream = torch.cuda.Stream(device, priority=priority)
         self.sent = [torch.cuda.Event() for _ in range(slots)]
         self.done = [torch.cuda.Event() for _ in range(slots)]
 
@@ -62,7 +63,7 @@ class Loopback:
 
     def __init__(self, geometry: Geometry, experts: Union[Dict[int, Mxfp4Experts], List[Dict[int, Mxfp4Experts]]],
                  *, device: int = 0, timeout_s: float = 10.0, swiglu_limit: float = 0.0,
-                 run_dir: Optional[str] = None, timing: bool = False, graphs: bool = False):
+                 run_dir: Optional[str] = None, timing: bool = False, graphs: bool = False, ffn_priority: int = -1):
         per_f = [experts] if isinstance(experts, dict) else list(experts)
         if geometry.num_a != 1 or geometry.group != 1 or geometry.num_f != len(per_f):
             raise ValueError("a loopback deployment is one A rank (num_a = group = 1) and num_f F ranks, one experts "
@@ -85,7 +86,7 @@ class Loopback:
         self.scheds = [FfnScheduler(srv, d, swiglu_limit=swiglu_limit, timeout_s=timeout_s, timing=timing)
                        for srv, d in zip(self.servers, per_f)]
         self.sched = self.scheds[0]
-        self.local = LocalFfn(self.scheds, 0, geometry.slots, device, graphs=graphs)
+        self.local = LocalFfn(self.scheds, 0, geometry.slots, device, graphs=graphs, priority=ffn_priority)
         self.buffer = AsapBuffer(self.channel, device, local_ffn=self.local)
 
     def install(self) -> AsapBuffer:

@@ -34,7 +34,8 @@ struct JobDesc {
   uint64_t t_reply;  // globaltimer (ns) when the reply's done flag was released
   int32_t rows;      // messages joined in this job (RowState entries after the descriptor)
   int32_t small;     // 1: the GEMMs run weights-as-M (gemmT), for jobs whose 128-row blocks are mostly padding
-  uint32_t pad[4];
+  uint32_t tiles[2];  // next unclaimed tile of GEMM1 / GEMM2 (the GEMMs' dynamic tile scheduler), zeroed per job
+  uint32_t pad[2];
 };
 static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
 
@@ -174,6 +175,7 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
   if (lane == 0) {
     d->t_seen = globaltimer_ns();
     d->t_reply = 0;
+    d->tiles[0] = d->tiles[1] = 0;
     d->seq = seq0;
     d->layer = layer0;
     d->epoch = epoch0;
@@ -222,6 +224,7 @@ __global__ void ffn_wait_any_kernel(const __grid_constant__ WaitArgs a) {
   if (lane == 0) {
     d->t_seen = globaltimer_ns();
     d->t_reply = 0;
+    d->tiles[0] = d->tiles[1] = 0;
     d->sync = 0;
     d->rows = 1;
   }
@@ -276,6 +279,7 @@ __global__ void ffn_post_kernel(const __grid_constant__ PostArgs a) {
   d->sync = 0;
   d->t_seen = 0;
   d->t_reply = 0;
+  d->tiles[0] = d->tiles[1] = 0;
   d->rows = a.rows;
   d->valid = 1;
 }
@@ -536,6 +540,10 @@ constexpr uint32_t TMEM_COLS = 512, TMEM_ACC = 0, TMEM_SFA = 256, TMEM_SFB = TME
 static_assert(TMEM_SFB + 8 * STAGES <= TMEM_COLS, "scale-factor columns exceed TMEM");
 constexpr int SMEM_TILES = STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES);
 constexpr int STAGE_OUT_BYTES = NUM_EPI_WARPS * 2048;  // per epilogue warp: 32 rows x 64 B of output in flight
+// Tiles are handed out at run time: the producer claims the next tile index from the job's counter (so CTAs that
+// start late -- beside another kernel on the GPU -- simply take fewer tiles) and passes it to the MMA and epilogue
+// warps through a queue of TILE_Q entries in shared memory.
+constexpr int TILE_Q = 8;
 constexpr int SMEM_BYTES =
     1024 /*align slack*/ + SMEM_TILES + STAGE_OUT_BYTES + 1024 /*barriers*/ + 4 * (ASAP_MAX_LOCAL_EXPERTS + 8);
 static_assert(SMEM_BYTES <= 232448, "shared memory over the 227 KB per block");
@@ -570,6 +578,7 @@ struct Params {
   uint8_t* out_q;          // GEMM1: [m_cap, N/2] E4M3
   uint8_t* out_sf;         // GEMM1: scale atoms [m_cap/128][(N/2)/128][512]
   __nv_bfloat16* out_bf;   // GEMM2: [m_cap, N]
+  uint32_t* tile_ctr;      // the job's tile counter of this GEMM (JobDesc::tiles)
   int32_t P, N, K;
   float swiglu_limit;
   uint64_t status, timeout_ns;
@@ -679,7 +688,10 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* mma_done = acc_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* tq_full = mma_done + 1;     // [TILE_Q] a tile index was published
+  uint64_t* tq_empty = tq_full + TILE_Q;  // [TILE_Q] the MMA warp and every epilogue warp have read it
+  int32_t* s_tile = reinterpret_cast<int32_t*>(tq_empty + TILE_Q);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_tile + TILE_Q);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int32_t* s_mstart = reinterpret_cast<int32_t*>(tmem_slot + 4);
 
@@ -695,6 +707,10 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, NUM_EPI_WARPS);
     mbar_init(mma_done, 1);
+    for (int q = 0; q < TILE_Q; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], 1 + NUM_EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -722,7 +738,18 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tq = 0; ok; ++tq) {
+        // claim the next tile and publish it (-1: none left) to the MMA and epilogue warps
+        const int q = tq % TILE_Q;
+        if (!mbar_wait(&tq_empty[q], ((tq / TILE_Q) & 1u) ^ 1u, deadline, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t claimed = atomicAdd(p.tile_ctr, 1u);
+        const int tile = claimed < (uint32_t)num_tiles ? (int)claimed : -1;
+        s_tile[q] = tile;
+        mbar_arrive(&tq_full[q]);
+        if (tile < 0) break;
         int e, m_blk, n_t;
         decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
         const int a_row = m_blk * BM;
@@ -769,7 +796,12 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       uint32_t phase = 0, acc_phase = 0;
       const uint32_t idesc = idesc_mxf8f6f4(BM, BN);
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tq = 0; ok; ++tq) {
+        const int q = tq % TILE_Q;
+        if (!mbar_wait(&tq_full[q], (tq / TILE_Q) & 1u, deadline, abort_flag)) break;
+        const int tile = s_tile[q];
+        mbar_arrive(&tq_empty[q]);
+        if (tile < 0) break;
         if (!mbar_wait(acc_empty, acc_phase ^ 1u, deadline, abort_flag)) {
           ok = false;
           break;
@@ -815,7 +847,13 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
     const int row_in_tile = q * 32 + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (uint32_t tq = 0;; ++tq) {
+      const int qi = tq % TILE_Q;
+      if (!mbar_wait(&tq_full[qi], (tq / TILE_Q) & 1u, deadline, abort_flag)) break;
+      const int tile = s_tile[qi];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tq_empty[qi]);
+      if (tile < 0) break;
       int e, m_blk, n_t;
       decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
       const int64_t row = (int64_t)m_blk * BM + row_in_tile;
@@ -1497,6 +1535,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     g1.row_w = pa.row_w;
     g1.out_q = B + L.hq;
     g1.out_sa = (float*)(B + L.hq_sf);
+    g1.tile_ctr = &desc->tiles[0];
     g1.P = L.P;
     g1.N = 2 * L.I;
     g1.K = L.H;
@@ -1514,6 +1553,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     g2.out_q = nullptr;
     g2.out_sa = nullptr;
     g2.out_bf = (__nv_bfloat16*)(B + L.y2);
+    g2.tile_ctr = &desc->tiles[1];
     g2.N = L.H;
     g2.K = L.I;
     gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::Cfg<1>::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
@@ -1538,6 +1578,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g1.row_w = pa.row_w;
   g1.out_q = B + L.hq;
   g1.out_sf = B + L.hq_sf;
+  g1.tile_ctr = &desc->tiles[0];
   g1.P = L.P;
   g1.N = 2 * L.I;
   g1.K = L.H;
@@ -1586,6 +1627,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.out_q = nullptr;
   g2.out_sf = nullptr;
   g2.out_bf = (__nv_bfloat16*)(B + L.y2);
+  g2.tile_ctr = &desc->tiles[1];
   g2.N = L.H;
   g2.K = L.I;
   if (token_major) {

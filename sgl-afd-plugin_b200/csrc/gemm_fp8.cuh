@@ -30,7 +30,8 @@ constexpr int CTRL_BYTES = 4096;     // barriers, TMEM slot, expert starts, row 
 constexpr int STAGE_OUT_BYTES = NUM_EPI_WARPS * 2048;  // GEMM2 output staging, 32 rows x 64 B per epilogue warp
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_OUT_BYTES + CTRL_BYTES;
 static_assert(SMEM_BYTES <= 232448, "shared memory over the 227 KB per block");
-static_assert(256 + 4 * (ASAP_MAX_LOCAL_EXPERTS + 1) <= 2048, "expert starts overlap the amax exchange");
+static_assert(256 + 4 * (ASAP_MAX_LOCAL_EXPERTS + 1) <= 1536, "expert starts overlap the tile queue");
+constexpr int TILE_Q = 8;  // dynamic tile scheduler queue (as gemm::moe_gemm_kernel), at ctrl + 1536
 constexpr float kE4M3Max = 448.f;
 
 // tcgen05 instruction descriptor, kind::f8f6f4: D fp32, A = B = E4M3, both K-major, M x N.
@@ -51,6 +52,7 @@ struct Params {
   uint8_t* out_q;          // GEMM1: [m_cap, N/2] E4M3
   float* out_sa;           // GEMM1: [(N/2)/128][m_cap] fp32
   __nv_bfloat16* out_bf;   // GEMM2: [m_cap, N]
+  uint32_t* tile_ctr;      // the job's tile counter of this GEMM (JobDesc::tiles)
   int32_t P, N, K;
   float swiglu_limit;
   uint64_t status, timeout_ns;
@@ -96,6 +98,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 192);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 196);
   int32_t* s_mstart = reinterpret_cast<int32_t*>(ctrl + 256);
+  uint64_t* tq_full = reinterpret_cast<uint64_t*>(ctrl + 1536);  // [TILE_Q] a tile index was published
+  uint64_t* tq_empty = tq_full + TILE_Q;                          // [TILE_Q] every consumer warp has read it
+  int32_t* s_tile = reinterpret_cast<int32_t*>(tq_empty + TILE_Q);
   float* s_amax = reinterpret_cast<float*>(ctrl + 2048);  // [2 tile parities][2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -113,6 +118,10 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
     }
     mbar_init(mma_done, 1);
     for (int b = 0; b < 8; ++b) mbar_init(&amax_bar[b], 64);
+    for (int q = 0; q < TILE_Q; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], 1 + NUM_EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -142,7 +151,18 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tq = 0; ok; ++tq) {
+        // claim the next tile and publish it (-1: none left) to the MMA and epilogue warps
+        const int q = tq % TILE_Q;
+        if (!mbar_wait(&tq_empty[q], ((tq / TILE_Q) & 1u) ^ 1u, deadline, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t claimed = atomicAdd(p.tile_ctr, 1u);
+        const int tile = claimed < (uint32_t)num_tiles ? (int)claimed : -1;
+        s_tile[q] = tile;
+        mbar_arrive(&tq_full[q]);
+        if (tile < 0) break;
         int e, m_blk, n_t;
         gemm::decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
         const int a_row = m_blk * BM;
@@ -193,7 +213,12 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
       uint32_t it = 0;
       const uint32_t idesc = idesc_f8f6f4(BM, BN);
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tq = 0; ok; ++tq) {
+        const int q = tq % TILE_Q;
+        if (!mbar_wait(&tq_full[q], (tq / TILE_Q) & 1u, deadline, abort_flag)) break;
+        const int tile = s_tile[q];
+        mbar_arrive(&tq_empty[q]);
+        if (tile < 0) break;
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const uint32_t buf = it & 1u;
           if (!mbar_wait(&acc_empty[buf], ((it >> 1) & 1u) ^ 1u, deadline, abort_flag) ||
@@ -234,7 +259,13 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1) moe_gemm_fp8_kernel(cons
     const int col1 = EPI == 0 ? 128 + 64 * half : 128 * half + 64;
     uint32_t it = 0, tcount = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
+    for (uint32_t tq = 0; ok; ++tq, ++tcount) {
+      const int qi = tq % TILE_Q;
+      if (!mbar_wait(&tq_full[qi], (tq / TILE_Q) & 1u, deadline, abort_flag)) break;
+      const int tile = s_tile[qi];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tq_empty[qi]);
+      if (tile < 0) break;
       int e, m_blk, n_t;
       gemm::decode_tile(s_mstart, P, NT, tile, e, m_blk, n_t);
       const int64_t row = (int64_t)m_blk * BM + row_in_tile;
