@@ -253,10 +253,9 @@ def f_job_launches(rows=1):
 
 
 def hbm_kernel_gbs(T, pairs, kernel_ms):
-    """Algorithmic GB/s of the HBM-bound F stages: quantise+permute reads each token's bf16 row once and writes its
-    activation codes + scales into every local pair row; the weighted reduce reads every pair's bf16 row and writes
-    each token's reply row.  With MXFP4 experts the reduce runs inside GEMM2's epilogue (its time is GEMM2's), and
-    the reduce_reply stage is only the zero rows of pairless tokens and the done flags."""
+    """Algorithmic GB/s of the two HBM-bound F kernels: quantise+permute reads each token's bf16 row once and
+    writes its activation codes + scales into every local pair row; the weighted reduce reads every pair's bf16 row
+    and writes each token's reply row."""
     scale_bytes = H // 32 if KIND == "mxfp4" else 4 * (H // 128)
     qp = T * 2 * H + pairs * (H + scale_bytes)
     red = pairs * 2 * H + T * 2 * H
@@ -264,7 +263,7 @@ def hbm_kernel_gbs(T, pairs, kernel_ms):
         return round(nbytes / (ms * 1e-3) / 1e9, 1) if ms and ms > 0 else None
 
     return {"quantise_permute": gbs(qp, kernel_ms.get("quantise_permute")),
-            "reduce_reply": "fused into GEMM2's epilogue" if KIND == "mxfp4" else gbs(red, kernel_ms.get("reduce_reply")),
+            "reduce_reply": gbs(red, kernel_ms.get("reduce_reply")),
             "bytes": {"quantise_permute": qp, "reduce_reply": red}}
 
 

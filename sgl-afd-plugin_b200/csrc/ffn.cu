@@ -70,9 +70,7 @@ constexpr int kPermChunks = 128;  // chunks of pairs the permutation is split in
 struct WsLayout {
   int32_t n_max, topk, P, H, I;
   int64_t m_cap;  // rows of the expert-major activation buffers (multiple of 128)
-  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, ids_all, w_all, xq, xq_sf, hq, hq_sf, y2, scnt, tpairs,
-      total;
-  int32_t slices;  // column slices of a reply row the fused reduce completes one by one: two per 256-column tile
+  uint64_t desc, ecnt, mstart, hist, pair_pos, row_tok, row_w, ids_all, w_all, xq, xq_sf, hq, hq_sf, y2, total;
 };
 
 static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
@@ -103,9 +101,6 @@ static WsLayout ws_layout(int n_max, int topk, int P, int H, int I) {
   L.hq = take((uint64_t)L.m_cap * I);
   L.hq_sf = take((uint64_t)L.m_cap * (I / 32));
   L.y2 = take((uint64_t)L.m_cap * H * 2);
-  L.slices = 2 * (H / 256);
-  L.scnt = take(4ull * n_max * L.slices);  // per (token, slice): pair rows of GEMM2 stored so far
-  L.tpairs = take(4ull * n_max);           // per token: its local pairs
   L.total = off;
   return L;
 }
@@ -453,9 +448,6 @@ struct QuantArgs {
   const int32_t* pair_pos;              // [n, topk] permuted row of each (token, slot), -1 when not local
   uint8_t* xq;                          // [m_cap, H] E4M3, expert-major
   uint8_t* xq_sf;                       // MXFP8: scale atoms [m_cap/128][H/128][512]; FP8: fp32 [H/128][m_cap]
-  int32_t* scnt;                        // MXFP8: the fused reduce's slice counters [n][slices], zeroed here
-  int32_t* tpairs;                      // MXFP8: local pairs per token [n], written here
-  int32_t slices;
 };
 
 // Quantise 32 consecutive fp32 values to E4M3 with one E8M0 scale; returns the scale byte.
@@ -490,9 +482,6 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const __grid_constan
   for (int64_t t = gwarp; t < n; t += nwarps) {
     const int32_t mine = lane < p.topk ? p.pair_pos[t * p.topk + lane] : -1;
     const uint32_t vmask = __ballot_sync(0xffffffffu, mine >= 0);
-    // the state GEMM2's fused reduce counts against: this token's pairs, and its slices not yet reduced
-    if (lane == 0) p.tpairs[t] = __popc(vmask);
-    for (int sl = lane; sl < p.slices; sl += 32) p.scnt[t * p.slices + sl] = 0;
     if (!vmask) continue;  // no local expert: nothing to copy
     int64_t local;
     const int r = row_of_token(p.desc, t, local);
@@ -590,13 +579,6 @@ struct Params {
   uint8_t* out_sf;         // GEMM1: scale atoms [m_cap/128][(N/2)/128][512]
   __nv_bfloat16* out_bf;   // GEMM2: [m_cap, N]
   uint32_t* tile_ctr;      // the job's tile counter of this GEMM (JobDesc::tiles)
-  // GEMM2's fused reduce (NULL scnt: the finalize kernel reduces): per (token, slice) counters, local pairs per
-  // token, the permutation, each message's reply segment
-  int32_t* scnt;
-  const int32_t* tpairs;
-  const int32_t* pair_pos;
-  __nv_bfloat16* reply_seg[kMaxJobRows];
-  int32_t topk, slices;
   int32_t P, N, K;
   float swiglu_limit;
   uint64_t status, timeout_ns;
@@ -639,90 +621,6 @@ __device__ __forceinline__ void store_rows_bf16x32(const uint32_t (&o)[16], uint
   __syncwarp();
 }
 
-// GEMM2's fused reduce.  The warp has just stored its 32 pair rows x 128 columns (slice 2 n_t + half of the reply
-// row) into y2.  Each stored row is counted on its token's slice; a token whose last local pair row of the slice
-// this was gets the slice reduced here and now -- the fp32 sum of its pair rows in ascending slot order rounded to
-// bf16, exactly finalize_reply_kernel's arithmetic -- and stored into its reply row (the A rank's ResultArena, peer
-// memory across GPUs).  So the reduce and the reply traffic overlap GEMM2's tensor work instead of following it.
-// Two tokens are reduced together, all their row loads in flight at once; the other tiles' rows are read with
-// ld.global.cg (never a stale L1 line of an earlier job).
-__device__ __forceinline__ void fused_reduce(const Params& p, int64_t row, bool valid, int n_t, int half, int lane) {
-  __threadfence();  // every lane's staged y2 stores of these rows are visible GPU-wide before they are counted
-  __syncwarp();
-  const int slice = n_t * 2 + half;
-  int32_t tok = -1;
-  bool last = false;
-  if (valid) {
-    tok = p.row_tok[row];
-    last = atomicAdd(&p.scnt[(int64_t)tok * p.slices + slice], 1) + 1 == p.tpairs[tok];
-  }
-  uint32_t pending = __ballot_sync(0xffffffffu, last);
-  if (!pending) return;
-  __threadfence();
-  const int64_t col = (int64_t)n_t * BN + half * 128 + lane * 4;  // this lane's 4 columns of the slice
-  constexpr int EV = 2;
-  while (pending) {
-    int32_t toks[EV], mine[EV], cnt[EV];
-    uint32_t vm[EV];
-    int ne = 0;
-#pragma unroll
-    for (int e = 0; e < EV; ++e) {
-      toks[e] = -1;
-      cnt[e] = 0;
-      mine[e] = -1;
-      vm[e] = 0;
-      if (pending) {  // warp-uniform
-        toks[e] = __shfl_sync(0xffffffffu, tok, __ffs(pending) - 1);
-        pending &= pending - 1;
-        mine[e] = lane < p.topk ? p.pair_pos[(int64_t)toks[e] * p.topk + lane] : -1;
-        vm[e] = __ballot_sync(0xffffffffu, mine[e] >= 0);
-        cnt[e] = __popc(vm[e]);
-        ne = e + 1;
-      }
-    }
-    uint2 v[EV][8];
-#pragma unroll
-    for (int e = 0; e < EV; ++e)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int32_t pos = __shfl_sync(0xffffffffu, mine[e], __fns(vm[e], 0, i + 1) & 31);
-        if (i < cnt[e]) v[e][i] = __ldcg(reinterpret_cast<const uint2*>(p.out_bf + (int64_t)pos * p.N + col));
-      }
-#pragma unroll
-    for (int e = 0; e < EV; ++e) {
-      if (e >= ne) break;
-      float a[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (i >= cnt[e]) break;
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[e][i]);
-        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-        a[0] += f0.x;
-        a[1] += f0.y;
-        a[2] += f1.x;
-        a[3] += f1.y;
-      }
-      for (int i = 8; i < cnt[e]; ++i) {  // more than 8 local experts of one token: the rest one by one
-        const int32_t pos = __shfl_sync(0xffffffffu, mine[e], __fns(vm[e], 0, i + 1) & 31);
-        const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p.out_bf + (int64_t)pos * p.N + col));
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-        a[0] += f0.x;
-        a[1] += f0.y;
-        a[2] += f1.x;
-        a[3] += f1.y;
-      }
-      int64_t local;
-      const int r = row_of_token(p.desc, toks[e], local);
-      uint2 o;
-      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
-      oh[0] = __floats2bfloat162_rn(a[0], a[1]);
-      oh[1] = __floats2bfloat162_rn(a[2], a[3]);
-      *reinterpret_cast<uint2*>(p.reply_seg[r] + local * p.N + col) = o;
-    }
-  }
-}
-
 // One epilogue warp's share of a finished 128 x 256 accumulator tile, already drained from TMEM into v: lane = row
 // `row` of quarter q, column half `half`.  EPI 0: h = silu(gate) * up quantised to MXFP8 (gate columns
 // [64 half, 64 half + 64) of the tile, up columns 128 further).  EPI 1: bf16(acc * w[row]) through the warp's 2 KB
@@ -746,7 +644,6 @@ __device__ __forceinline__ void epilogue_store(const Params& p, const uint32_t (
       }
       store_rows_bf16x32(o, wb, out0 + c * 32, p.N, valid_rows, lane);
     }
-    if (p.scnt) fused_reduce(p, row, valid, n_t, half, lane);
   } else {
     if (!valid) return;
     const int I = p.N / 2;
@@ -1004,13 +901,11 @@ struct FinalArgs {
   __nv_bfloat16* reply_seg[kMaxJobRows];  // each message's A ResultArena seg(f, slot) (peer memory across GPUs)
   uint32_t* reply_done[kMaxJobRows];      // each message's done flag (f, slot); NULL: no flag
   JobDesc* desc_rw;
-  int32_t fused;  // 1: GEMM2 reduced every token with local pairs (unless the job ran the weights-as-M GEMMs)
 };
 
 __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_constant__ FinalArgs p) {
   if (!p.desc->valid) return;
   const int n = p.desc->n;
-  const bool fused = p.fused && !p.desc->small;
   const int lane = threadIdx.x & 31;
   const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -1023,7 +918,6 @@ __global__ void __launch_bounds__(256) finalize_reply_kernel(const __grid_consta
     const int32_t mine = lane < p.topk ? p.pair_pos[t * p.topk + lane] : -1;
     const uint32_t vmask = __ballot_sync(0xffffffffu, mine >= 0);
     const int cnt = __popc(vmask);
-    if (fused && cnt) continue;    // its reply row came from GEMM2's epilogue; this kernel writes the zero rows
     const __nv_bfloat16* rowp[8];  // the first 8 rows, resolved once per token
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -1187,7 +1081,7 @@ static int ensure_gemm_attrs() {
 // K5b launch shared by both weight kinds; `mark` records the job's last timing event.
 template <class Mark>
 static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_t* B, int R,
-                    const asap_ffn_row_t* rows, cudaStream_t st, int sms, Mark& mark, int fused) {
+                    const asap_ffn_row_t* rows, cudaStream_t st, int sms, Mark& mark) {
   FinalArgs fa{};
   fa.desc = desc;
   fa.topk = L.topk;
@@ -1199,7 +1093,6 @@ static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_
     fa.reply_done[r] = (uint32_t*)rows[r].reply_done;
   }
   fa.desc_rw = desc;
-  fa.fused = fused;
   finalize_reply_kernel<<<sms * 4, 256, 0, st>>>(fa);
   ASAP_CHECK_LAUNCH("finalize_reply_kernel");
   mark(5);
@@ -1666,11 +1559,8 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::Cfg<1>::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
     ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<1>");
     mark(4);
-    return finalize(desc, L, pa, B, R, rows, st, sms, mark, 0);
+    return finalize(desc, L, pa, B, R, rows, st, sms, mark);
   }
-  qa.scnt = (int32_t*)(B + L.scnt);
-  qa.tpairs = (int32_t*)(B + L.tpairs);
-  qa.slices = L.slices;
   quant_permute_kernel<<<sms * 4, 256, 0, st>>>(qa);
   ASAP_CHECK_LAUNCH("quant_permute_kernel");
   mark(2);
@@ -1738,12 +1628,6 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.out_sf = nullptr;
   g2.out_bf = (__nv_bfloat16*)(B + L.y2);
   g2.tile_ctr = &desc->tiles[1];
-  g2.scnt = (int32_t*)(B + L.scnt);  // the reduce runs in GEMM2's epilogue
-  g2.tpairs = (const int32_t*)(B + L.tpairs);
-  g2.pair_pos = pa.pair_pos;
-  for (int r = 0; r < R; ++r) g2.reply_seg[r] = (__nv_bfloat16*)rows[r].reply_seg;
-  g2.topk = L.topk;
-  g2.slices = L.slices;
   g2.N = L.H;
   g2.K = L.I;
   if (token_major) {
@@ -1767,7 +1651,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   }
   mark(4);
 
-  return finalize(desc, L, pa, B, R, rows, st, sms, mark, 1);
+  return finalize(desc, L, pa, B, R, rows, st, sms, mark);
 }
 
 int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode) {
