@@ -304,12 +304,6 @@ typedef struct {
 int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t rows, const asap_ffn_row_t* row_views,
                       float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream);
 
-/* GEMM variant of the MXFP4 jobs on this workspace: 0 (default) token-major 128 x 256 tiles; 1 weights as the MMA's
- * M operand with N = 64 or 128 tokens per tile (less tensor work on padding for small messages; measured slower
- * than the default on this build, so opt-in); -1 chooses per job on the device (weights-as-M when the experts'
- * 128-row token blocks are on average less than half full). */
-int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode);
-
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
  * stream around its 5 stages (routing, quantise+permute, gemm1, gemm2, reduce+reply); last_timing waits
  * for the recorded jobs (the last 64 since enable) and returns each kernel's mean duration in ms (n >= 5). */

@@ -110,7 +110,6 @@ _SIGS = {
                                     c_void_p]),
     "asap_ffn_job": (c_int32, [c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_float,
                                c_uint64, c_uint64, c_void_p]),
-    "asap_ffn_set_small_mode": (c_int32, [c_uint64, c_int32]),
     "asap_ffn_enable_timing": (c_int32, [c_uint64, c_int32]),
     "asap_ffn_last_timing": (c_int32, [c_uint64, POINTER(c_float), c_int32]),
     "asap_ffn_job_info": (c_int32, [c_uint64, POINTER(c_int32), POINTER(c_int32), POINTER(c_uint32),

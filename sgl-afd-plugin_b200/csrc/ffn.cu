@@ -1,7 +1,7 @@
 // libasap F side: doorbell waits (one message, several joined messages, or the first ready one), the expert-major
 // permutation, activation quantisation (MXFP8, or FP8 per 1x128 for block-FP8 experts), the tcgen05 grouped GEMMs
 // with fused epilogues (MXFP8 x MXFP4 block-scaled here; FP8 x FP8 with block-scale promotion in gemm_fp8.cuh;
-// the opt-in weights-as-M variant in gemm_small.cuh), the weighted reduce that
+// the weighted reduce that
 // writes the replies straight into the A ranks' ResultArenas, and the CUDA-graph capture of whole jobs.
 //
 // Reference behaviour replaced here (python/sgl_asap_plugin/):
@@ -33,9 +33,8 @@ struct JobDesc {
   uint64_t t_seen;   // globaltimer (ns) when the doorbell wait saw the message (0: posted by the host)
   uint64_t t_reply;  // globaltimer (ns) when the reply's done flag was released
   int32_t rows;      // messages joined in this job (RowState entries after the descriptor)
-  int32_t small;     // 1: the GEMMs run weights-as-M (gemmT), for jobs whose 128-row blocks are mostly padding
   uint32_t tiles[2];  // next unclaimed tile of GEMM1 / GEMM2 (the GEMMs' dynamic tile scheduler), zeroed per job
-  uint32_t pad[2];
+  uint32_t pad[3];
 };
 static_assert(sizeof(JobDesc) == 64, "JobDesc is one cache line");
 
@@ -322,7 +321,6 @@ struct PermArgs {
   int32_t* row_tok;   // [m_cap]
   float* row_w;       // [m_cap]
   int32_t* hist;      // [kPermChunks][ASAP_MAX_LOCAL_EXPERTS] chunk histograms, then chunk bases
-  int32_t small_mode;  // -1: choose per job (blocks under half full on average); 0 / 1: never / always
 };
 
 __device__ __forceinline__ void perm_chunking(const PermArgs& p, int64_t& total, int64_t& chunk, int& chunks) {
@@ -352,8 +350,6 @@ __global__ void __launch_bounds__(256) route_count_kernel(const __grid_constant_
 
 __global__ void __launch_bounds__(ASAP_MAX_LOCAL_EXPERTS) route_scan_kernel(const __grid_constant__ PermArgs p) {
   __shared__ int32_t wsum[ASAP_MAX_LOCAL_EXPERTS / 32];
-  __shared__ int32_t pairs_total;
-  if (threadIdx.x == 0) pairs_total = 0;
   int64_t total, chunk;
   int chunks;
   perm_chunking(p, total, chunk, chunks);
@@ -395,13 +391,6 @@ __global__ void __launch_bounds__(ASAP_MAX_LOCAL_EXPERTS) route_scan_kernel(cons
     }
   }
   if (e == p.P - 1) p.mstart[p.P] = mst + tiles;
-  if (e < p.P && c) atomicAdd(&pairs_total, c);
-  __syncthreads();
-  if (e == p.P - 1) {  // GEMM variant of this job (both are launched; the other exits at once)
-    const int64_t blocks = mst + tiles;
-    JobDesc* d = const_cast<JobDesc*>(p.desc);
-    d->small = p.small_mode >= 0 ? p.small_mode : (2ll * pairs_total < blocks * 128 ? 1 : 0);
-  }
 }
 
 __global__ void __launch_bounds__(32) route_place_kernel(const __grid_constant__ PermArgs p) {
@@ -675,7 +664,6 @@ __device__ __forceinline__ void epilogue_store(const Params& p, const uint32_t (
 // EPI 0: h = silu(gate) * up, quantised to MXFP8 (GEMM1).  EPI 1: bf16(acc * w[row]) (GEMM2).
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_constant__ Params p) {
-  if (p.desc->valid && p.desc->small) return;  // the weights-as-M kernel (gemmT) runs this job
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -890,7 +878,6 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
 }  // namespace gemm
 
 #include "gemm_fp8.cuh"
-#include "gemm_small.cuh"
 
 // ------------------------------------------------------------------ K5b: weighted reduce + reply
 struct FinalArgs {
@@ -1028,7 +1015,6 @@ struct ExpertsHandle {
   asap_mxfp4_experts_t e;   // kMxfp4 (num_local/expert_base/hidden/inter filled for both kinds)
   asap_fp8_experts_t f8;    // kFp8Block
   CUtensorMap w13_map, w2_map;
-  CUtensorMap w13_map_t, w2_map_t;  // kMxfp4: 128-row boxes (weights-as-M kernels)
 };
 constexpr int kTimedKernels = 5;  // routing (count+scan+place), quantise+permute, gemm1, gemm2, finalize_reply
 constexpr int kTimedJobs = 64;     // ring of event sets: the last 64 jobs since timing was enabled
@@ -1037,7 +1023,6 @@ struct WsHandle {
   WsLayout L;
   CUtensorMap xq_map, hq_map;
   bool timing = false;
-  int small_mode = 0;  // PermArgs::small_mode (the weights-as-M kernels measured slower: opt-in)
   int jobs = 0;  // jobs recorded since enable
   cudaEvent_t ev[kTimedJobs][kTimedKernels + 1] = {};
 };
@@ -1070,10 +1055,6 @@ static int ensure_gemm_attrs() {
                                  gemm8::SMEM_BYTES));
   ASAP_CUDA(cudaFuncSetAttribute(gemm8::moe_gemm_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  gemm8::SMEM_BYTES));
-  ASAP_CUDA(cudaFuncSetAttribute(gemmT::moe_gemm_t_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 gemmT::SMEM_BYTES));
-  ASAP_CUDA(cudaFuncSetAttribute(gemmT::moe_gemm_t_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 gemmT::SMEM_BYTES));
   gemm_attr_set = true;
   return ASAP_OK;
 }
@@ -1130,12 +1111,6 @@ int asap_experts_register(const asap_mxfp4_experts_t* e, uint64_t* handle) {
   if (!rc)
     rc = make_tmap_2d(&h->w2_map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2, gemm::BK,
                       gemm::BN, "w2");
-  if (!rc)
-    rc = make_tmap_2d(&h->w13_map_t, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w13, H, P * 2 * I, H / 2,
-                      gemmT::BK, gemmT::BW, "w13 (128-row boxes)");
-  if (!rc)
-    rc = make_tmap_2d(&h->w2_map_t, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (const void*)e->w2, I, P * H, I / 2,
-                      gemmT::BK, gemmT::BW, "w2 (128-row boxes)");
   if (rc) {
     delete h;
     return rc;
@@ -1476,7 +1451,6 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   pa.row_tok = (int32_t*)(B + L.row_tok);
   pa.row_w = (float*)(B + L.row_w);
   pa.hist = (int32_t*)(B + L.hist);
-  pa.small_mode = eh->kind == kMxfp4 ? wh->small_mode : 0;
   const int slot_ev = wh->jobs % kTimedJobs;
   if (wh->timing) ++wh->jobs;
   auto mark = [&](int i) {
@@ -1585,37 +1559,8 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g1.swiglu_limit = swiglu_limit;
   g1.status = status;
   g1.timeout_ns = timeout_ns;
-  // Which GEMM pair runs is decided per job on the device (JobDesc::small) only in mode -1; in modes 0 / 1 the
-  // host launches just the token-major / weights-as-M kernels, so no launch exits without work.
-  const bool token_major = wh->small_mode != 1, weights_as_m = wh->small_mode != 0;
-  if (token_major) {
-    gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
-    ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
-  }
-  gemmT::Params t1;
-  memset(&t1, 0, sizeof(t1));
-  t1.tmap_w = eh->w13_map_t;
-  t1.tmap_x = wh->xq_map;
-  t1.sfw = g1.sfb;
-  t1.sfw_expert_stride = g1.sfb_expert_stride;
-  t1.sfx = g1.sfa;
-  t1.desc = desc;
-  t1.mstart = pa.mstart;
-  t1.ecnt = pa.ecnt;
-  t1.row_tok = pa.row_tok;
-  t1.row_w = pa.row_w;
-  t1.out_q = g1.out_q;
-  t1.out_sf = g1.out_sf;
-  t1.P = L.P;
-  t1.N = 2 * L.I;
-  t1.K = L.H;
-  t1.swiglu_limit = swiglu_limit;
-  t1.status = status;
-  t1.timeout_ns = timeout_ns;
-  if (weights_as_m) {
-    gemmT::moe_gemm_t_kernel<0><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t1);
-    ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<0>");
-  }
+  gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
+  ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
   mark(3);
 
   gemm::Params g2 = g1;
@@ -1630,38 +1575,11 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.tile_ctr = &desc->tiles[1];
   g2.N = L.H;
   g2.K = L.I;
-  if (token_major) {
-    gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
-    ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
-  }
-  gemmT::Params t2 = t1;
-  t2.tmap_w = eh->w2_map_t;
-  t2.tmap_x = wh->hq_map;
-  t2.sfw = g2.sfb;
-  t2.sfw_expert_stride = g2.sfb_expert_stride;
-  t2.sfx = g2.sfa;
-  t2.out_q = nullptr;
-  t2.out_sf = nullptr;
-  t2.out_bf = g2.out_bf;
-  t2.N = L.H;
-  t2.K = L.I;
-  if (weights_as_m) {
-    gemmT::moe_gemm_t_kernel<1><<<sms, gemmT::THREADS, gemmT::SMEM_BYTES, st>>>(t2);
-    ASAP_CHECK_LAUNCH("moe_gemm_t_kernel<1>");
-  }
+  gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
+  ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
   mark(4);
 
   return finalize(desc, L, pa, B, R, rows, st, sms, mark);
-}
-
-int asap_ffn_set_small_mode(uint64_t ws_handle, int32_t mode) {
-  WsHandle* w = get_ws(ws_handle);
-  if (!w || mode < -1 || mode > 1) {
-    set_error("asap_ffn_set_small_mode: unknown workspace handle or mode %d outside {-1, 0, 1}", mode);
-    return ASAP_EINVAL;
-  }
-  w->small_mode = mode;
-  return ASAP_OK;
 }
 
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable) {

@@ -40,7 +40,7 @@ class FfnHarness:
     """The F chain through the C ABI on plain torch buffers: x/ids/w as a RecvArena row, a reply segment and a
     done flag as an A rank's ResultArena would hold them."""
 
-    def __init__(self, experts: Mxfp4Experts, n_max: int, topk: int, small_mode: int = 0):
+    def __init__(self, experts: Mxfp4Experts, n_max: int, topk: int):
         self.e, self.n_max, self.topk = experts, n_max, topk
         nbytes = N.lib().asap_ffn_ws_bytes(n_max, topk, experts.num_local, experts.hidden, experts.inter)
         self._owner, self.ws = _aligned_empty(nbytes, "cuda")
@@ -48,7 +48,6 @@ class FfnHarness:
         N.call("asap_ffn_ws_register", self.ws.data_ptr(), n_max, topk, experts.num_local, experts.hidden,
                experts.inter, ctypes.byref(h))
         self.handle = h.value
-        N.call("asap_ffn_set_small_mode", self.handle, small_mode)
         self.status = torch.zeros(1, dtype=torch.int64, device="cuda")
         self.reply = torch.zeros(n_max, experts.hidden, dtype=torch.bfloat16, device="cuda")
         self.done = torch.zeros(16, dtype=torch.int32, device="cuda")

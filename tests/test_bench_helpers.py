@@ -107,6 +107,5 @@ def test_hbm_kernel_gbs():
 
 
 def test_f_job_launches():
-    """wait + route count/scan/place + quantise + GEMM1 + GEMM2 + reduce (+ gather for joined jobs): the
-    weights-as-M GEMMs are not launched in the default mode."""
+    """wait + route count/scan/place + quantise + GEMM1 + GEMM2 + reduce (+ gather for joined jobs)."""
     assert bench.f_job_launches() == 8 and bench.f_job_launches(4) == 9

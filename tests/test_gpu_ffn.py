@@ -161,44 +161,23 @@ def test_ffn_chain_deepseek_dims(cuda_ok):
 
 
 @pytest.mark.parametrize("n,k,P,H,I,e0", [
-    (64, 2, 4, 256, 128, 4),        # every expert in one block of <= 64 rows (MMA N = 64)
-    (300, 4, 6, 512, 256, 0),       # experts over 128 rows: N = 128 blocks and a tail block
+    (64, 2, 4, 256, 128, 4),        # every expert in one block of <= 64 rows
+    (300, 4, 6, 512, 256, 0),       # experts over 128 rows: full blocks and a tail block
     (64, 12, 16, 256, 128, 0),      # more than 8 local experts per token
-    (40, 8, 32, 1024, 512, 0),      # config-5-like: many experts, a handful of rows each
+    (40, 8, 32, 1024, 512, 0),      # config-5-like: many experts, a handful of rows each (mostly padding blocks)
 ])
-def test_ffn_chain_weights_as_m(cuda_ok, n, k, P, H, I, e0):
-    """The small-segment GEMMs (weights as the MMA's M operand, tokens as N = 64 / 128), forced on: the same
-    bit-exact routing / activation codes and the same tolerances as the token-major kernels."""
+def test_ffn_chain_small_segments(cuda_ok, n, k, P, H, I, e0):
+    """Small jobs (few rows per expert, most of each 128-row block padding): the bit-exact routing / activation
+    codes and the tolerances of the other chain tests."""
     rng = np.random.default_rng(n + 1000)
     e = Mxfp4Experts.random(P, H, I, expert_base=e0, seed=n + 3)
     gate, up, w2 = experts_to_oracle(e)
     x, ids, w = random_inputs(rng, n, H, k, e0 - 2, e0 + P + 2, bias_expert=e0)
-    h = FfnHarness(e, n_max=n, topk=k, small_mode=1)
+    h = FfnHarness(e, n_max=n, topk=k)
     h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), seq=23)
     check_chain(h, x, ids, w, gate, up, w2, e0, P)
     assert int(h.done[0].item()) == 23
     h.release()
-    e.release()
-
-
-def test_ffn_chain_variant_choice_same_answer(cuda_ok):
-    """Per-job choice (mode -1: a small job runs weights-as-M) against both forced variants: replies within the
-    tolerance of each other and of the oracle."""
-    rng = np.random.default_rng(77)
-    n, k, P, H, I = 48, 4, 16, 512, 256
-    e = Mxfp4Experts.random(P, H, I, seed=5)
-    gate, up, w2 = experts_to_oracle(e)
-    x, ids, w = random_inputs(rng, n, H, k, 0, P)
-    outs = []
-    for mode in (-1, 0, 1):
-        h = FfnHarness(e, n_max=n, topk=k, small_mode=mode)
-        h.run(bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
-        outs.append(np_from_bf16(h.reply[:n]))
-        h.release()
-    ref = moe.ffn_rank(x, ids, w, gate, up, w2, 0, P, act_quant=True)
-    for o in outs:
-        assert moe.rel_l2(o, ref) < TOL
-    np.testing.assert_array_equal(outs[0], outs[2])  # the automatic choice took weights-as-M here
     e.release()
 
 
