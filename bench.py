@@ -604,21 +604,27 @@ def _cpu_cores():
     return len(os.sched_getaffinity(0))
 
 
-def _dequant_first(experts, n_experts):
-    """Dequantised (gate, up, w2) fp32 numpy arrays of local experts [0, n_experts) of device-layout experts."""
+def _dequant_first(experts, n_experts, which=None):
+    """Dequantised (gate, up, w2) fp32 numpy arrays of local experts [0, n_experts) of device-layout experts, or of
+    the local experts listed in ``which`` (in that order)."""
+    import torch
+
     from oracle import moe
 
-    n = n_experts
+    idx = torch.arange(n_experts) if which is None else torch.as_tensor(list(which), dtype=torch.long)
+    n = len(idx)
+
+    def rows(t, P):
+        return t.view(P, -1).index_select(0, idx.to(t.device)).cpu().numpy()
+
     if getattr(experts, "kind", "mxfp4") == "fp8":
-        return moe.dequant_fp8(experts.w13[:n].cpu().numpy(), experts.w13_scale[:n].cpu().numpy(),
-                               experts.w2[:n].cpu().numpy(), experts.w2_scale[:n].cpu().numpy())
+        return moe.dequant_fp8(experts.w13.index_select(0, idx.to(experts.w13.device)).cpu().numpy(),
+                               experts.w13_scale.index_select(0, idx.to(experts.w13.device)).cpu().numpy(),
+                               experts.w2.index_select(0, idx.to(experts.w2.device)).cpu().numpy(),
+                               experts.w2_scale.index_select(0, idx.to(experts.w2.device)).cpu().numpy())
     P, Hh, Ii = experts.num_local, experts.hidden, experts.inter
-    w13 = experts.w13.view(P, -1)[:n].cpu().numpy()
-    sf13 = experts.w13_sf.view(P, -1)[:n].cpu().numpy()
-    w2 = experts.w2.view(P, -1)[:n].cpu().numpy()
-    sf2 = experts.w2_sf.view(P, -1)[:n].cpu().numpy()
-    gate, up = moe.dequant_w13(w13, sf13, n, Hh, Ii)
-    return gate, up, moe.dequant_w2(w2, sf2, n, Hh, Ii)
+    gate, up = moe.dequant_w13(rows(experts.w13, P), rows(experts.w13_sf, P), n, Hh, Ii)
+    return gate, up, moe.dequant_w2(rows(experts.w2, P), rows(experts.w2_sf, P), n, Hh, Ii)
 
 
 def _time_torch_cpu(x, ids, w, weights, n_experts, act, reps):
@@ -688,15 +694,18 @@ def cpu_baseline(n_experts=4, seed=0, steps=1, warmup=0, inputs=None):
             "config1": cpu_config1()}
 
 
-def check_single(x, ids, w, experts, sched, out, shared_out, n_experts=4, n_tokens=64, seed=0):
+def check_single(x, ids, w, experts, sched, out, shared_out, n_experts=4, n_tokens=64, seed=0, busiest=False):
     """Parity of the timed configuration (the CPU-baseline leg's check; oracle/ is the checker): the last step's
-    device buffers against the oracle on the benchmark's own inputs.
-      * routing: per-local-expert counts and the expert-major position of every (token, slot) pair, bit-exact
-        (all pairs of the step);
-      * experts [0, n_experts): MXFP8 activation codes + scales of their pairs bit-exact (config 2), and the
-        weighted GEMM2 rows within relative L2 1e-2 of the oracle's ffn_pairs;
-      * n_tokens sampled tokens: reply = fp32 sum of their pair rows in slot order and the combined output
-        (+ shared expert) bit-exact from the device's own pair rows.
+    device buffers against the oracle on the benchmark's own inputs.  ``experts`` / ``sched``: one F rank's, or
+    lists of them (F ranks of a loopback deployment in F order, contiguous expert ranges from 0).
+      * routing: per F rank, the per-local-expert counts and the expert-major position of every pair of the
+        tokens sent to it (in token order), bit-exact (all pairs of the step);
+      * F rank 0's local experts [0, n_experts) -- or, with ``busiest``, its n_experts experts with the most
+        pairs this step (skewed routing can leave the first ones empty): MXFP8 activation codes + scales of their
+        pairs bit-exact (MXFP4 layers), and the weighted GEMM2 rows within relative L2 1e-2 of the oracle's
+        ffn_pairs;
+      * n_tokens sampled tokens: every F rank's reply (fp32 sum of the token's pair rows in slot order) and the
+        combined output (+ shared expert) bit-exact from the device's own pair rows.
     -> (parity dict, inputs for cpu_baseline)."""
     import numpy as np
     import torch
@@ -704,49 +713,73 @@ def check_single(x, ids, w, experts, sched, out, shared_out, n_experts=4, n_toke
     from asap_b200.transport.server import _raw_bytes
     from oracle import moe, mx
 
+    ex_list = list(experts) if isinstance(experts, (list, tuple)) else [experts]
+    sc_list = list(sched) if isinstance(sched, (list, tuple)) else [sched]
     dev = x.device
     ids_np, w_np = ids.cpu().numpy(), w.cpu().numpy()
     T, k = ids_np.shape
-    P = experts.num_local
-    dbg = sched.debug_tensors()
-    counts = dbg["expert_counts"].cpu().numpy()
-    pos = dbg["pair_pos"][:T].cpu().numpy()
-    pos_ref, _, counts_ref = moe.expert_permutation(ids_np, experts.expert_base, P)
-    tables = bool(np.array_equal(counts, counts_ref) and np.array_equal(pos, pos_ref))
+    ids64 = ids_np.astype(np.int64)
+    tables, pairs = True, 0
+    per_f = []  # (tokens sent to F f, their compacted index, pair positions, y2 view)
+    for e_f, s_f in zip(ex_list, sc_list):
+        P, e0 = e_f.num_local, e_f.expert_base
+        sent = np.any((ids64 >= e0) & (ids64 < e0 + P), axis=1)
+        n_f = int(sent.sum())
+        dbg = s_f.debug_tensors()
+        pos_ref, _, counts_ref = moe.expert_permutation(ids_np[sent], e0, P)
+        counts = dbg["expert_counts"].cpu().numpy()
+        pos = dbg["pair_pos"][:n_f].cpu().numpy()
+        tables = tables and bool(np.array_equal(counts, counts_ref) and np.array_equal(pos, pos_ref))
+        pairs += int(counts_ref.sum())
+        rows = int(pos_ref.max()) + 1 if n_f else 1
+        y2 = _raw_bytes(dbg["y2"], rows * H * 2, dev.index).view(torch.bfloat16).view(rows, H)
+        per_f.append((sent, np.cumsum(sent) - 1, pos_ref, y2, dbg, rows))
     x_np = x.float().cpu().numpy()
-    weights = _dequant_first(experts, n_experts)
-    sel = np.any(ids_np < n_experts, axis=1)
+    experts0 = ex_list[0]
+    e00, P0 = experts0.expert_base, experts0.num_local
+    if busiest:
+        cnt0 = np.bincount(np.clip(ids64 - e00, -1, P0)[(ids64 >= e00) & (ids64 < e00 + P0)], minlength=P0)
+        which = sorted(np.argsort(-cnt0, kind="stable")[:n_experts].tolist())
+    else:
+        which = list(range(n_experts))
+    weights = _dequant_first(experts0, n_experts, which)
+    sent0, cidx0, pos0, y2_0, dbg0, rows0 = per_f[0]
+    sel = np.any(np.isin(ids64, e00 + np.asarray(which)), axis=1)
     tsel = np.nonzero(sel)[0]
-    y_ref, used = moe.ffn_pairs(x_np[sel], ids_np[sel], w_np[sel], *weights, 0, n_experts,
+    y_ref, used = moe.ffn_pairs(x_np[sel], ids_np[sel], w_np[sel], *weights, e00, P0, experts=which,
                                 act_quant="fp8" if KIND == "fp8" else True)
     tt, jj = np.nonzero(used)
-    prow = torch.from_numpy(pos_ref[tsel[tt], jj].astype(np.int64)).to(dev)
-    rows = int(pos_ref.max()) + 1
-    y2 = _raw_bytes(dbg["y2"], rows * H * 2, dev.index).view(torch.bfloat16).view(rows, H)
-    y_gpu = y2.index_select(0, prow).float().cpu().numpy()
+    prow = torch.from_numpy(pos0[cidx0[tsel[tt]], jj].astype(np.int64)).to(dev)
+    y_gpu = y2_0.index_select(0, prow).float().cpu().numpy()
     rel = moe.rel_l2(y_gpu, y_ref[tt, jj])
     act_ok = None
     if KIND == "mxfp4":
-        xq = _raw_bytes(dbg["xq"], rows * H, dev.index).view(rows, H).index_select(0, prow).cpu().numpy()
+        xq = _raw_bytes(dbg0["xq"], rows0 * H, dev.index).view(rows0, H).index_select(0, prow).cpu().numpy()
         kb = H // 32
-        sfb = _raw_bytes(dbg["xq_sf"], -(-rows // 128) * 128 * kb, dev.index).cpu().numpy()
+        sfb = _raw_bytes(dbg0["xq_sf"], -(-rows0 // 128) * 128 * kb, dev.index).cpu().numpy()
         pr = prow.cpu().numpy()[:, None]
         sf = sfb[mx.sf_atom_offset(pr, np.arange(kb)[None, :], kb)]
         q_ref, s_ref = mx.mx_quantize(x_np[tsel[tt]])
         act_ok = bool(np.array_equal(xq, q_ref) and np.array_equal(sf, s_ref))
     rng = np.random.default_rng(seed)
     toks = np.sort(rng.choice(T, size=min(n_tokens, T), replace=False))
-    tp = pos_ref[toks]
-    live = tp >= 0
-    gathered = y2.index_select(0, torch.from_numpy(np.where(live, tp, 0).reshape(-1).astype(np.int64)).to(dev))
-    y_tok = gathered.float().cpu().numpy().reshape(len(toks), k, H)
-    reply = moe.reduce_pairs(y_tok, live)
+    replies, row_of = [], []
+    for sent, cidx, pos_ref, y2, _, _ in per_f:
+        hit = sent[toks]
+        tp = np.full((len(toks), k), -1, np.int64)
+        if hit.any():
+            tp[hit] = pos_ref[cidx[toks[hit]]]
+        live = tp >= 0
+        gathered = y2.index_select(0, torch.from_numpy(np.where(live, tp, 0).reshape(-1).astype(np.int64)).to(dev))
+        replies.append(moe.reduce_pairs(gathered.float().cpu().numpy().reshape(len(toks), k, H), live))
+        row_of.append(np.where(hit, np.arange(len(toks)), -1).astype(np.int32))
     shared_rows = shared_out[toks].float().cpu().numpy() if shared_out is not None else None
-    want = moe.combine([reply], np.arange(len(toks))[None, :].astype(np.int32), len(toks), shared_rows)
+    want = moe.combine(replies, np.stack(row_of), len(toks), shared_rows)
     got = out[toks].float().cpu().numpy()
     combine_ok = bool(np.array_equal(got, want))
     parity = {"checked": "timed configuration, last step's buffers", "tables_bitexact": tables,
-              "pairs": int(counts_ref.sum()), "experts_checked": n_experts, "pairs_checked": int(len(tt)),
+              "f_ranks": len(per_f), "pairs": pairs, "experts_checked": [e00 + e for e in which],
+              "pairs_checked": int(len(tt)),
               "rel_l2": round(rel, 6), "tol": 1e-2, "act_codes_bitexact": act_ok,
               "tokens_checked": int(len(toks)), "reply_combine_bitexact": combine_ok,
               "pass": bool(tables and rel < 1e-2 and act_ok is not False and combine_ok)}
@@ -843,7 +876,8 @@ def run_sweep(args):
 
         def step():
             d = disp.dispatch(x, topk)
-            return disp.combine(d, shared=shared(x)), d.ticket
+            s_out = shared(x)
+            return disp.combine(d, shared=s_out), d.ticket, s_out
 
         for _ in range(args.warmup):
             step()
@@ -869,13 +903,13 @@ def run_sweep(args):
             f0_ms = dict(zip(("routing", "quantise_permute", "gemm1", "gemm2", "reduce_reply"),
                              [round(v, 4) for v in kms]))
         pairs_f = [int(sc.debug_tensors()["expert_counts"].sum().item()) for sc in lb.scheds]
-        busiest = max(range(n_f), key=lambda f: pairs_f[f])
-        roof = step_roofline(6.0 * H * I * pairs_f[busiest],
-                             (bounds[busiest + 1] - bounds[busiest]) * expert_bytes(), ms,
-                             f"step of the busiest F rank ({pairs_f[busiest]} pairs, its weights read once)")
+        # the four F ranks share this one GPU: the step's bound is all their pairs' FLOPs or all experts' bytes
+        roof = step_roofline(6.0 * H * I * sum(pairs_f), E * expert_bytes(), ms,
+                             f"step of all {n_f} F ranks on this GPU ({sum(pairs_f)} pairs, every expert's weights "
+                             "read once)")
         lat, busy, rows = [], [], None
         for _ in range(max(args.latency_iters, 1)):
-            _, ticket = step()
+            out, ticket, s_out = step()
             torch.cuda.synchronize()
             info = lb.channel.dispatch_info(ticket.slot, stream.cuda_stream)
             jobs = [sc.job_info(stream.cuda_stream) for sc in lb.scheds]
@@ -883,6 +917,8 @@ def run_sweep(args):
             lat.append((jobs[0]["t_seen_ns"] - info["t_ring_ns"]) * 1e-3)
             busy.append(sum(j["t_reply_ns"] - j["t_seen_ns"] for j in jobs) * 1e-9)
         lb.check()
+        # parity of this T on the last step's buffers (every F rank's tables and replies, F rank 0's busiest experts)
+        parity, _ = check_single(x, ids, w, [d[0] for d in per_f], lb.scheds, out, s_out, busiest=True)
         mean_f = sum(rows) / n_f
         line = {
             "metric": METRIC, "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
@@ -901,7 +937,7 @@ def run_sweep(args):
             "f_busy_ms_p50": round(statistics.median(busy) * 1e3, 4), "f0_kernels_ms": f0_ms,
             "weights_gb_read_per_step": round(E * (2 * I * H + H * I) * (0.5 + 1 / 32) / 1e9, 3),
             "e2e": None, "gpu_launches": args.steps * (4 + f_job_launches() * n_f), "roofline": roof,
-            "f_pairs": pairs_f, "cpu_baseline": None,
+            "f_pairs": pairs_f, "cpu_baseline": None, "parity": parity,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -982,7 +1018,7 @@ def run_stack(args):
 
             def feed():
                 torch.cuda.set_device(local)
-                for step in range(steps_total):
+                for step in range(steps_total + 1):  # + the parity step
                     for l in range(L):
                         for mb in range(2):
                             for a in range(n_a):
@@ -1004,15 +1040,20 @@ def run_stack(args):
         def norm(t):  # the RMSNorm in front of every DeepSeek MoE block (keeps the stack's activations bounded)
             return torch.nn.functional.rms_norm(t, (H,))
 
-        def step():
-            xs = x_in
+        def step(record=False):
+            xs, rec = x_in, None
             for l in range(L):
                 d0 = disps[l].dispatch(xs[0], topk[l][0], micro_batch=0)
                 s0 = shared(xs[0])
                 d1 = disps[l].dispatch(xs[1], topk[l][1], micro_batch=1)
                 s1 = shared(xs[1])
-                xs = [norm(disps[l].combine(d0, shared=s0)), norm(disps[l].combine(d1, shared=s1))]
-            return xs
+                c0 = disps[l].combine(d0, shared=s0)
+                n0 = norm(c0)
+                c1 = disps[l].combine(d1, shared=s1)
+                if record and l == L - 1:  # the last layer's second micro-batch: the F ranks' last job
+                    rec = (xs[1], topk[l][1], c1, s1)
+                xs = [n0, norm(c1)]
+            return (xs, rec) if record else xs
 
         for _ in range(args.warmup):
             step()
@@ -1030,6 +1071,10 @@ def run_stack(args):
         clocks_summary = clocks.summary()
         ms = t0.elapsed_time(t1) / args.steps
         finite = bool(torch.isfinite(out[0]).all().item() and torch.isfinite(out[1]).all().item())
+        # parity step: one more pass; the last layer's second micro-batch is checked below
+        _, rec = step(record=True)
+        torch.cuda.synchronize()
+    parity = None
     if world > 1:
         mt = torch.tensor([ms])
         dist.all_reduce(mt, op=dist.ReduceOp.MAX)
@@ -1039,8 +1084,27 @@ def run_stack(args):
         torch.cuda.synchronize()
         (sched if not is_a else channel).check()
         dist.barrier()
+        mine = None
+        if is_a:  # against a 1-GPU loopback twin of the last layer (its experts regenerated from the F seeds)
+            xr, tk, cr, sr = rec
+            counts = channel.dispatch_info(1, torch.cuda.current_stream().cuda_stream)["counts"]
+            mine = twin_check((xr, tk.topk_ids, tk.topk_weights, sr, cr, counts), bounds, dev, local,
+                              seed_base=100 + 10 * (L - 1))
+        parities = [None] * world
+        dist.all_gather_object(parities, mine)
+        parities = [p for p in parities if p is not None]
+        parity = {"mode": "last layer, micro-batch 1 of the parity step: each A replica's output and per-F row "
+                          "counts against a 1-GPU loopback twin of that layer (same experts, same tokens), byte "
+                          "for byte", "replicas": len(parities),
+                  "output_bitexact": all(p["output_bitexact"] for p in parities),
+                  "tables_bitexact": all(p["tables_bitexact"] for p in parities),
+                  "counts_match_routing": all(p["counts_match_routing"] for p in parities),
+                  "pass": all(p["pass"] for p in parities)}
     else:
         lb.check()
+        xr, tk, cr, sr = rec
+        parity, _ = check_single(xr, tk.topk_ids, tk.topk_weights, layers[L - 1], lb.sched, cr, sr)
+        parity["checked"] = "last layer, micro-batch 1 of the parity step (the F rank's last job)"
     if rank == 0:
         line = {
             "metric": "MoE layer-stack tokens/s A->F->A (8 DeepSeek-V3-shape MXFP4 layers, 2 micro-batches)",
@@ -1058,7 +1122,7 @@ def run_stack(args):
                 6.0 * H * I * L * n_a * T * K_TOP * max(bounds[f + 1] - bounds[f] for f in range(n_f)) / E,
                 L * max(bounds[f + 1] - bounds[f] for f in range(n_f)) * expert_bytes(), ms,
                 "stack step of the busiest F rank (uniform routing: its share of every layer's pairs)"),
-            "cpu_baseline": None, "clocks": clocks_summary,
+            "cpu_baseline": None, "parity": parity, "clocks": clocks_summary,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1089,12 +1153,12 @@ def expert_bounds(num_f):
     return [(f * E) // num_f for f in range(num_f + 1)]
 
 
-def twin_check(check, bounds, dev, local):
+def twin_check(check, bounds, dev, local, seed_base=100):
     """An A replica's parity-step output against a 1-GPU loopback twin: the same experts (regenerated from the F
     ranks' seeds on this GPU), the same tokens, routing and shared-expert rows, one F scheduler per F rank over the
     same transport.  The kernels are deterministic, so the combined output and the per-F row counts must match
     byte for byte; the counts are also checked against the routing itself (tokens with an expert in each F rank's
-    range)."""
+    range).  F rank f's experts are regenerated from seed ``seed_base + f``."""
     import torch
 
     from asap_b200.dispatcher import AsapBuffer, AsapDispatcher
@@ -1104,7 +1168,7 @@ def twin_check(check, bounds, dev, local):
 
     x, ids, w, s, out, counts = check
     T, n_f = x.shape[0], len(bounds) - 1
-    per_f = [{0: make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + f, dev)} for f in range(n_f)]
+    per_f = [{0: make_experts(bounds[f + 1] - bounds[f], bounds[f], seed_base + f, dev)} for f in range(n_f)]
     lb = Loopback(Geometry(1, 1, 1, T, H, K_TOP, n_f), per_f, device=local, timeout_s=30.0)
     prev = AsapBuffer._buffer
     lb.install()

@@ -312,7 +312,7 @@ struct CombineArgs {
   uint64_t status, timeout_ns;
 };
 
-__global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ CombineArgs p) {
+__global__ void __launch_bounds__(256, 2) combine_kernel(const __grid_constant__ CombineArgs p) {
   const asap_geometry_t& g = p.g;
   const int F = g.num_f;
   const Offsets o = offsets_of(g);
@@ -322,40 +322,61 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ Co
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int H = g.hidden;
   const int nvec = H / 8;  // 8 bf16 per 16-byte vector
+  constexpr int U = 4;  // 16-byte vectors per lane per pass: every load of a pass is issued before its first use
   for (int64_t t = gwarp; t < p.n; t += nwarps) {
     int32_t rows[ASAP_MAX_F];
     for (int f = 0; f < F; ++f) rows[f] = row_of[(int64_t)f * g.n_max + t];
-    for (int c = lane; c < nvec; c += 32) {
-      float acc[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int f = 0; f < F; ++f) {
-        if (rows[f] < 0) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(p.result + seg_off(g, o, f, p.slot) +
-                                                        (uint64_t)rows[f] * H * 2 + (uint64_t)c * 16);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 ff = __bfloat1622float2(h[i]);
-          acc[2 * i] += ff.x;
-          acc[2 * i + 1] += ff.y;
-        }
-      }
-      uint4 r;
-      __nv_bfloat162* rh = reinterpret_cast<__nv_bfloat162*>(&r);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) rh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    for (int c0 = lane; c0 < nvec; c0 += 32 * U) {
+      uint4 sv[U];
       if (p.shared) {
-        const uint4 s = *reinterpret_cast<const uint4*>(p.shared + (uint64_t)t * H + (uint64_t)c * 8);
-        const __nv_bfloat162* sh = reinterpret_cast<const __nv_bfloat162*>(&s);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 a = __bfloat1622float2(rh[i]);
-          const float2 b = __bfloat1622float2(sh[i]);
-          rh[i] = __floats2bfloat162_rn(a.x + b.x, a.y + b.y);
+        for (int u = 0; u < U; ++u)
+          if (c0 + 32 * u < nvec)
+            sv[u] = *reinterpret_cast<const uint4*>(p.shared + (uint64_t)t * H + (uint64_t)(c0 + 32 * u) * 8);
+      }
+      float acc[U][8];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
+      for (int f = 0; f < F; ++f) {  // fp32 sum over F ranks in rank order
+        if (rows[f] < 0) continue;
+        const uint8_t* src = p.result + seg_off(g, o, f, p.slot) + (uint64_t)rows[f] * H * 2;
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (c0 + 32 * u < nvec) v[u] = *reinterpret_cast<const uint4*>(src + (uint64_t)(c0 + 32 * u) * 16);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (c0 + 32 * u >= nvec) continue;
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 ff = __bfloat1622float2(h[i]);
+            acc[u][2 * i] += ff.x;
+            acc[u][2 * i + 1] += ff.y;
+          }
         }
       }
-      *reinterpret_cast<uint4*>(p.out + (uint64_t)t * H + (uint64_t)c * 8) = r;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= nvec) continue;
+        uint4 r;
+        __nv_bfloat162* rh = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rh[i] = __floats2bfloat162_rn(acc[u][2 * i], acc[u][2 * i + 1]);
+        if (p.shared) {  // the shared expert is added to the bf16 sum, rounded again (two roundings)
+          const __nv_bfloat162* sh = reinterpret_cast<const __nv_bfloat162*>(&sv[u]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 a = __bfloat1622float2(rh[i]);
+            const float2 b = __bfloat1622float2(sh[i]);
+            rh[i] = __floats2bfloat162_rn(a.x + b.x, a.y + b.y);
+          }
+        }
+        *reinterpret_cast<uint4*>(p.out + (uint64_t)t * H + (uint64_t)c * 8) = r;
+      }
     }
   }
 }
@@ -780,8 +801,8 @@ int asap_combine(const asap_geometry_t* g, int32_t slot, uint32_t seq, int32_t n
   wait_replies_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, slot, seq, (const uint8_t*)result, status, timeout_ns,
                                                           reinterpret_cast<uint64_t*>(route_ws + kWsRing + 8));
   ASAP_CHECK_LAUNCH("wait_replies_kernel");
-  const int warps = 8;
-  int blocks = std::min((n + warps - 1) / warps, sm_count() * 4);
+  const int warps = 8;  // one token per warp; two CTAs of 8 warps per SM, one wave
+  int blocks = std::min((n + warps - 1) / warps, sm_count() * 2);
   combine_kernel<<<blocks, warps * 32, 0, (cudaStream_t)stream>>>(p);
   ASAP_CHECK_LAUNCH("combine_kernel");
   return ASAP_OK;
