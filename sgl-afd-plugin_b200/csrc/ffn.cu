@@ -348,49 +348,60 @@ __global__ void __launch_bounds__(256) route_count_kernel(const __grid_constant_
   for (int i = threadIdx.x; i < p.P; i += blockDim.x) p.hist[(int64_t)blockIdx.x * ASAP_MAX_LOCAL_EXPERTS + i] = h[i];
 }
 
-__global__ void __launch_bounds__(ASAP_MAX_LOCAL_EXPERTS) route_scan_kernel(const __grid_constant__ PermArgs p) {
+// One CTA: every chunk histogram is staged in shared memory with coalesced loads (one round trip instead of one
+// per chunk), each expert's thread (threads < P) sums its column and turns it into chunk bases in place, the
+// tile-aligned expert starts come from a block scan, and the bases go back with coalesced stores.
+constexpr int kScanThreads = 1024;
+constexpr int kScanSmemBytes = kPermChunks * ASAP_MAX_LOCAL_EXPERTS * 4;
+__global__ void __launch_bounds__(kScanThreads) route_scan_kernel(const __grid_constant__ PermArgs p) {
+  extern __shared__ int32_t sh[];  // [chunks][P]
   __shared__ int32_t wsum[ASAP_MAX_LOCAL_EXPERTS / 32];
   int64_t total, chunk;
   int chunks;
   perm_chunking(p, total, chunk, chunks);
+  const int P = p.P;
+  const int cells = chunks * P;
+  for (int i = threadIdx.x; i < cells; i += kScanThreads) {
+    const int g = i / P, e = i - g * P;
+    sh[i] = p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + e];
+  }
+  __syncthreads();
   const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
   int32_t c = 0;
-  if (e < p.P) {
-#pragma unroll 8
-    for (int g = 0; g < chunks; ++g) c += p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + e];
-  }
-  const int32_t tiles = (e < p.P) ? (c + 127) / 128 : 0;
-  int32_t v = tiles;  // block exclusive scan of tiles over experts
+  if (e < P)
+    for (int g = 0; g < chunks; ++g) c += sh[g * P + e];
+  const int32_t tiles = (e < P) ? (c + 127) / 128 : 0;
+  int32_t v = tiles;  // exclusive scan of tiles over experts (warps 0..7 hold experts 0..255)
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
     const int32_t u = __shfl_up_sync(0xffffffffu, v, d);
     if (lane >= d) v += u;
   }
-  if (lane == 31) wsum[warp] = v;
+  if (lane == 31 && warp < ASAP_MAX_LOCAL_EXPERTS / 32) wsum[warp] = v;
   __syncthreads();
   int32_t before = 0;
-  for (int w = 0; w < warp; ++w) before += wsum[w];
+  for (int w = 0; w < warp && w < ASAP_MAX_LOCAL_EXPERTS / 32; ++w) before += wsum[w];
   const int32_t mst = before + v - tiles;
-  if (e < p.P) {
+  if (e < P) {
     p.ecnt[e] = c;
     p.mstart[e] = mst;
     int32_t base = mst * 128;
-    for (int g0 = 0; g0 < chunks; g0 += 8) {  // chunk bases, in place; 8 loads in flight
-      int32_t t[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) t[i] = (g0 + i < chunks) ? p.hist[(int64_t)(g0 + i) * ASAP_MAX_LOCAL_EXPERTS + e] : 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (g0 + i < chunks) p.hist[(int64_t)(g0 + i) * ASAP_MAX_LOCAL_EXPERTS + e] = base;
-        base += t[i];
-      }
+    for (int g = 0; g < chunks; ++g) {  // chunk bases, in place
+      const int32_t t = sh[g * P + e];
+      sh[g * P + e] = base;
+      base += t;
     }
     for (int32_t r = base; r < (mst + tiles) * 128; ++r) {  // padding rows: no token
       p.row_tok[r] = -1;
       p.row_w[r] = 0.f;
     }
+    if (e == P - 1) p.mstart[P] = mst + tiles;
   }
-  if (e == p.P - 1) p.mstart[p.P] = mst + tiles;
+  __syncthreads();
+  for (int i = threadIdx.x; i < cells; i += kScanThreads) {
+    const int g = i / P, e2 = i - g * P;
+    p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + e2] = sh[i];
+  }
 }
 
 __global__ void __launch_bounds__(32) route_place_kernel(const __grid_constant__ PermArgs p) {
@@ -404,25 +415,38 @@ __global__ void __launch_bounds__(32) route_place_kernel(const __grid_constant__
   __syncwarp();
   const uint32_t lt_mask = (1u << lane) - 1u;
   const int64_t q0 = blockIdx.x * chunk, q1 = min(total, q0 + chunk);
-  for (int64_t qb = q0; qb < q1; qb += 32) {
-    const int64_t q = qb + lane;
-    int e = -1;
-    if (q < q1) {
-      e = p.ids[q] - p.expert_base;
-      if (e < 0 || e >= p.P) e = -1;
+  constexpr int U = 8;  // 32-pair steps whose ids / weights are loaded together (one round trip per U steps)
+  for (int64_t qs = q0; qs < q1; qs += 32 * U) {
+    int eu[U];
+    float wu[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t q = qs + 32 * u + lane;
+      eu[u] = -1;
+      wu[u] = 0.f;
+      if (q < q1) {
+        const int e = p.ids[q] - p.expert_base;
+        eu[u] = (e >= 0 && e < p.P) ? e : -1;
+        wu[u] = p.w[q];
+      }
     }
-    const uint32_t active = __ballot_sync(0xffffffffu, e >= 0);
-    const uint32_t peers = __match_any_sync(0xffffffffu, e) & active;
-    int32_t pos = -1;
-    if (e >= 0) pos = off[e] + __popc(peers & lt_mask);
-    __syncwarp();
-    if (e >= 0 && (peers & lt_mask) == 0) off[e] += __popc(peers);
-    __syncwarp();
-    if (q < q1) {
-      p.pair_pos[q] = pos;
-      if (pos >= 0) {
-        p.row_tok[pos] = (int32_t)(q / p.topk);
-        p.row_w[pos] = p.w[q];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {  // the steps in pair order: positions as with one step at a time
+      const int64_t q = qs + 32 * u + lane;
+      const int e = eu[u];
+      const uint32_t active = __ballot_sync(0xffffffffu, e >= 0);
+      const uint32_t peers = __match_any_sync(0xffffffffu, e) & active;
+      int32_t pos = -1;
+      if (e >= 0) pos = off[e] + __popc(peers & lt_mask);
+      __syncwarp();
+      if (e >= 0 && (peers & lt_mask) == 0) off[e] += __popc(peers);
+      __syncwarp();
+      if (q < q1) {
+        p.pair_pos[q] = pos;
+        if (pos >= 0) {
+          p.row_tok[pos] = (int32_t)(q / p.topk);
+          p.row_w[pos] = wu[u];
+        }
       }
     }
   }
@@ -499,14 +523,28 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const __grid_constan
       // first lane (kblocks is a multiple of 4, so a group is all active or all inactive)
       const uint32_t word = sb | (__shfl_down_sync(0xffffffffu, sb, 1) << 8) |
                             (__shfl_down_sync(0xffffffffu, sb, 2) << 16) | (__shfl_down_sync(0xffffffffu, sb, 3) << 24);
+      // codes regrouped so that each store instruction writes 512 contiguous bytes: in half h, lane j stores the
+      // 16-byte unit j of blocks [kb0 + 16 h, kb0 + 16 h + 16) (block 16 h + j / 2, its low or high 16 bytes)
+      uint4 unit[2];
+      bool unit_act[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int src = 16 * h + (lane >> 1);
+        const uint4 l2 = make_uint4(__shfl_sync(0xffffffffu, lo.x, src), __shfl_sync(0xffffffffu, lo.y, src),
+                                    __shfl_sync(0xffffffffu, lo.z, src), __shfl_sync(0xffffffffu, lo.w, src));
+        const uint4 h2 = make_uint4(__shfl_sync(0xffffffffu, hi.x, src), __shfl_sync(0xffffffffu, hi.y, src),
+                                    __shfl_sync(0xffffffffu, hi.z, src), __shfl_sync(0xffffffffu, hi.w, src));
+        unit[h] = (lane & 1) ? h2 : l2;
+        unit_act[h] = kb0 + src < kblocks;
+      }
       for (uint32_t m = vmask; m; m &= m - 1) {
         const int32_t row = __shfl_sync(0xffffffffu, mine, __ffs(m) - 1);
-        if (act) {
-          uint4* dst = reinterpret_cast<uint4*>(p.xq + (int64_t)row * H + (int64_t)kb * 32);
-          dst[0] = lo;
-          dst[1] = hi;
-          if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(p.xq_sf + sf_atom_off(row, kb, kblocks)) = word;
-        }
+        uint4* dst = reinterpret_cast<uint4*>(p.xq + (int64_t)row * H + (int64_t)kb0 * 32);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (unit_act[h]) dst[32 * h + lane] = unit[h];
+        if (act && (lane & 3) == 0)
+          *reinterpret_cast<uint32_t*>(p.xq_sf + sf_atom_off(row, kb, kblocks)) = word;
       }
     }
   }
@@ -1055,6 +1093,7 @@ static int ensure_gemm_attrs() {
                                  gemm8::SMEM_BYTES));
   ASAP_CUDA(cudaFuncSetAttribute(gemm8::moe_gemm_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  gemm8::SMEM_BYTES));
+  ASAP_CUDA(cudaFuncSetAttribute(route_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmemBytes));
   gemm_attr_set = true;
   return ASAP_OK;
 }
@@ -1477,7 +1516,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   }
   route_count_kernel<<<kPermChunks, 256, 0, st>>>(pa);
   ASAP_CHECK_LAUNCH("route_count_kernel");
-  route_scan_kernel<<<1, ASAP_MAX_LOCAL_EXPERTS, 0, st>>>(pa);
+  route_scan_kernel<<<1, kScanThreads, kScanSmemBytes, st>>>(pa);
   ASAP_CHECK_LAUNCH("route_scan_kernel");
   route_place_kernel<<<kPermChunks, 32, 0, st>>>(pa);
   ASAP_CHECK_LAUNCH("route_place_kernel");
