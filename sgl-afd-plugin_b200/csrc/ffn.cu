@@ -348,22 +348,32 @@ __global__ void __launch_bounds__(256) route_count_kernel(const __grid_constant_
   for (int i = threadIdx.x; i < p.P; i += blockDim.x) p.hist[(int64_t)blockIdx.x * ASAP_MAX_LOCAL_EXPERTS + i] = h[i];
 }
 
-// One CTA: every chunk histogram is staged in shared memory with coalesced loads (one round trip instead of one
-// per chunk), each expert's thread (threads < P) sums its column and turns it into chunk bases in place, the
-// tile-aligned expert starts come from a block scan, and the bases go back with coalesced stores.
+// One CTA: every chunk histogram is staged in shared memory with coalesced loads (eight in flight per thread), each
+// expert's thread (threads < P) sums its column and turns it into chunk bases in place, the tile-aligned expert
+// starts come from a block scan, and the bases and the padding rows go out with coalesced stores (a warp per
+// expert for the padding: one thread storing its expert's padding rows alone made every warp store touch 32 lines).
 constexpr int kScanThreads = 1024;
 constexpr int kScanSmemBytes = kPermChunks * ASAP_MAX_LOCAL_EXPERTS * 4;
 __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(const __grid_constant__ PermArgs p) {
   extern __shared__ int32_t sh[];  // [chunks][P]
   __shared__ int32_t wsum[ASAP_MAX_LOCAL_EXPERTS / 32];
+  __shared__ int32_t pad_lo[ASAP_MAX_LOCAL_EXPERTS], pad_hi[ASAP_MAX_LOCAL_EXPERTS];
   int64_t total, chunk;
   int chunks;
   perm_chunking(p, total, chunk, chunks);
   const int P = p.P;
   const int cells = chunks * P;
-  for (int i = threadIdx.x; i < cells; i += kScanThreads) {
-    const int g = i / P, e = i - g * P;
-    sh[i] = p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + e];
+  for (int i0 = threadIdx.x; i0 < cells; i0 += kScanThreads * 8) {  // eight loads in flight per thread
+    int32_t t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kScanThreads;
+      const int g = i / P;
+      t[u] = i < cells ? p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + (i - g * P)] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * kScanThreads < cells) sh[i0 + u * kScanThreads] = t[u];
   }
   __syncthreads();
   const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
@@ -391,13 +401,16 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(const __grid_c
       sh[g * P + e] = base;
       base += t;
     }
-    for (int32_t r = base; r < (mst + tiles) * 128; ++r) {  // padding rows: no token
-      p.row_tok[r] = -1;
-      p.row_w[r] = 0.f;
-    }
+    pad_lo[e] = base;  // padding rows of the expert's last tile: [base, (mst + tiles) * 128)
+    pad_hi[e] = (mst + tiles) * 128;
     if (e == P - 1) p.mstart[P] = mst + tiles;
   }
   __syncthreads();
+  for (int x = warp; x < P; x += kScanThreads / 32)  // padding rows: no token (a warp per expert, coalesced)
+    for (int32_t r = pad_lo[x] + lane; r < pad_hi[x]; r += 32) {
+      p.row_tok[r] = -1;
+      p.row_w[r] = 0.f;
+    }
   for (int i = threadIdx.x; i < cells; i += kScanThreads) {
     const int g = i / P, e2 = i - g * P;
     p.hist[(int64_t)g * ASAP_MAX_LOCAL_EXPERTS + e2] = sh[i];
