@@ -17,7 +17,7 @@ from asap_b200 import args as asap_args
 from asap_b200.dispatcher import AsapBuffer
 from asap_b200.layer import AsapMoE
 from asap_b200.transport import channel as channel_mod
-from asap_b200.transport.layout import Geometry, HandshakeError
+from asap_b200.transport.layout import HandshakeError
 from asap_b200.transport.server import FfnServer
 from host_mem import HostMem
 

@@ -5,7 +5,6 @@ into the A rank's ResultArena, reconnect -- with a host-memory stand-in for the 
 stores are emulated by plain host stores of the same words at the same offsets)."""
 
 import ctypes
-import mmap
 import os
 import socket
 import tempfile
