@@ -1481,17 +1481,17 @@ def run_multi(args):
     else:
         sched.check()
     dist.barrier()
-    # NVLink rates: every replica sends one message at a time (all replicas at once, F ranks idle and already
-    # waiting), CUDA events around each A rank's dispatch and the F ranks' per-stage timing of their replies; then
-    # a copy-engine write of 256 MB from each A rank into one F rank's unused slot-1 region (the link rate the
-    # roofline uses)
+    # NVLink rates, at the largest token count of the run: every replica sends one message at a time (all replicas
+    # at once, F ranks idle and already waiting), CUDA events around each A rank's dispatch and the F ranks'
+    # per-stage timing of their replies; then a copy-engine write of 256 MB from each A rank into one F rank's
+    # unused slot-1 region (the link rate the roofline uses)
     seq_a = phases * steps_per_phase + 1 + (lat_iters if a_idx == 0 else 0)  # the replica's last message
     seqs = [None] * world
     dist.all_gather_object(seqs, seq_a if is_a else None)
     seqs = [seqs[r] for r in a_ranks]
     link = measure_links(args, is_a, channel if is_a else None, sched if not is_a else None,
                          stream, send_stream if is_a else None, x_all if is_a else None, a_idx, n_a, n_f, a_ranks,
-                         f_ranks, seqs, rank, world, dev, T)
+                         f_ranks, seqs, rank, world, dev, T_max)
     if is_a:
         channel.check()
     else:
