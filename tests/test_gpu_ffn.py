@@ -77,6 +77,7 @@ def check_chain(h: FfnHarness, x, ids, w, gate, up, w2, e0, P, swiglu_limit=None
     (64, 2, 4, 256, 128, 4),       # one tile each way, non-zero expert base
     (300, 4, 6, 512, 256, 0),      # several experts > 128 rows, two n-tiles in GEMM1/GEMM2
     (64, 12, 16, 256, 128, 0),     # more than 8 local experts per token (the reduce's long path)
+    (8192, 8, 256, 256, 128, 0),   # the maximum of 256 local experts, 128 permutation chunks (config 2's routing)
 ])
 def test_ffn_chain_random_weights(cuda_ok, n, k, P, H, I, e0):
     rng = np.random.default_rng(n)
