@@ -756,7 +756,7 @@ static int dispatch_impl(const asap_geometry_t* g, int32_t a, int32_t slot, uint
     p.bell[f] = (uint64_t*)bells[f];
     p.epoch[f] = (uint32_t)epochs[f];
   }
-  // one warp per 8-row chunk: at most num_f * n / 8 + num_f chunks, and at most 4 CTAs of 8 warps per SM
+  // one warp per 4-row chunk: at most num_f * n / 4 + num_f chunks, and at most 4 CTAs of 8 warps per SM
   const int warps = 8;
   const int64_t chunks = ((int64_t)g->num_f * n + kPackRows - 1) / kPackRows + g->num_f;
   const int blocks = (int)std::min<int64_t>((chunks + warps - 1) / warps, (int64_t)sm_count() * 4);
