@@ -1322,7 +1322,8 @@ def run_multi(args):
         experts = make_experts(bounds[f + 1] - bounds[f], bounds[f], 100 + f, dev)
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
-        sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s, join=n_a if args.join_replicas else 1)
+        sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s,
+                             join=n_a if (args.join_replicas or args.first_then_rest) else 1)
         ep = ("127.0.0.1", server.port)
     eps = [None] * world
     dist.all_gather_object(eps, ep)
@@ -1344,6 +1345,10 @@ def run_multi(args):
                         sched.run_graph(msgs, 0, stream.cuda_stream)
                     else:
                         sched.run_device_wait_rows(msgs, 0, stream.cuda_stream)
+                    continue
+                if args.first_then_rest and n_a > 1:  # the first ready message alone, then the rest together
+                    sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream)
+                    sched.run_device_wait_rest([(a, 0, s + 1) for a in range(n_a)], 0, stream.cuda_stream)
                     continue
                 if args.any_order:  # each job answers whichever replica's message is ready first (round robin)
                     for _ in range(n_a):
@@ -1504,8 +1509,9 @@ def run_multi(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE[KIND], "data": "synthetic",
             "gpu_launches": args.steps * (4 * n_a +
-                                          (f_job_launches(n_a) if args.join_replicas else f_job_launches() * n_a)
-                                          * n_f), "roofline": None,  # set per line below
+                                          (f_job_launches(n_a) if args.join_replicas else
+                                           f_job_launches() + f_job_launches(n_a) if args.first_then_rest and n_a > 1
+                                           else f_job_launches() * n_a) * n_f), "roofline": None,  # set per line below
             "cpu_baseline": None,
             "clocks": clock_summary,
         }
@@ -1523,6 +1529,8 @@ def run_multi(args):
                 "expert_bounds": bounds, "routing": args.routing,
                 "placement": args.placement, "a_ranks": a_ranks,
                 "f_jobs": ("one joined job per step (all replicas' messages)" if args.join_replicas else
+                           "two jobs per step: the first ready message alone, then the step's other messages joined"
+                           if args.first_then_rest and n_a > 1 else
                            "one job per message" + (", first ready replica first (round robin on the device)"
                                                     if args.any_order else ""))
                           + (", CUDA-graph replays" if args.graphs else ""), "host_binding": binding,
@@ -1613,6 +1621,9 @@ def main():
     ap.add_argument("--no-numa-bind", action="store_true", help="N>1: do not bind ranks to their GPU's NUMA node")
     ap.add_argument("--join-replicas", action="store_true",
                     help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
+    ap.add_argument("--first-then-rest", action="store_true",
+                    help="N>1: each F rank answers the first ready message of a step alone (asap_ffn_wait_any), then "
+                         "the step's other messages with one joined job (asap_ffn_wait_rest)")
     args = ap.parse_args()
     layer = LAYERS["fp8-layer" if args.workload == "fp8-layer" else "layer"]
     globals().update(layer)

@@ -273,6 +273,17 @@ int asap_ffn_wait_any(uint64_t ws_handle, int32_t rows, const uint64_t* bells, c
                       const int32_t* expect_epochs, int32_t n_max, uint64_t rr_state, uint64_t status,
                       uint64_t timeout_ns, void* stream);
 
+/* Answer every message of this round not answered yet: row r is left out when its sequence word (as in
+ * asap_ffn_wait_state) already reached round_seqs[r] -- typically taken by an asap_ffn_wait_any job before it --
+ * and every other row's next message is awaited and joined into one job (row states in row order, each row's view
+ * its index: pass asap_ffn_job_rows all `rows` views).  A job with no row left is empty: not valid, no error, no
+ * reply.  With the reference's one-message-at-a-time poll (server.py:262-294) an F rank serving several A replicas
+ * runs one job per message; answering the first ready message alone and the rest of the round together starts as
+ * early and runs the remaining messages as one larger job. */
+int asap_ffn_wait_rest(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,
+                       const uint32_t* round_seqs, const int32_t* expect_epochs, int32_t n_max, uint64_t status,
+                       uint64_t timeout_ns, void* stream);
+
 /* CUDA graphs of F chains (the analogue of the reference's FfnCudaGraphRunner, srt/model_executor/runner/
  * ffn_cuda_graph_runner.py:75-92, here with no host copy into static buffers: the chain sizes itself on the
  * device).  asap_graph_begin starts capturing `stream` (thread-local mode): the asap_* launches on it until

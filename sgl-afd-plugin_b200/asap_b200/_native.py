@@ -100,6 +100,8 @@ _SIGS = {
                                       c_uint64, c_uint64, c_void_p]),
     "asap_ffn_wait_any": (c_int32, [c_uint64, c_int32, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_int32), c_int32,
                                     c_uint64, c_uint64, c_uint64, c_void_p]),
+    "asap_ffn_wait_rest": (c_int32, [c_uint64, c_int32, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint32),
+                                     POINTER(c_int32), c_int32, c_uint64, c_uint64, c_void_p]),
     "asap_graph_begin": (c_int32, [c_void_p]),
     "asap_graph_end": (c_int32, [c_void_p, POINTER(c_uint64)]),
     "asap_graph_launch": (c_int32, [c_uint64, c_void_p]),

@@ -285,6 +285,39 @@ class FfnScheduler:
             enqueue(stream)
         self.layer_calls[layer_id] += 1
 
+    def run_device_wait_rest(self, messages, layer_id: int, stream: int) -> None:
+        """One joined job over the messages of this round not answered yet, ``messages`` = [(a, slot, seq), ...]
+        with ``seq`` each source's message of the round: a source whose device sequence word already reached it
+        (answered by an earlier run_device_wait_any job) is left out on the device (asap_ffn_wait_rest), the others'
+        doorbells are awaited and their messages answered by one chain.  Enqueued after one run_device_wait_any
+        per round, an F rank serving several replicas starts on the first message to arrive and answers the rest
+        with one larger job."""
+        server = self.server
+        rows, targets = [], []
+        for a, slot, _ in messages:
+            row = server.row_for(a, slot, 0, self.g.n_max, layer_id)
+            target = server.reply_target(row)
+            if target is None:
+                raise RuntimeError(f"A rank {a} is not connected to F rank {self.f}")
+            rows.append(row)
+            targets.append(target)
+            if (a, slot) not in self._dev_owned:  # the device word takes over from the host's bookkeeping
+                last = server.last_seq(a, slot)
+                N.call("asap_write32", self._state_ptr(a, slot), last & SEQ_MASK, ctypes.c_void_p(stream))
+                self._dev_owned.add((a, slot))
+                self._dev_seq[(a, slot)] = None
+        R = len(rows)
+        if R > min(self.join, N.MAX_JOB_ROWS):
+            raise ValueError(f"a job of {R} rows needs join >= {R} (this scheduler: {self.join})")
+        N.call("asap_ffn_wait_rest", self.ws_handle, R,
+               (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
+               (ctypes.c_uint64 * R)(*[self._state_ptr(r.a, r.slot) for r in rows]),
+               (ctypes.c_uint32 * R)(*[seq & SEQ_MASK for _, _, seq in messages]),
+               (ctypes.c_int32 * R)(*[server.peers[r.a].epoch for r in rows]), self.g.n_max, self.status.ptr,
+               self.timeout_ns, ctypes.c_void_p(stream))
+        self._launch_rows(self.experts[layer_id], rows, targets, stream)
+        self.layer_calls[layer_id] += 1
+
     def _state_ptr(self, a: int, slot: int) -> int:
         return self.seq_state.data_ptr() + 4 * (a * self.g.slots + slot)
 

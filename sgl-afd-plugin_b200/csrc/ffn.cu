@@ -121,21 +121,31 @@ struct WaitArgs {
   uint32_t* seq_state[kMaxJobRows];  // device words holding the last consumed seq (used and advanced when set)
   int32_t epoch[kMaxJobRows];
   int32_t* any;  // non-NULL: answer ONE message, the first ready in round-robin order after *any (then updated)
+  int32_t rest;  // answer every row not yet answered this round: rows whose seq word reached round_seq are left out
+  uint32_t round_seq[kMaxJobRows];
   uint64_t status, timeout_ns;
 };
 
 // One warp; lane r spins (bounded) on row r's doorbell until its seq is cyclically ahead of last_seq[r], then
 // decodes it.  The job is valid when every doorbell came, every epoch and size checks, all rows name the same
-// layer and the tokens fit the workspace.
+// layer and the tokens fit the workspace.  In the `rest` form a row whose sequence word already reached its
+// round_seq (answered this round by an earlier job) is left out: the job joins the other rows' messages, its row
+// states numbered in row order with the row as their view, and a job left with no row is empty (not valid, no
+// error).
 __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
   JobDesc* d = a.d;
   RowState* rs = reinterpret_cast<RowState*>(d + 1);
   const int lane = threadIdx.x;
   int ok = 1, n = 0, layer = 0, epoch = 0;
   uint32_t seq = 0;
-  if (lane < a.rows) {
+  bool take = lane < a.rows;
+  uint32_t last = 0;
+  if (take) {
+    last = a.seq_state[lane] ? *a.seq_state[lane] : a.last_seq[lane];
+    if (a.rest && (int32_t)(last - a.round_seq[lane]) >= 0) take = false;  // answered this round already
+  }
+  if (take) {
     const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
-    const uint32_t last = a.seq_state[lane] ? *a.seq_state[lane] : a.last_seq[lane];
     uint64_t word = 0;
     for (;;) {
       word = ld_relaxed_sys_u64(a.bell[lane]);
@@ -159,18 +169,21 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
     }
   }
   ok = __all_sync(0xffffffffu, ok);
-  const int layer0 = __shfl_sync(0xffffffffu, layer, 0);
-  const bool same_layer = __all_sync(0xffffffffu, lane >= a.rows || layer == layer0);
-  int incl = ok ? n : 0;  // inclusive scan of the row sizes
+  const uint32_t taken = __ballot_sync(0xffffffffu, take);
+  const int first = taken ? __ffs(taken) - 1 : 0;
+  const int layer0 = __shfl_sync(0xffffffffu, layer, first);
+  const bool same_layer = __all_sync(0xffffffffu, !take || layer == layer0);
+  int incl = (ok && take) ? n : 0;  // inclusive scan of the taken rows' sizes
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int u = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += u;
   }
   const int total = __shfl_sync(0xffffffffu, incl, 31);
-  if (lane < a.rows) rs[lane] = RowState{ok ? n : 0, incl - (ok ? n : 0), seq, layer, lane, {0, 0, 0}};
-  const uint32_t seq0 = __shfl_sync(0xffffffffu, seq, 0);
-  const int epoch0 = __shfl_sync(0xffffffffu, epoch, 0);
+  if (take)
+    rs[__popc(taken & ((1u << lane) - 1u))] = RowState{ok ? n : 0, incl - (ok ? n : 0), seq, layer, lane, {0, 0, 0}};
+  const uint32_t seq0 = __shfl_sync(0xffffffffu, seq, first);
+  const int epoch0 = __shfl_sync(0xffffffffu, epoch, first);
   if (lane == 0) {
     d->t_seen = globaltimer_ns();
     d->t_reply = 0;
@@ -179,8 +192,8 @@ __global__ void ffn_wait_kernel(const __grid_constant__ WaitArgs a) {
     d->layer = layer0;
     d->epoch = epoch0;
     d->sync = 0;
-    d->rows = a.rows;
-    bool valid = ok != 0;
+    d->rows = __popc(taken);
+    bool valid = ok != 0 && taken != 0;
     if (valid && (!same_layer || total > a.capacity)) {
       report(a.status, status_word(ASAP_ST_BAD_JOB, 0, 0, seq0));
       valid = false;
@@ -1279,7 +1292,7 @@ int asap_ffn_ws_release(uint64_t handle) {
 
 static int ffn_wait_impl(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint32_t* last_seqs,
                          const uint64_t* seq_states, const int32_t* expect_epochs, int32_t n_max, uint64_t status,
-                         uint64_t timeout_ns, void* stream) {
+                         uint64_t timeout_ns, void* stream, const uint32_t* round_seqs = nullptr) {
   WsHandle* w = get_ws(ws_handle);
   if (!w || rows < 1 || rows > kMaxJobRows || !bells || !(last_seqs || seq_states) || !expect_epochs) {
     set_error("asap_ffn_wait: unknown workspace handle, NULL arrays or rows %d outside [1, %d]", rows, kMaxJobRows);
@@ -1307,7 +1320,9 @@ static int ffn_wait_impl(uint64_t ws_handle, int32_t rows, const uint64_t* bells
     a.last_seq[r] = last_seqs ? last_seqs[r] : 0u;
     a.seq_state[r] = seq_states ? (uint32_t*)seq_states[r] : nullptr;
     a.epoch[r] = expect_epochs[r];
+    a.round_seq[r] = round_seqs ? round_seqs[r] : 0u;
   }
+  a.rest = round_seqs ? 1 : 0;
   a.status = status;
   a.timeout_ns = timeout_ns;
   ffn_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(a);
@@ -1333,6 +1348,17 @@ int asap_ffn_wait_state(uint64_t ws_handle, int32_t rows, const uint64_t* bells,
     return ASAP_EINVAL;
   }
   return ffn_wait_impl(ws_handle, rows, bells, nullptr, seq_states, expect_epochs, n_max, status, timeout_ns, stream);
+}
+
+int asap_ffn_wait_rest(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,
+                       const uint32_t* round_seqs, const int32_t* expect_epochs, int32_t n_max, uint64_t status,
+                       uint64_t timeout_ns, void* stream) {
+  if (!seq_states || !round_seqs) {
+    set_error("asap_ffn_wait_rest: NULL seq_states or round_seqs");
+    return ASAP_EINVAL;
+  }
+  return ffn_wait_impl(ws_handle, rows, bells, nullptr, seq_states, expect_epochs, n_max, status, timeout_ns, stream,
+                       round_seqs);
 }
 
 int asap_ffn_wait_any(uint64_t ws_handle, int32_t rows, const uint64_t* bells, const uint64_t* seq_states,

@@ -255,3 +255,77 @@ def test_round_robin_any_ready_message(cuda_ok, graph):
             ch.close()
         srv.close()
         experts.release()
+
+
+def test_first_message_then_the_rest(cuda_ok):
+    """asap_ffn_wait_rest after asap_ffn_wait_any: three A replicas send one message each; the first job answers
+    one of them, the second answers the other two together (its token count is theirs), every combined output
+    matches the oracle.  In a second round three any-jobs answer all three messages, so the rest-job that follows
+    finds nothing left: an empty job, with no error and no reply."""
+    import os
+    import tempfile
+
+    run_dir = tempfile.mkdtemp(dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else None)
+    rng = np.random.default_rng(21)
+    T, H, I, k, E = 96, 256, 128, 4, 8
+    sizes = (T, T - 5, T - 11)
+    g = Geometry(3, 1, 1, T, H, k, 1)
+    experts = Mxfp4Experts.random(E, H, I, seed=8)
+    srv = FfnServer(0, g, device=0, run_dir=run_dir, listen=False).start()
+    chans = [AttnChannel(a, g, [("in-process", 0)], device=0, timeout_s=5.0, expert_bounds=[0, E],
+                         _connector=lambda f, hello: srv.handshake(hello)).connect() for a in range(3)]
+    sched = FfnScheduler(srv, {0: experts}, timeout_s=5.0, join=3)
+    gate, up, w2 = experts_to_oracle(experts)
+    f_stream = torch.cuda.Stream()
+    stream = torch.cuda.current_stream()
+    sources = [(a, 0) for a in range(3)]
+    keep = []
+
+    def send_all():
+        sent = []
+        for a in range(3):
+            x, ids, w = random_inputs(rng, sizes[a], H, k, 0, E)
+            dev = (bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+            keep.append(dev)
+            t = chans[a].send(0, 0, dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), sizes[a],
+                              stream.cuda_stream)
+            sent.append((t, (x, ids, w)))
+        f_stream.wait_stream(stream)  # the F jobs run after every send (no kernel spins on another of this GPU)
+        return sent
+
+    def check_all(sent):
+        for a, (t, msg) in enumerate(sent):
+            out = torch.empty(sizes[a], H, dtype=torch.bfloat16, device="cuda")
+            chans[a].combine(t, out.data_ptr(), stream.cuda_stream)
+            torch.cuda.synchronize()
+            chans[a].check()
+            ref = moe.round_trip(*msg, [0, E], [(gate, up, w2)])
+            assert moe.rel_l2(np_from_bf16(out), ref) < TOL, a
+
+    try:
+        sent = send_all()
+        sched.run_device_wait_any(sources, 0, f_stream.cuda_stream)
+        torch.cuda.synchronize()
+        first = sched.job_info()["n"]
+        assert first in sizes
+        sched.run_device_wait_rest([(a, 0, 1) for a in range(3)], 0, f_stream.cuda_stream)
+        torch.cuda.synchronize()
+        sched.check()
+        info = sched.job_info()
+        assert info["valid"] == 1 and info["n"] == sum(sizes) - first
+        check_all(sent)
+        sent = send_all()
+        for _ in range(3):
+            sched.run_device_wait_any(sources, 0, f_stream.cuda_stream)
+        sched.run_device_wait_rest([(a, 0, 2) for a in range(3)], 0, f_stream.cuda_stream)
+        torch.cuda.synchronize()
+        sched.check()
+        assert sched.job_info()["valid"] == 0  # nothing left this round: an empty job
+        check_all(sent)
+    finally:
+        torch.cuda.synchronize()
+        sched.close()
+        for ch in chans:
+            ch.close()
+        srv.close()
+        experts.release()
