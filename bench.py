@@ -244,6 +244,19 @@ def gemm_flops(pairs):
 
 
 NVLINK_NOMINAL_GBS = 900.0  # NVLink 5 per direction per GPU (nominal)
+# --serve auto: below this many expected (token, local expert) pairs per message and F rank, the rest of a step's
+# messages are answered as one joined job (measured at 4A4F: configs 4 and 5 up to T=4096 gain, config 2's 32768
+# pairs per message lose to per-message jobs, whose replies overlap the next job)
+FTR_PAIRS = 32768
+
+
+def first_then_rest(args, n_a, T, p_max):
+    """Whether an F rank answers a step of n_a messages of T tokens as first-ready + joined rest (--serve)."""
+    if n_a < 2 or args.join_replicas:
+        return False
+    if args.serve != "auto":
+        return args.serve == "first-then-rest"
+    return T * K_TOP * p_max / E < FTR_PAIRS
 
 
 def f_job_launches(rows=1):
@@ -1309,6 +1322,8 @@ def run_multi(args):
     T_max = max(t_list)
     g = Geometry(n_a, 1, 2, T_max, H, K_TOP, n_f)
     bounds = expert_bounds(n_f)
+    p_max = max(bounds[i + 1] - bounds[i] for i in range(n_f))
+    ftr = [first_then_rest(args, n_a, T, p_max) for T in t_list]  # F serving mode per token count of the run
     a_ranks, f_ranks = placement(world, n_a, args.placement)
     is_a = rank in a_ranks
     a_idx = a_ranks.index(rank) if is_a else -1
@@ -1323,7 +1338,7 @@ def run_multi(args):
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
         sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s,
-                             join=n_a if (args.join_replicas or args.first_then_rest) else 1)
+                             join=n_a if (args.join_replicas or any(ftr)) else 1)
         ep = ("127.0.0.1", server.port)
     eps = [None] * world
     dist.all_gather_object(eps, ep)
@@ -1346,7 +1361,8 @@ def run_multi(args):
                     else:
                         sched.run_device_wait_rows(msgs, 0, stream.cuda_stream)
                     continue
-                if args.first_then_rest and n_a > 1:  # the first ready message alone, then the rest together
+                if ftr[min(s // (steps_per_phase * (1 if sweep else 2)), len(t_list) - 1)]:
+                    # the first ready message alone, then the rest of the step together
                     sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream)
                     sched.run_device_wait_rest([(a, 0, s + 1) for a in range(n_a)], 0, stream.cuda_stream)
                     continue
@@ -1510,7 +1526,8 @@ def run_multi(args):
             "dtype": DTYPE[KIND], "data": "synthetic",
             "gpu_launches": args.steps * (4 * n_a +
                                           (f_job_launches(n_a) if args.join_replicas else
-                                           f_job_launches() + f_job_launches(n_a) if args.first_then_rest and n_a > 1
+                                           f_job_launches() + f_job_launches(n_a)
+                                           if first_then_rest(args, n_a, T, p_max)
                                            else f_job_launches() * n_a) * n_f), "roofline": None,  # set per line below
             "cpu_baseline": None,
             "clocks": clock_summary,
@@ -1530,7 +1547,7 @@ def run_multi(args):
                 "placement": args.placement, "a_ranks": a_ranks,
                 "f_jobs": ("one joined job per step (all replicas' messages)" if args.join_replicas else
                            "two jobs per step: the first ready message alone, then the step's other messages joined"
-                           if args.first_then_rest and n_a > 1 else
+                           if first_then_rest(args, n_a, T, p_max) else
                            "one job per message" + (", first ready replica first (round robin on the device)"
                                                     if args.any_order else ""))
                           + (", CUDA-graph replays" if args.graphs else ""), "host_binding": binding,
@@ -1621,9 +1638,12 @@ def main():
     ap.add_argument("--no-numa-bind", action="store_true", help="N>1: do not bind ranks to their GPU's NUMA node")
     ap.add_argument("--join-replicas", action="store_true",
                     help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
-    ap.add_argument("--first-then-rest", action="store_true",
-                    help="N>1: each F rank answers the first ready message of a step alone (asap_ffn_wait_any), then "
-                         "the step's other messages with one joined job (asap_ffn_wait_rest)")
+    ap.add_argument("--serve", choices=("auto", "per-message", "first-then-rest"), default="auto",
+                    help="N>1, several A replicas: per-message = one F job per message; first-then-rest = the first "
+                         "ready message of a step alone (asap_ffn_wait_any), then the step's other messages as one "
+                         "joined job (asap_ffn_wait_rest); auto = first-then-rest when a message brings an F rank "
+                         f"fewer than {FTR_PAIRS} expected pairs (small jobs: fewer chains), else per-message (the "
+                         "replies of earlier jobs overlap later jobs' compute)")
     args = ap.parse_args()
     layer = LAYERS["fp8-layer" if args.workload == "fp8-layer" else "layer"]
     globals().update(layer)

@@ -109,3 +109,18 @@ def test_hbm_kernel_gbs():
 def test_f_job_launches():
     """wait + route count/scan/place + quantise + GEMM1 + GEMM2 + reduce (+ gather for joined jobs)."""
     assert bench.f_job_launches() == 8 and bench.f_job_launches(4) == 9
+
+
+def test_first_then_rest_policy():
+    """--serve auto: the first ready message alone and the rest joined when a message brings an F rank fewer than
+    FTR_PAIRS expected pairs; per-message jobs otherwise, and always with a single replica."""
+    from types import SimpleNamespace
+
+    args = SimpleNamespace(serve="auto", join_replicas=False)
+    assert bench.E == 256 and bench.K_TOP == 8
+    assert not bench.first_then_rest(args, 4, 16384, 64)  # config 2 at 4A4F: 32768 pairs per message
+    assert bench.first_then_rest(args, 4, 4096, 64)
+    assert not bench.first_then_rest(args, 1, 256, 256)  # one replica: nothing to join
+    assert bench.first_then_rest(SimpleNamespace(serve="first-then-rest", join_replicas=False), 4, 16384, 64)
+    assert not bench.first_then_rest(SimpleNamespace(serve="per-message", join_replicas=False), 4, 256, 64)
+    assert not bench.first_then_rest(SimpleNamespace(serve="auto", join_replicas=True), 4, 256, 64)
