@@ -254,6 +254,8 @@ def first_then_rest(args, n_a, T, p_max):
     """Whether an F rank answers a step of n_a messages of T tokens as first-ready + joined rest (--serve)."""
     if n_a < 2 or args.join_replicas:
         return False
+    if args.serve == "auto" and n_a < 3:  # the rest of a step is one message: nothing to join
+        return False
     if args.serve != "auto":
         return args.serve == "first-then-rest"
     return T * K_TOP * p_max / E < FTR_PAIRS
@@ -1641,9 +1643,9 @@ def main():
     ap.add_argument("--serve", choices=("auto", "per-message", "first-then-rest"), default="auto",
                     help="N>1, several A replicas: per-message = one F job per message; first-then-rest = the first "
                          "ready message of a step alone (asap_ffn_wait_any), then the step's other messages as one "
-                         "joined job (asap_ffn_wait_rest); auto = first-then-rest when a message brings an F rank "
-                         f"fewer than {FTR_PAIRS} expected pairs (small jobs: fewer chains), else per-message (the "
-                         "replies of earlier jobs overlap later jobs' compute)")
+                         "joined job (asap_ffn_wait_rest); auto = first-then-rest with three or more replicas when a "
+                         f"message brings an F rank fewer than {FTR_PAIRS} expected pairs (small jobs: fewer chains), "
+                         "else per-message (the replies of earlier jobs overlap later jobs' compute)")
     args = ap.parse_args()
     layer = LAYERS["fp8-layer" if args.workload == "fp8-layer" else "layer"]
     globals().update(layer)

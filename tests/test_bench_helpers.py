@@ -112,8 +112,8 @@ def test_f_job_launches():
 
 
 def test_first_then_rest_policy():
-    """--serve auto: the first ready message alone and the rest joined when a message brings an F rank fewer than
-    FTR_PAIRS expected pairs; per-message jobs otherwise, and always with a single replica."""
+    """--serve auto: the first ready message alone and the rest joined when three or more replicas send and a
+    message brings an F rank fewer than FTR_PAIRS expected pairs; per-message jobs otherwise."""
     from types import SimpleNamespace
 
     args = SimpleNamespace(serve="auto", join_replicas=False)
@@ -121,6 +121,7 @@ def test_first_then_rest_policy():
     assert not bench.first_then_rest(args, 4, 16384, 64)  # config 2 at 4A4F: 32768 pairs per message
     assert bench.first_then_rest(args, 4, 4096, 64)
     assert not bench.first_then_rest(args, 1, 256, 256)  # one replica: nothing to join
+    assert not bench.first_then_rest(args, 2, 4096, 43)  # two replicas: the rest is a single message
     assert bench.first_then_rest(SimpleNamespace(serve="first-then-rest", join_replicas=False), 4, 16384, 64)
     assert not bench.first_then_rest(SimpleNamespace(serve="per-message", join_replicas=False), 4, 256, 64)
     assert not bench.first_then_rest(SimpleNamespace(serve="auto", join_replicas=True), 4, 256, 64)
