@@ -1306,6 +1306,7 @@ def run_multi(args):
     import torch
     import torch.distributed as dist
 
+    from asap_b200 import _native as N
     from asap_b200.experts import Mxfp4Experts
     from asap_b200.scheduler import FfnScheduler
     from asap_b200.transport.channel import AttnChannel, serve_order
@@ -1380,6 +1381,8 @@ def run_multi(args):
                     else:
                         sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
 
+        if not args.graphs:  # per-stage CUDA events of every job (host-side marks: not inside captured graphs)
+            N.call("asap_ffn_enable_timing", sched.ws_handle, 1)
         feeder = threading.Thread(target=feed, daemon=True)
         feeder.start()
     else:
@@ -1474,6 +1477,26 @@ def run_multi(args):
     parities = [None] * world
     dist.all_gather_object(parities, parity)
     parities = [p for p in parities if p is not None]
+    # the F ranks' mean per-stage kernel times over their last 64 jobs (the end of the last phase and the parity step)
+    fk = None
+    if not is_a and not args.graphs:
+        kms = (ctypes.c_float * 5)()
+        N.call("asap_ffn_last_timing", sched.ws_handle, kms, 5)
+        N.call("asap_ffn_enable_timing", sched.ws_handle, 0)
+        fk = [float(v) for v in kms]
+    fks = [None] * world
+    dist.all_gather_object(fks, fk)
+    fks = [v for v in fks if v is not None]
+    f_kernels = None
+    if fks:
+        stages = ("routing", "quantise_permute", "gemm1", "gemm2", "reduce_reply")
+        mean = [statistics.mean(v[i] for v in fks) for i in range(5)]
+        f_kernels = {"per_job_ms_mean_over_f": {k: round(v, 4) for k, v in zip(stages, mean)},
+                     "per_job_ms_sum": round(sum(mean), 4),
+                     "note": "CUDA events per stage inside each F job, mean over each F rank's last 64 jobs (of the "
+                             "last token count), then over the F ranks; jobs per step per F rank: "
+                             + ("2 (first ready, then the rest joined)" if ftr[-1] else
+                                "1 (joined)" if args.join_replicas else str(n_a))}
     # doorbell latency: one message at a time from A rank 0, F ranks idle and already spinning on their doorbell
     lat = []
     seq_next = phases * steps_per_phase + 2
@@ -1573,6 +1596,8 @@ def run_multi(args):
                               "counts_match_routing": all(p["counts_match_routing"] for p in parities),
                               "pass": all(p["pass"] for p in parities)}
             line["nvlink"] = link
+            if res is results[-1] and f_kernels is not None:
+                line["f_kernels_ms"] = f_kernels
             if "e2e_ms" in res:
                 e = res["e2e_ms"]
                 line["e2e"] = {"value": round(n_a * T / (e * 1e-3), 1), "unit": "tokens/s",
