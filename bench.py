@@ -1228,7 +1228,7 @@ def measure_links(args, is_a, channel, sched, stream, send_stream, x_all, a_idx,
 
     res = {}
     if not is_a:
-        N.call("asap_ffn_enable_timing", sched.ws_handle, 1)
+        sched.enable_timing(True)
         for r in range(rounds):
             for a in range(n_a):
                 sched.run_device_wait(a, 0, seqs[a] + 1 + r, 0, stream.cuda_stream)
@@ -1252,10 +1252,9 @@ def measure_links(args, is_a, channel, sched, stream, send_stream, x_all, a_idx,
         res = {"dispatch_ms": statistics.median(times), "dispatch_bytes": nbytes, "counts": counts}
     else:
         torch.cuda.synchronize()
-        kms = (ctypes.c_float * 5)()
-        N.call("asap_ffn_last_timing", sched.ws_handle, kms, 5)
-        N.call("asap_ffn_enable_timing", sched.ws_handle, 0)
-        res = {"reply_ms": float(kms[4])}  # mean over this rank's jobs of the rounds
+        kms = sched.last_timing()
+        sched.enable_timing(False)
+        res = {"reply_ms": float(kms[4]) if kms else 0.0}  # mean over this rank's jobs of the rounds
     dist.barrier()
     # copy-engine peer write, each A rank into one F rank's slot-1 region (unused by this benchmark)
     if is_a:
@@ -1341,7 +1340,8 @@ def run_multi(args):
         server = FfnServer(f, g, device=local, run_dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else "/tmp",
                            host="127.0.0.1", port=0).start()
         sched = FfnScheduler(server, {0: experts}, timeout_s=timeout_s,
-                             join=n_a if (args.join_replicas or any(ftr)) else 1)
+                             join=n_a if (args.join_replicas or any(ftr)) else 1,
+                             overlap_replies=args.overlap_replies if n_a > 1 and not args.graphs else 0)
         ep = ("127.0.0.1", server.port)
     eps = [None] * world
     dist.all_gather_object(eps, ep)
@@ -1364,15 +1364,16 @@ def run_multi(args):
                     else:
                         sched.run_device_wait_rows(msgs, 0, stream.cuda_stream)
                     continue
+                ov = sched.reserve > 0  # every job of the step but its last replies from the side stream
                 if ftr[min(s // (steps_per_phase * (1 if sweep else 2)), len(t_list) - 1)]:
                     # the first ready message alone, then the rest of the step together
-                    sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream)
+                    sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream, overlap=ov)
                     sched.run_device_wait_rest([(a, 0, s + 1) for a in range(n_a)], 0, stream.cuda_stream)
                     continue
                 if args.any_order:  # each job answers whichever replica's message is ready first (round robin)
-                    for _ in range(n_a):
+                    for i in range(n_a):
                         sched.run_device_wait_any([(a, 0) for a in range(n_a)], 0, stream.cuda_stream,
-                                                  graph=args.graphs)
+                                                  graph=args.graphs, overlap=ov and i < n_a - 1)
                     continue
                 # fixed order: answer the A ranks in the order their messages complete here (send_order)
                 for a in serve_order(f, n_a, n_f):
@@ -1382,7 +1383,7 @@ def run_multi(args):
                         sched.run_device_wait(a, 0, s + 1, 0, stream.cuda_stream)
 
         if not args.graphs:  # per-stage CUDA events of every job (host-side marks: not inside captured graphs)
-            N.call("asap_ffn_enable_timing", sched.ws_handle, 1)
+            sched.enable_timing(True)
         feeder = threading.Thread(target=feed, daemon=True)
         feeder.start()
     else:
@@ -1480,10 +1481,8 @@ def run_multi(args):
     # the F ranks' mean per-stage kernel times over their last 64 jobs (the end of the last phase and the parity step)
     fk = None
     if not is_a and not args.graphs:
-        kms = (ctypes.c_float * 5)()
-        N.call("asap_ffn_last_timing", sched.ws_handle, kms, 5)
-        N.call("asap_ffn_enable_timing", sched.ws_handle, 0)
-        fk = [float(v) for v in kms]
+        fk = sched.last_timing()
+        sched.enable_timing(False)
     fks = [None] * world
     dist.all_gather_object(fks, fk)
     fks = [v for v in fks if v is not None]
@@ -1494,7 +1493,9 @@ def run_multi(args):
         f_kernels = {"per_job_ms_mean_over_f": {k: round(v, 4) for k, v in zip(stages, mean)},
                      "per_job_ms_sum": round(sum(mean), 4),
                      "note": "CUDA events per stage inside each F job, mean over each F rank's last 64 jobs (of the "
-                             "last token count), then over the F ranks; jobs per step per F rank: "
+                             "last token count), then over the F ranks; replies on a side stream: "
+                             + (f"every job of a step but its last, on {args.overlap_replies} SMs"
+                                if args.overlap_replies and n_a > 1 else "no") + "; jobs per step per F rank: "
                              + ("2 (first ready, then the rest joined)" if ftr[-1] else
                                 "1 (joined)" if args.join_replicas else str(n_a))}
     # doorbell latency: one message at a time from A rank 0, F ranks idle and already spinning on their doorbell
@@ -1665,6 +1666,9 @@ def main():
     ap.add_argument("--no-numa-bind", action="store_true", help="N>1: do not bind ranks to their GPU's NUMA node")
     ap.add_argument("--join-replicas", action="store_true",
                     help="N>1: each F rank answers all A replicas' messages of a step with one joined job")
+    ap.add_argument("--overlap-replies", type=int, default=0,
+                    help="N>1: SMs left to the F ranks' replies, which then run on a side stream while the step's "
+                         "next job computes (every job of a step but its last; 0 = each reply in its job's order)")
     ap.add_argument("--serve", choices=("auto", "per-message", "first-then-rest"), default="auto",
                     help="N>1, several A replicas: per-message = one F job per message; first-then-rest = the first "
                          "ready message of a step alone (asap_ffn_wait_any), then the step's other messages as one "

@@ -315,6 +315,17 @@ typedef struct {
 int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t rows, const asap_ffn_row_t* row_views,
                       float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream);
 
+/* asap_ffn_job_rows whose reduce + reply (the reference's FfnServer.reply, server.py:340-350) runs on
+ * `reply_stream` with `reply_ctas` CTAs, after an event behind GEMM2, while `stream` goes on to the next job with
+ * persistent GEMM grids of `gemm_ctas` CTAs (fewer than the SMs leaves SMs free for the reply).  Across GPUs the
+ * reply's stores cross NVLink, and this lets them overlap the next message's GEMMs.  The reply still reads this
+ * workspace: a caller must not start another job on it before the reply is done (an event recorded on
+ * `reply_stream` after this call), so consecutive jobs alternate between two workspaces. */
+int asap_ffn_job_rows_overlap(uint64_t experts_handle, uint64_t ws_handle, int32_t rows,
+                              const asap_ffn_row_t* row_views, float swiglu_limit, uint64_t status,
+                              uint64_t timeout_ns, void* stream, void* reply_stream, int32_t gemm_ctas,
+                              int32_t reply_ctas);
+
 /* Per-kernel timing of asap_ffn_job on this workspace: when enabled, CUDA events are recorded on the job's
  * stream around its 5 stages (routing, quantise+permute, gemm1, gemm2, reduce+reply); last_timing waits
  * for the recorded jobs (the last 64 since enable) and returns each kernel's mean duration in ms (n >= 5). */

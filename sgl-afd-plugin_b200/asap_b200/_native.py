@@ -110,6 +110,8 @@ _SIGS = {
                                      POINTER(c_int32), c_void_p]),
     "asap_ffn_job_rows": (c_int32, [c_uint64, c_uint64, c_int32, POINTER(FfnRow_t), c_float, c_uint64, c_uint64,
                                     c_void_p]),
+    "asap_ffn_job_rows_overlap": (c_int32, [c_uint64, c_uint64, c_int32, POINTER(FfnRow_t), c_float, c_uint64,
+                                            c_uint64, c_void_p, c_void_p, c_int32, c_int32]),
     "asap_ffn_job": (c_int32, [c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_float,
                                c_uint64, c_uint64, c_void_p]),
     "asap_ffn_enable_timing": (c_int32, [c_uint64, c_int32]),

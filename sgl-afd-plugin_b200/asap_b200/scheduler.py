@@ -83,7 +83,7 @@ class FfnScheduler:
     """The experts of one F rank (``experts[layer_id]``) answering the jobs of ``server``."""
 
     def __init__(self, server: FfnServer, experts: Dict[int, Mxfp4Experts], *, swiglu_limit: float = 0.0,
-                 timeout_s: float = 60.0, timing: bool = False, join: int = 1):
+                 timeout_s: float = 60.0, timing: bool = False, join: int = 1, overlap_replies: int = 0):
         g = server.g
         if g.group != 1:
             raise NotImplementedError("AFD supports attention TP size 1 only (group=1), as the reference's "
@@ -111,6 +111,24 @@ class FfnScheduler:
         N.call("asap_ffn_ws_register", self.ws.data_ptr(), cap, g.topk, first.num_local, first.hidden,
                first.inter, ctypes.byref(h))
         self.ws_handle = h.value
+        # overlap_replies = k > 0: device-wait jobs that ask for it send their reduce + reply from a side stream on
+        # k SMs (the GEMMs keep the others) while the next job computes; jobs alternate between two workspaces so
+        # that a reply still reading one never meets the next job writing it
+        self.reserve = int(overlap_replies)
+        self._wss, self._owners = [self.ws_handle], [self._ws_owner]
+        self._ws_i = 0
+        self._reply_done = [None, None]
+        self._reply_stream = None
+        if self.reserve:
+            if not 0 < self.reserve < 64:
+                raise ValueError("overlap_replies: SMs left to the replies, in [1, 63]")
+            owner2, ws2 = _aligned_empty(nbytes, f"cuda:{self.device}")
+            h2 = ctypes.c_uint64()
+            N.call("asap_ffn_ws_register", ws2.data_ptr(), cap, g.topk, first.num_local, first.hidden,
+                   first.inter, ctypes.byref(h2))
+            self._wss.append(h2.value)
+            self._owners.append(owner2)
+            self._reply_stream = torch.cuda.Stream(self.device)
         self.status = HostWords(1)
         # CUDA-graph mode: per (A rank, slot) the last consumed seq lives on the device (asap_ffn_wait_state), so a
         # chain captured once replays for every message; _dev_seq mirrors what those words will hold
@@ -131,9 +149,35 @@ class FfnScheduler:
             N.call("asap_graph_release", h)
         self._graphs.clear()
         if self.ws_handle:
-            N.call("asap_ffn_ws_release", self.ws_handle)
+            for h in self._wss:
+                N.call("asap_ffn_ws_release", h)
             self.ws_handle = 0
         self.status.close()
+
+    def _next_ws(self, stream: int) -> None:
+        """Overlapped replies: the next job takes the other workspace, after the reply that last read it."""
+        if not self.reserve:
+            return
+        self._ws_i ^= 1
+        self.ws_handle = self._wss[self._ws_i]
+        ev = self._reply_done[self._ws_i]
+        if ev is not None:
+            torch.cuda.ExternalStream(stream, device=self.device).wait_event(ev)
+
+    def enable_timing(self, on: bool) -> None:
+        """Per-stage CUDA events of every job (asap_ffn_enable_timing on each workspace)."""
+        for h in self._wss:
+            N.call("asap_ffn_enable_timing", h, 1 if on else 0)
+
+    def last_timing(self) -> Optional[list]:
+        """Mean per-stage ms (routing, quantise+permute, gemm1, gemm2, reduce+reply) of the recorded jobs, over
+        the workspaces that recorded any; None if none did."""
+        got = []
+        for h in self._wss:
+            kms = (ctypes.c_float * 5)()
+            if N.lib().asap_ffn_last_timing(h, kms, 5) == 0:
+                got.append([float(v) for v in kms])
+        return [sum(v[i] for v in got) / len(got) for i in range(5)] if got else None
 
     def check(self) -> None:
         word = self.status.read()
@@ -147,11 +191,22 @@ class FfnScheduler:
         N.call("asap_ffn_job", experts.handle, self.ws_handle, row.x_ptr, row.ids_ptr, row.w_ptr, seg, done,
                ctypes.c_float(self.swiglu_limit), self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
 
-    def _launch_rows(self, experts, rows, targets, stream: int) -> None:
+    def _launch_rows(self, experts, rows, targets, stream: int, overlap: bool = False) -> None:
         views = (N.FfnRow_t * len(rows))(*[N.FfnRow_t(r.x_ptr, r.ids_ptr, r.w_ptr, seg, done)
                                             for r, (seg, done) in zip(rows, targets)])
+        if self.reserve and overlap:
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            N.call("asap_ffn_job_rows_overlap", experts.handle, self.ws_handle, len(rows), views,
+                   ctypes.c_float(self.swiglu_limit), self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream),
+                   ctypes.c_void_p(self._reply_stream.cuda_stream), sms - self.reserve, 2 * self.reserve)
+            ev = torch.cuda.Event()
+            ev.record(self._reply_stream)
+            self._reply_done[self._ws_i] = ev
+            return
         N.call("asap_ffn_job_rows", experts.handle, self.ws_handle, len(rows), views,
                ctypes.c_float(self.swiglu_limit), self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
+        if self.reserve:
+            self._reply_done[self._ws_i] = None  # this job's reply is ordered on the job's own stream
 
     def run_job(self, job: Job, stream: Optional[int] = None) -> None:
         """One expert chain for the rows of one job (host-poll mode; the rows' tokens are answered together, as
@@ -160,6 +215,7 @@ class FfnScheduler:
         started = timer.start() if timer else None
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
+        self._next_ws(stream)
         live = [(row, self.server.reply_target(row)) for row in job.rows]
         live = [(row, t) for row, t in live if t is not None]  # reconnected A ranks: dropped (server.py:343-346)
         if not live:
@@ -182,7 +238,8 @@ class FfnScheduler:
         if timer:
             timer.add(sum(r.n_tokens for r in rows), started, time.perf_counter() - tic)
 
-    def run_device_wait(self, a: int, slot: int, seq: int, layer_id: int, stream: int) -> None:
+    def run_device_wait(self, a: int, slot: int, seq: int, layer_id: int, stream: int,
+                        overlap: bool = False) -> None:
         """Enqueue a job for the next message of (a, slot) before it arrives: the chain starts with a bounded
         device spin on the doorbell (libasap asap_ffn_wait), which also validates epoch and size.  The token count
         comes from the doorbell on the device; ``seq`` is the message the host expects (backpressure forbids
@@ -193,9 +250,13 @@ class FfnScheduler:
         target = server.reply_target(row)
         if target is None:
             return
+        self._next_ws(stream)
         N.call("asap_ffn_wait", self.ws_handle, server.bell_dev(a, slot), (seq - 1) & SEQ_MASK, peer.epoch,
                self.g.n_max, self.status.ptr, self.timeout_ns, ctypes.c_void_p(stream))
-        self._launch(self.experts[layer_id], row, target, stream)
+        if self.reserve:
+            self._launch_rows(self.experts[layer_id], [row], [target], stream, overlap)
+        else:
+            self._launch(self.experts[layer_id], row, target, stream)
         server.advance(a, slot, seq)
         self._dev_seq[(a, slot)] = None  # the device word was not used: re-sync before the next graph replay
         self._dev_owned.discard((a, slot))
@@ -205,6 +266,8 @@ class FfnScheduler:
         """``run_device_wait`` / ``run_device_wait_rows`` for ``messages`` = [(a, slot, seq), ...] as one replay of a
         CUDA graph captured on first use per (their (a, slot) pairs, layer, epochs) -- the device-side doorbell
         wait (sequence words on the device) and the whole expert chain in one launch."""
+        if self.reserve:
+            raise ValueError("CUDA-graph jobs do not overlap their replies (overlap_replies=0)")
         server = self.server
         rows, targets = [], []
         for a, slot, seq in messages:
@@ -232,7 +295,8 @@ class FfnScheduler:
             self._dev_seq[(r.a, r.slot)] = r.seq & SEQ_MASK
         self.layer_calls[layer_id] += 1
 
-    def run_device_wait_any(self, sources, layer_id: int, stream: int, graph: bool = False) -> None:
+    def run_device_wait_any(self, sources, layer_id: int, stream: int, graph: bool = False,
+                            overlap: bool = False) -> None:
         """One job answering ONE message of layer ``layer_id``: the first of ``sources`` = [(a, slot), ...] with a new
         message, in round-robin order after the source answered last -- the reference's poll order over ready
         doorbells (server.py:270-275), decided on the device (asap_ffn_wait_any), so one slow replica does not
@@ -257,13 +321,18 @@ class FfnScheduler:
             raise ValueError(f"at most {N.MAX_JOB_ROWS} sources")
         epochs = [server.peers[r.a].epoch for r in rows]
 
+        if graph and self.reserve:
+            raise ValueError("CUDA-graph jobs do not overlap their replies (overlap_replies=0)")
+        if not graph:
+            self._next_ws(stream)
+
         def enqueue(st: int) -> None:
             N.call("asap_ffn_wait_any", self.ws_handle, R,
                    (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
                    (ctypes.c_uint64 * R)(*[self._state_ptr(r.a, r.slot) for r in rows]),
                    (ctypes.c_int32 * R)(*epochs), self.g.n_max, self.rr_state.data_ptr(), self.status.ptr,
                    self.timeout_ns, ctypes.c_void_p(st))
-            self._launch_rows(self.experts[layer_id], rows, targets, st)
+            self._launch_rows(self.experts[layer_id], rows, targets, st, overlap)
 
         if graph:
             key = ("any", tuple(sources), layer_id, tuple(epochs))
@@ -285,7 +354,7 @@ class FfnScheduler:
             enqueue(stream)
         self.layer_calls[layer_id] += 1
 
-    def run_device_wait_rest(self, messages, layer_id: int, stream: int) -> None:
+    def run_device_wait_rest(self, messages, layer_id: int, stream: int, overlap: bool = False) -> None:
         """One joined job over the messages of this round not answered yet, ``messages`` = [(a, slot, seq), ...]
         with ``seq`` each source's message of the round: a source whose device sequence word already reached it
         (answered by an earlier run_device_wait_any job) is left out on the device (asap_ffn_wait_rest), the others'
@@ -309,13 +378,14 @@ class FfnScheduler:
         R = len(rows)
         if R > min(self.join, N.MAX_JOB_ROWS):
             raise ValueError(f"a job of {R} rows needs join >= {R} (this scheduler: {self.join})")
+        self._next_ws(stream)
         N.call("asap_ffn_wait_rest", self.ws_handle, R,
                (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
                (ctypes.c_uint64 * R)(*[self._state_ptr(r.a, r.slot) for r in rows]),
                (ctypes.c_uint32 * R)(*[seq & SEQ_MASK for _, _, seq in messages]),
                (ctypes.c_int32 * R)(*[server.peers[r.a].epoch for r in rows]), self.g.n_max, self.status.ptr,
                self.timeout_ns, ctypes.c_void_p(stream))
-        self._launch_rows(self.experts[layer_id], rows, targets, stream)
+        self._launch_rows(self.experts[layer_id], rows, targets, stream, overlap)
         self.layer_calls[layer_id] += 1
 
     def _state_ptr(self, a: int, slot: int) -> int:
@@ -356,6 +426,7 @@ class FfnScheduler:
         R = len(rows)
         if R > self.join:
             raise ValueError(f"a job of {R} rows needs join >= {R} (this scheduler: {self.join})")
+        self._next_ws(stream)
         N.call("asap_ffn_wait_rows", self.ws_handle, R,
                (ctypes.c_uint64 * R)(*[server.bell_dev(r.a, r.slot) for r in rows]),
                (ctypes.c_uint32 * R)(*[(r.seq - 1) & SEQ_MASK for r in rows]),

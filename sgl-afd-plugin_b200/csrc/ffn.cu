@@ -1089,6 +1089,7 @@ struct WsHandle {
   bool timing = false;
   int jobs = 0;  // jobs recorded since enable
   cudaEvent_t ev[kTimedJobs][kTimedKernels + 1] = {};
+  cudaEvent_t split = nullptr;  // GEMM2 done -> the reply stream's finalize (asap_ffn_job_rows_overlap)
 };
 
 static std::mutex g_mu;
@@ -1124,10 +1125,10 @@ static int ensure_gemm_attrs() {
   return ASAP_OK;
 }
 
-// K5b launch shared by both weight kinds; `mark` records the job's last timing event.
+// K5b launch shared by both weight kinds, on `st` with `ctas` CTAs; `mark` records the job's last timing event.
 template <class Mark>
 static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_t* B, int R,
-                    const asap_ffn_row_t* rows, cudaStream_t st, int sms, Mark& mark) {
+                    const asap_ffn_row_t* rows, cudaStream_t st, int ctas, Mark& mark) {
   FinalArgs fa{};
   fa.desc = desc;
   fa.topk = L.topk;
@@ -1139,9 +1140,9 @@ static int finalize(JobDesc* desc, const WsLayout& L, const PermArgs& pa, uint8_
     fa.reply_done[r] = (uint32_t*)rows[r].reply_done;
   }
   fa.desc_rw = desc;
-  finalize_reply_kernel<<<sms * 4, 256, 0, st>>>(fa);
+  finalize_reply_kernel<<<ctas, 256, 0, st>>>(fa);
   ASAP_CHECK_LAUNCH("finalize_reply_kernel");
-  mark(5);
+  mark(5, st);
   return ASAP_OK;
 }
 
@@ -1285,6 +1286,7 @@ int asap_ffn_ws_release(uint64_t handle) {
   for (int j = 0; j < kTimedJobs; ++j)
     for (int i = 0; i <= kTimedKernels; ++i)
       if (it->second->ev[j][i]) cudaEventDestroy(it->second->ev[j][i]);
+  if (it->second->split) cudaEventDestroy(it->second->split);
   delete it->second;
   g_ws.erase(it);
   return ASAP_OK;
@@ -1482,8 +1484,9 @@ int asap_ffn_job(uint64_t experts_handle, uint64_t ws_handle, uint64_t x, uint64
   return asap_ffn_job_rows(experts_handle, ws_handle, 1, &row, swiglu_limit, status, timeout_ns, stream);
 }
 
-int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, const asap_ffn_row_t* rows,
-                      float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream) {
+static int ffn_job_impl(uint64_t experts_handle, uint64_t ws_handle, int32_t R, const asap_ffn_row_t* rows,
+                        float swiglu_limit, uint64_t status, uint64_t timeout_ns, cudaStream_t st,
+                        cudaStream_t reply_st, int32_t gemm_ctas, int32_t reply_ctas) {
   ExpertsHandle* eh = get_experts(experts_handle);
   WsHandle* wh = get_ws(ws_handle);
   if (!eh || !wh) {
@@ -1511,10 +1514,11 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   }
   int rc = ensure_gemm_attrs();
   if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
+  if (reply_st && !wh->split) ASAP_CUDA(cudaEventCreateWithFlags(&wh->split, cudaEventDisableTiming));
   uint8_t* B = wh->base;
   JobDesc* desc = (JobDesc*)(B + L.desc);
   const int sms = sm_count();
+  const int gctas = gemm_ctas > 0 && gemm_ctas < sms ? gemm_ctas : sms;  // persistent GEMM grids
 
   PermArgs pa{};
   pa.desc = desc;
@@ -1531,10 +1535,17 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   pa.hist = (int32_t*)(B + L.hist);
   const int slot_ev = wh->jobs % kTimedJobs;
   if (wh->timing) ++wh->jobs;
-  auto mark = [&](int i) {
-    if (wh->timing) cudaEventRecord(wh->ev[slot_ev][i], st);
+  auto mark = [&](int i, cudaStream_t on) {
+    if (wh->timing) cudaEventRecord(wh->ev[slot_ev][i], on);
   };
-  mark(0);
+  // the reduce + reply: on `st` after GEMM2, or on `reply_st` (after an event) while `st` goes on to the next job
+  auto reply = [&]() -> int {
+    if (!reply_st) return finalize(desc, L, pa, B, R, rows, st, sms * 4, mark);
+    ASAP_CUDA(cudaEventRecord(wh->split, st));
+    ASAP_CUDA(cudaStreamWaitEvent(reply_st, wh->split, 0));
+    return finalize(desc, L, pa, B, R, rows, reply_st, reply_ctas > 0 ? reply_ctas : sms * 4, mark);
+  };
+  mark(0, st);
   if (!pa.desc || !pa.ids || !pa.w || !pa.ecnt || !pa.mstart || !pa.pair_pos || !pa.row_tok || !pa.row_w ||
       !pa.hist) {
     set_error("asap_ffn_job: internal error, a permutation buffer is unset");
@@ -1559,7 +1570,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   ASAP_CHECK_LAUNCH("route_scan_kernel");
   route_place_kernel<<<kPermChunks, 32, 0, st>>>(pa);
   ASAP_CHECK_LAUNCH("route_place_kernel");
-  mark(1);
+  mark(1, st);
 
   QuantArgs qa{};
   qa.desc = desc;
@@ -1573,7 +1584,7 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   if (eh->kind == kFp8Block) {
     quant_permute_fp8_kernel<<<sms * 4, 256, 0, st>>>(qa);
     ASAP_CHECK_LAUNCH("quant_permute_fp8_kernel");
-    mark(2);
+    mark(2, st);
     gemm8::Params g1;
     memset(&g1, 0, sizeof(g1));
     g1.tmap_a = wh->xq_map;
@@ -1594,9 +1605,9 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     g1.swiglu_limit = swiglu_limit;
     g1.status = status;
     g1.timeout_ns = timeout_ns;
-    gemm8::moe_gemm_fp8_kernel<0><<<sms, gemm8::Cfg<0>::THREADS, gemm8::SMEM_BYTES, st>>>(g1);
+    gemm8::moe_gemm_fp8_kernel<0><<<gctas, gemm8::Cfg<0>::THREADS, gemm8::SMEM_BYTES, st>>>(g1);
     ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<0>");
-    mark(3);
+    mark(3, st);
     gemm8::Params g2 = g1;
     g2.tmap_a = wh->hq_map;
     g2.tmap_b = eh->w2_map;
@@ -1608,14 +1619,14 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
     g2.tile_ctr = &desc->tiles[1];
     g2.N = L.H;
     g2.K = L.I;
-    gemm8::moe_gemm_fp8_kernel<1><<<sms, gemm8::Cfg<1>::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
+    gemm8::moe_gemm_fp8_kernel<1><<<gctas, gemm8::Cfg<1>::THREADS, gemm8::SMEM_BYTES, st>>>(g2);
     ASAP_CHECK_LAUNCH("moe_gemm_fp8_kernel<1>");
-    mark(4);
-    return finalize(desc, L, pa, B, R, rows, st, sms, mark);
+    mark(4, st);
+    return reply();
   }
   quant_permute_kernel<<<sms * 4, 256, 0, st>>>(qa);
   ASAP_CHECK_LAUNCH("quant_permute_kernel");
-  mark(2);
+  mark(2, st);
 
   gemm::Params g1;
   memset(&g1, 0, sizeof(g1));
@@ -1637,9 +1648,9 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g1.swiglu_limit = swiglu_limit;
   g1.status = status;
   g1.timeout_ns = timeout_ns;
-  gemm::moe_gemm_kernel<0><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
+  gemm::moe_gemm_kernel<0><<<gctas, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g1);
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<0>");
-  mark(3);
+  mark(3, st);
 
   gemm::Params g2 = g1;
   g2.tmap_a = wh->hq_map;
@@ -1653,11 +1664,28 @@ int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, co
   g2.tile_ctr = &desc->tiles[1];
   g2.N = L.H;
   g2.K = L.I;
-  gemm::moe_gemm_kernel<1><<<sms, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
+  gemm::moe_gemm_kernel<1><<<gctas, gemm::THREADS, gemm::SMEM_BYTES, st>>>(g2);
   ASAP_CHECK_LAUNCH("moe_gemm_kernel<1>");
-  mark(4);
+  mark(4, st);
 
-  return finalize(desc, L, pa, B, R, rows, st, sms, mark);
+  return reply();
+}
+
+int asap_ffn_job_rows(uint64_t experts_handle, uint64_t ws_handle, int32_t R, const asap_ffn_row_t* rows,
+                      float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream) {
+  return ffn_job_impl(experts_handle, ws_handle, R, rows, swiglu_limit, status, timeout_ns, (cudaStream_t)stream,
+                      nullptr, 0, 0);
+}
+
+int asap_ffn_job_rows_overlap(uint64_t experts_handle, uint64_t ws_handle, int32_t R, const asap_ffn_row_t* rows,
+                              float swiglu_limit, uint64_t status, uint64_t timeout_ns, void* stream,
+                              void* reply_stream, int32_t gemm_ctas, int32_t reply_ctas) {
+  if (!reply_stream || reply_stream == stream || gemm_ctas < 1 || reply_ctas < 1) {
+    set_error("asap_ffn_job_rows_overlap: needs a reply stream other than the job's and positive CTA counts");
+    return ASAP_EINVAL;
+  }
+  return ffn_job_impl(experts_handle, ws_handle, R, rows, swiglu_limit, status, timeout_ns, (cudaStream_t)stream,
+                      (cudaStream_t)reply_stream, gemm_ctas, reply_ctas);
 }
 
 int asap_ffn_enable_timing(uint64_t ws_handle, int32_t enable) {

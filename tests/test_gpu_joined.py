@@ -329,3 +329,58 @@ def test_first_message_then_the_rest(cuda_ok):
             ch.close()
         srv.close()
         experts.release()
+
+
+def test_overlapped_replies_alternate_workspaces(cuda_ok):
+    """FfnScheduler(overlap_replies=k): a job's reduce + reply runs on a side stream (k SMs left to it, the GEMMs
+    on the rest) while the next job computes, and consecutive jobs alternate between two workspaces.  Three A
+    replicas, two rounds of three round-robin jobs (the first two of each round overlapped): every combined output
+    matches the oracle and every done flag carries its message's seq."""
+    import os
+    import tempfile
+
+    run_dir = tempfile.mkdtemp(dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else None)
+    rng = np.random.default_rng(33)
+    T, H, I, k, E = 128, 256, 128, 4, 8
+    sizes = (T, T - 7, T - 20)
+    g = Geometry(3, 1, 1, T, H, k, 1)
+    experts = Mxfp4Experts.random(E, H, I, seed=9)
+    srv = FfnServer(0, g, device=0, run_dir=run_dir, listen=False).start()
+    chans = [AttnChannel(a, g, [("in-process", 0)], device=0, timeout_s=5.0, expert_bounds=[0, E],
+                         _connector=lambda f, hello: srv.handshake(hello)).connect() for a in range(3)]
+    sched = FfnScheduler(srv, {0: experts}, timeout_s=5.0, overlap_replies=8)
+    gate, up, w2 = experts_to_oracle(experts)
+    f_stream = torch.cuda.Stream()
+    stream = torch.cuda.current_stream()
+    sources = [(a, 0) for a in range(3)]
+    keep = []
+    try:
+        assert len(sched._wss) == 2
+        for rnd in range(2):
+            sent = []
+            for a in range(3):
+                x, ids, w = random_inputs(rng, sizes[a], H, k, 0, E)
+                dev = (bf16_tensor_from_np(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
+                keep.append(dev)
+                t = chans[a].send(0, 0, dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), sizes[a],
+                                  stream.cuda_stream)
+                sent.append((t, (x, ids, w)))
+            f_stream.wait_stream(stream)  # the F jobs run after every send (no kernel spins on another here)
+            for i in range(3):
+                sched.run_device_wait_any(sources, 0, f_stream.cuda_stream, overlap=i < 2)
+            torch.cuda.synchronize()
+            sched.check()
+            for a, (t, msg) in enumerate(sent):
+                out = torch.empty(sizes[a], H, dtype=torch.bfloat16, device="cuda")
+                chans[a].combine(t, out.data_ptr(), stream.cuda_stream)
+                torch.cuda.synchronize()
+                chans[a].check()
+                ref = moe.round_trip(*msg, [0, E], [(gate, up, w2)])
+                assert moe.rel_l2(np_from_bf16(out), ref) < TOL, (rnd, a)
+    finally:
+        torch.cuda.synchronize()
+        sched.close()
+        for ch in chans:
+            ch.close()
+        srv.close()
+        experts.release()
